@@ -1,0 +1,526 @@
+"""Benchmark of the W4A16 GEMV hot path on B200 (one JSON line on rank 0).
+
+Workload (the metric's own config): M = 1, N = K = 8192, RTN 4-bit group
+128, fp16 scale and zero, weights N(0, 0.02), activations N(0, 1), seeded synthetic data. One
+step = one call of the operator (int4gemv.ops.w4a16) on one batch.
+
+Measurement:
+  value       effective HBM bandwidth, algorithmic bytes (N K/2 + N K/32 + 2 M K + 2 M N, the
+              reference's int4_bytes) per call / device time per call, summed over ranks;
+              K back-to-back calls replayed from CUDA graphs, each call on a different weight
+              set from a rotation whose total size is > 2x the L2, so every call reads its
+              weights from HBM (no flush kernel in the timed region)
+  e2e         the same metric through the public API with host buffers: per step, copy x from
+              pinned host memory, call ops.w4a16, copy y back to pinned host memory and wait
+  roofline    achieved bytes/s of the GEMV kernel vs the measured HBM copy peak
+              (MEASURED_PEAKS.json), DRAM traffic per launch from the committed ncu summary
+  cuBLAS FP16 F.linear(x, W16) on the same box, same rotation rule: the speedup of the metric
+  cpu_baseline the reference's own CPU path (csrc/sequential.cpp built from its sources into
+              oracle/_ref; else the C oracle port), single-threaded, a bounded sample of rows
+
+--impl reference times the reference's CPU implementation (all host threads) on a bounded row
+sample of the same workload, in the same unit.
+Multi-GPU (torchrun): every rank runs the same workload on its own weights (independent weight
+matrices, e.g. different layers); no collective in the data path; value = sum over ranks of bytes
+/ the slowest rank's time ("scaling": "weak").
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "int4-gemv-cuda_b200"))
+sys.path.insert(0, str(REPO / "oracle"))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+M, N, K, GROUP = 1, 8192, 8192, 128
+METRIC = "µs/call and HBM GB/s (% of B200 peak) at M=1, 8192×8192 W4A16; × vs cuBLAS FP16"
+FALLBACK_HBM_GBS = 6650.0
+L2_BYTES = 126 * 1024 * 1024
+
+
+def int4_bytes(m, n, k, g):
+    """Bytes one W4A16 call must move (the reference's bench/timing.py int4_bytes)."""
+    return n * k // 2 + 2 * n * (k // g) * 2 + m * k * 2 + m * n * 2
+
+
+def fp16_bytes(m, n, k):
+    return n * k * 2 + m * k * 2 + m * n * 2
+
+
+def measured_peak():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic():
+    p = REPO / "profiles" / "ncu_traffic.json"
+    if not p.exists():
+        return None
+    try:
+        return json.loads(p.read_text())
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------- clocks during the timed region
+class ClockSampler:
+    """Samples SM clock, max clock and throttle reasons with NVML in a thread."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, index: int):
+        self.samples = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._ok = False
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._ok = True
+        except Exception:
+            self._ok = False
+
+    def _read(self):
+        nv = self._nv
+        sm = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+        try:
+            reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+        except Exception:
+            reasons = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
+        return time.perf_counter(), sm, reasons
+
+    def _loop(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self._read())
+            except Exception:
+                return
+            time.sleep(0.002)
+
+    def start(self):
+        if self._ok:
+            self._t = threading.Thread(target=self._loop, daemon=True)
+            self._t.start()
+        return self
+
+    def stop(self):
+        self._stop.set()
+        if self._ok:
+            self._t.join()
+        return self
+
+    def summary(self, t0: float, t1: float) -> dict:
+        if not self._ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0,
+                    "note": "NVML unavailable"}
+        inside = [s for s in self.samples if t0 <= s[0] <= t1]
+        if not inside and self.samples:  # region shorter than the sampling period: nearest sample
+            inside = [min(self.samples, key=lambda s: abs(s[0] - 0.5 * (t0 + t1)))]
+        reasons = set()
+        for _, _, r in inside:
+            for bit, name in self.REASONS.items():
+                if r & bit and name != "gpu_idle":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(s[1] for s in inside) if inside else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(reasons), "samples": len(inside)}
+
+
+# ---------------------------------------------------------------- distributed plumbing
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- data
+def make_sets(n_sets: int, seed: int):
+    from int4gemv import quant
+
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    sets = []
+    for _ in range(n_sets):
+        w = torch.randn(N, K, generator=gen, device="cuda") * 0.02
+        sets.append(quant.quantize(w, GROUP))
+        del w
+    x = torch.randn(M, K, generator=gen, device="cuda").half()
+    return sets, x
+
+
+def reference_module():
+    so = sorted((REPO / "oracle" / "_ref").glob("int4gemv_ref*.so"))
+    if not so:
+        return None
+    spec = importlib.util.spec_from_file_location("int4gemv_ref", so[0])
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+# ---------------------------------------------------------------- timing helpers
+def graph_of(calls):
+    """Capture a list of zero-argument callables into one CUDA graph."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for c in calls:  # warm: lazy init, shared-memory attributes
+            c()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for c in calls:
+            c()
+    return g
+
+
+def time_graph_calls(calls, total_calls: int, warmup_calls: int):
+    """Replay `calls` (one graph) until total_calls calls ran; returns seconds per call."""
+    per = len(calls)
+    g = graph_of(calls)
+    reps_w = max(1, math.ceil(warmup_calls / per))
+    for _ in range(reps_w):
+        g.replay()
+    torch.cuda.synchronize()
+    reps = max(1, math.ceil(total_calls / per))
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(reps):
+        g.replay()
+    end.record()
+    end.synchronize()
+    return start.elapsed_time(end) / 1e3 / (reps * per)
+
+
+def cpu_sample(ref, x_cpu, q_cpu, s_cpu, z_cpu, budget_s: float, threads: int):
+    """Time the reference's CPU path on growing row samples until budget_s is spent."""
+    if ref is not None:
+        def run(rows):
+            if threads > 1:
+                return ref.sequential_threads(x_cpu, q_cpu[:rows], s_cpu[:rows], z_cpu[:rows],
+                                              GROUP, threads)
+            return ref.sequential(x_cpu, q_cpu[:rows].contiguous(), s_cpu[:rows].contiguous(),
+                                  z_cpu[:rows].contiguous(), GROUP)
+        kind = "reference"
+    else:
+        import oracle
+
+        xn, qn, sn, zn = (t.numpy() for t in (x_cpu, q_cpu, s_cpu, z_cpu))
+
+        def run(rows):
+            return oracle.sequential(xn, qn[:rows], sn[:rows], zn[:rows], GROUP)
+        kind = "port"
+        threads = 1
+    rows = 256
+    run(rows)  # warm
+    t0 = time.perf_counter()
+    done_rows, calls = 0, 0
+    while time.perf_counter() - t0 < budget_s:
+        run(rows)
+        done_rows += rows
+        calls += 1
+        elapsed = time.perf_counter() - t0
+        if elapsed < budget_s / 8 and rows < N:
+            rows = min(N, rows * 2)
+    elapsed = time.perf_counter() - t0
+    bytes_done = done_rows / N * int4_bytes(M, N, K, GROUP)
+    return {"value": bytes_done / elapsed / 1e9, "unit": "GB/s", "cores": threads, "kind": kind,
+            "sample": f"{calls} calls over {done_rows} rows of the {N}x{K} M=1 workload "
+                      f"({done_rows / N:.2f} full GEMVs) in {elapsed:.1f} s",
+            "us_per_call": elapsed / (done_rows / N) * 1e6}
+
+
+# ---------------------------------------------------------------- arms
+def run_reference_arm(args, world, rank):
+    if rank != 0:
+        return
+    ref = reference_module()
+    threads = os.cpu_count() or 1
+    gen = torch.Generator().manual_seed(0)
+    from int4gemv import quant
+
+    w = torch.randn(N, K, generator=gen) * 0.02
+    q, s, z = quant.quantize(w, GROUP)
+    x = torch.randn(M, K, generator=gen).half()
+    # Each step is a bounded row sample, sized from a calibration call so that warmup + steps
+    # take about a minute and a half whatever K is.
+    kind = "reference" if ref is not None else "port"
+
+    def run(rows):
+        if ref is not None:
+            return ref.sequential_threads(x, q[:rows], s[:rows], z[:rows], GROUP, threads)
+        import oracle
+
+        return oracle.sequential(x.numpy(), q[:rows].numpy(), s[:rows].numpy(), z[:rows].numpy())
+
+    cal_rows = min(N, 1024)
+    run(cal_rows)
+    t_cal = time.perf_counter()
+    run(cal_rows)
+    per_row = (time.perf_counter() - t_cal) / cal_rows
+    budget = 90.0
+    rows = int(budget / max(1, args.steps + args.warmup) / per_row)
+    rows = max(min(N, 8 * threads), min(N, rows))
+
+    def step():
+        return run(rows)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / max(1, args.steps)
+    full_us = dt * N / rows * 1e6
+    value = int4_bytes(M, N, K, GROUP) / (full_us * 1e-6) / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt * 1e3, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp32 accumulate, fp16 in/out", "data": "synthetic",
+        "us_per_call": round(full_us, 1),
+        "config": {"workload": f"W4A16 GEMV M={M} N={N} K={K} group={GROUP}",
+                   "m": M, "n": N, "k": K, "group_size": GROUP,
+                   "sample_rows_per_step": rows},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads,
+                         "kind": kind,
+                         "sample": f"{rows} of {N} rows per step, {args.steps} steps"},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, world, rank, local):
+    from int4gemv import ops
+    import torch.nn.functional as F
+
+    set_bytes = N * K // 2 + 2 * N * (K // GROUP) * 2
+    n_sets = max(2, math.ceil(2 * L2_BYTES / set_bytes) + 1)
+    sets, x = make_sets(n_sets, seed=1234 + rank)
+
+    # Parity gate before timing (as the reference's benchmarks do): set 0 against the oracle.
+    import oracle
+
+    q0, s0, z0 = (t.cpu().numpy() for t in sets[0])
+    ref = oracle.reference(x.cpu().numpy(), q0, s0, z0, GROUP)
+    y0 = ops.w4a16(x, *sets[0], GROUP)
+    ok, msg = oracle.check_close(y0.float().cpu().numpy(), ref)
+    if not ok:
+        raise SystemExit(f"bench: parity gate failed: {msg}")
+    kernel = ops.w4a16_kernel(x, *sets[0], GROUP)
+
+    def call(i):
+        return lambda: ops.w4a16(x, *sets[i], GROUP)
+
+    calls = [call(i) for i in range(n_sets)]
+    per_graph = n_sets * max(1, 64 // n_sets)
+    calls = [calls[i % n_sets] for i in range(per_graph)]
+    g = graph_of(calls)
+    reps_w = max(1, math.ceil(args.warmup / per_graph))
+    for _ in range(reps_w):
+        g.replay()
+    torch.cuda.synchronize()
+
+    # ---- timed region: exactly `steps` calls (full graphs, then the remainder launched directly)
+    full, rem = divmod(args.steps, per_graph)
+    sampler = ClockSampler(torch.cuda.current_device()).start()
+    barrier(world)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(full):
+        g.replay()
+    for i in range(rem):
+        calls[i]()
+    end.record()
+    end.synchronize()
+    t1 = time.perf_counter()
+    barrier(world)
+    sampler.stop()
+    local_s = start.elapsed_time(end) / 1e3
+    total_s = max_over_ranks(local_s, world)
+    per_call_s = total_s / args.steps
+    bytes_call = int4_bytes(M, N, K, GROUP)
+    value = world * bytes_call * args.steps / total_s / 1e9
+    clocks = sampler.summary(t0, t1)
+    del g
+
+    # ---- kernel-only duration per launch (events around each launch, rotating weights)
+    kstart = [torch.cuda.Event(enable_timing=True) for _ in range(200)]
+    kend = [torch.cuda.Event(enable_timing=True) for _ in range(200)]
+    for i in range(200):
+        kstart[i].record()
+        calls[i % n_sets]()
+        kend[i].record()
+    torch.cuda.synchronize()
+    launch_s = statistics.median(a.elapsed_time(b) for a, b in zip(kstart, kend)) / 1e3
+
+    extra = {}
+    if rank == 0:
+        # ---- cuBLAS FP16 on the same box (F.linear, rotation > 2x L2)
+        w16 = [torch.randn(N, K, device="cuda", dtype=torch.float16) * 0.02
+               for _ in range(max(2, math.ceil(2 * L2_BYTES / (N * K * 2)) + 1))]
+        cub = [(lambda w=w: F.linear(x, w)) for w in w16]
+        cublas_s = time_graph_calls(cub * max(1, 16 // len(cub)), 2000, 50)
+        del w16, cub
+        extra["cublas_fp16_us"] = round(cublas_s * 1e6, 3)
+        extra["speedup_vs_cublas_fp16"] = round(cublas_s / per_call_s, 3)
+        # ---- the reference's own vectorized kernel, built for sm_100a, same rotation
+        refm = reference_module()
+        if refm is not None:
+            rv = [(lambda i=i: refm.vectorized(x, *sets[i], GROUP)) for i in range(n_sets)]
+            ref_s = time_graph_calls(rv * max(1, 64 // n_sets), 5000, 100)
+            extra["reference_vectorized_us"] = round(ref_s * 1e6, 3)
+            extra["speedup_vs_reference_vectorized"] = round(ref_s / per_call_s, 3)
+        # ---- our vectorized (the reference-shaped API kernel)
+        vv = [(lambda i=i: ops.vectorized(x, *sets[i], GROUP)) for i in range(n_sets)]
+        extra["vectorized_us"] = round(time_graph_calls(vv * max(1, 64 // n_sets), 5000, 100) * 1e6, 3)
+
+    # ---- end to end through the public API with host buffers
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty(M, N, dtype=torch.float16).pin_memory()
+    x_dev = torch.empty_like(x)
+    stream = torch.cuda.current_stream()
+    e2e_steps = min(max(args.steps, 50), 2000)
+    for i in range(20):
+        x_dev.copy_(x_host, non_blocking=True)
+        y_host.copy_(ops.w4a16(x_dev, *sets[i % n_sets], GROUP), non_blocking=True)
+        stream.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(e2e_steps):
+        x_dev.copy_(x_host, non_blocking=True)
+        y_host.copy_(ops.w4a16(x_dev, *sets[i % n_sets], GROUP), non_blocking=True)
+        stream.synchronize()  # the host reads this step's result
+    e1.record()
+    e1.synchronize()
+    e2e_s = max_over_ranks(e0.elapsed_time(e1) / 1e3, world) / e2e_steps
+    e2e = {"value": round(world * bytes_call / e2e_s / 1e9, 3), "unit": "GB/s",
+           "us_per_call": round(e2e_s * 1e6, 3),
+           "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2}
+
+    peak, peak_kind = measured_peak()
+    achieved = bytes_call / launch_s / 1e9
+    traffic = ncu_traffic()
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                "traffic": traffic.get("bytes_per_launch") if traffic else None,
+                "algorithmic_bytes": bytes_call,
+                "kernel": kernel, "launch_us": round(launch_s * 1e6, 3)}
+
+    if rank != 0:
+        return
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        x_cpu = x.cpu()
+        q_cpu, s_cpu, z_cpu = (t.cpu() for t in sets[0])
+        cpu = cpu_sample(reference_module(), x_cpu, q_cpu, s_cpu, z_cpu, args.cpu_seconds, 1)
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_call_s * 1e3, 6),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp16 in/out, int4 weights, fp32 accumulate", "data": "synthetic",
+        "us_per_call": round(per_call_s * 1e6, 3),
+        "pct_of_peak": round(100 * bytes_call / per_call_s / 1e9 / peak, 2),
+        "config": {"workload": f"W4A16 GEMV M={M} N={N} K={K} group={GROUP} (BASELINE config 1)",
+                   "m": M, "n": N, "k": K, "group_size": GROUP, "kernel": kernel,
+                   "l2": f"no flush; {n_sets} rotating weight sets of {set_bytes / 2**20:.1f} MiB "
+                         f"(> 2x the 126 MB L2) so every call reads its weights from HBM",
+                   "timing": "CUDA graphs of back-to-back calls, CUDA events",
+                   "parallelism": f"independent weights per GPU x{world}"},
+        "roofline": roofline, "clocks": clocks, "e2e": e2e, "gpu_launches": args.steps,
+        **extra, "parity": msg,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    world, rank, local = (int(os.environ.get("WORLD_SIZE", "1")),
+                          int(os.environ.get("RANK", "0")),
+                          int(os.environ.get("LOCAL_RANK", "0")))
+    if args.impl == "reference":
+        if rank == 0:
+            run_reference_arm(args, world, rank)
+        return
+    if not torch.cuda.is_available():
+        raise SystemExit("bench: no CUDA device")
+    world, rank, local = dist_setup()
+    try:
+        run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,122 @@
+/*
+ * int4gemv_b200: C ABI of the B200-native (sm_100a) W4A16 GEMV library.
+ *
+ * The operator is y = x @ dequant(W)^T with w = (q - z) * s, every group_size weights along K
+ * sharing one fp16 scale s and one fp16 zero z. Layouts follow the reference operator contract
+ * (Yu-TingLee/int4-GEMV-cuda, csrc/w4a16.h:10-16), all contiguous row-major:
+ *   x        [M, K]          fp16
+ *   qweight  [N, K / 8]      int32, eight 4-bit q per word, weight k in bits 4*(k%8).. of word k/8
+ *   scales   [N, K / group]  fp16
+ *   zeros    [N, K / group]  fp16
+ *   y        [M, N]          fp16 (written)
+ * Unless stated otherwise pointers are DEVICE pointers on the current CUDA device, `stream` is a
+ * cudaStream_t (NULL = the legacy default stream), and calls are asynchronous: they enqueue work on
+ * `stream` and return. No entry point synchronises the device.
+ *
+ * Every entry point returns INT4GEMV_OK (0) or an error code; int4gemv_last_error() then gives a
+ * message for the calling thread. Argument errors use the reference's check messages
+ * (csrc/checks.cpp:9-44, csrc/common.cuh:84-112), prefixed by the operator name.
+ * M, N or K equal to 0 is valid: nothing is launched (y is empty).
+ */
+#ifndef INT4GEMV_B200_H_
+#define INT4GEMV_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define INT4GEMV_OK 0
+#define INT4GEMV_ERR_INVALID 1     /* an argument fails a check; nothing was launched */
+#define INT4GEMV_ERR_CUDA 2        /* a CUDA runtime call failed */
+#define INT4GEMV_ERR_WORKSPACE 3   /* workspace missing or smaller than *_workspace_size */
+
+/* Message for the last failing call on this thread ("" if none). Valid until the next call. */
+const char* int4gemv_last_error(void);
+
+/* Library version as MAJOR * 10000 + MINOR * 100 + PATCH. */
+int int4gemv_version(void);
+
+/* ---- The reference's operators (csrc/w4a16.h), re-implemented for sm_100a -------------------- */
+
+/* Replaces int4gemv::naive (csrc/w4a16.h:27-28): one thread per output row. */
+int int4gemv_naive(void* y, const void* x, const void* qweight, const void* scales,
+                   const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
+                   void* stream);
+
+/* Replaces int4gemv::coalesced (csrc/w4a16.h:32-33): one warp per output row. */
+int int4gemv_coalesced(void* y, const void* x, const void* qweight, const void* scales,
+                       const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
+                       void* stream);
+
+/* Replaces int4gemv::vectorized (csrc/w4a16.h:38-40): rows_per_warp (1, 2 or 4) rows per warp,
+ * threads_per_block a multiple of 32 in [32, 1024], 16-byte loads. Needs group_size % 32 == 0 and
+ * 16-byte aligned x and qweight (csrc/common.cuh:94-101). */
+int int4gemv_vectorized(void* y, const void* x, const void* qweight, const void* scales,
+                        const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
+                        int64_t threads_per_block, int64_t rows_per_warp, void* stream);
+
+/* Replaces int4gemv::load_only (csrc/w4a16.h:45-47): the vectorized loads without the GEMV math,
+ * M = 1 only. out is uint32 [N]; out[r] is the XOR of every 32-bit word of qweight row r, of the
+ * zero-extended 16-bit patterns of scales/zeros row r, and of the words of x read with each chunk. */
+int int4gemv_load_only(void* out, const void* x, const void* qweight, const void* scales,
+                       const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
+                       int64_t threads_per_block, int64_t rows_per_warp, void* stream);
+
+/* Replaces naive_info / coalesced_info / vectorized_info (csrc/w4a16.h:29,34,41;
+ * csrc/common.cuh:115-128). kernel is "naive", "coalesced", "vectorized" or "w4a16".
+ * threads_per_block / rows_per_warp are used by "vectorized" only. Writes six values to info:
+ * registers, local_bytes, threads_per_block, max_threads_per_block, blocks_per_sm, warps_per_sm. */
+int int4gemv_kernel_info(const char* kernel, int64_t m, int64_t threads_per_block,
+                         int64_t rows_per_warp, int64_t* info);
+
+/* Replaces int4gemv::sequential (csrc/w4a16.h:23-24): the CPU path. HOST pointers. Same order of
+ * fp32 operations as the reference, so the result is bit-identical; rows are spread over
+ * `threads` host threads (0 = one per hardware thread), which does not change the result. */
+int int4gemv_sequential(void* y, const void* x, const void* qweight, const void* scales,
+                        const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
+                        int64_t threads);
+
+/* ---- The B200 fast path (new; no counterpart in the reference) ------------------------------- */
+
+/* Bytes of device workspace int4gemv_w4a16 needs for this shape (0 if none). */
+int64_t int4gemv_w4a16_workspace_size(int64_t m, int64_t n, int64_t k, int64_t group_size);
+
+/* y = x @ dequant(W)^T through the fastest kernel for the shape: a persistent, TMA-bulk-fed,
+ * tensor-core dequant GEMV when the shape allows it, else the SIMT kernels. Same inputs and result
+ * contract as the operators above (csrc/w4a16.h:10-16), parity with int4gemv/reference.py within
+ * rtol = 1e-2, atol = 1e-2. workspace may be NULL when int4gemv_w4a16_workspace_size returns 0. */
+int int4gemv_w4a16(void* y, const void* x, const void* qweight, const void* scales,
+                   const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
+                   void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Name of the kernel int4gemv_w4a16 picks for this shape and these pointers ("mma_pipeline",
+ * "vectorized", "naive"); for tests and the benchmark. Static storage. */
+const char* int4gemv_w4a16_kernel_name(const void* x, const void* qweight, const void* scales,
+                                       const void* zeros, int64_t m, int64_t n, int64_t k,
+                                       int64_t group_size);
+
+/* ---- Packed-format helpers on the device (int4gemv/quant.py:40-53), bit-exact ---------------- */
+
+/* q [N, K] int32 = the 4-bit values of qweight [N, K/8]   (quant.py:40-44). */
+int int4gemv_unpack(void* q, const void* qweight, int64_t n, int64_t k, void* stream);
+
+/* w [N, K] fp32 = (q - z) * s with one fp32 subtraction and one fp32 multiplication per weight
+ * (quant.py:47-53), bit-identical to the reference. */
+int int4gemv_dequantize(void* w, const void* qweight, const void* scales, const void* zeros,
+                        int64_t n, int64_t k, int64_t group_size, void* stream);
+
+/* ---- Device-side status --------------------------------------------------------------------- */
+
+/* Reads and clears the current device's kernel status word: 0 if every pipelined kernel since the
+ * last call finished normally, else a nonzero code recorded by a kernel whose bounded wait on a
+ * shared-memory barrier timed out (the kernel then skipped its work and returned). Synchronises
+ * the current device. */
+int int4gemv_device_status(int* status);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* INT4GEMV_B200_H_ */

@@ -1,0 +1,195 @@
+// The torch binding: the Python module int4gemv_ops with the reference's eight functions, names,
+// argument names and defaults (csrc/bindings.cpp:20-41 of Yu-TingLee/int4-GEMV-cuda), plus the
+// B200 fast path and the packed-format helpers. Each function checks its tensors (checks.cpp),
+// allocates the output through torch's caching allocator on the input's device, and calls the
+// torch-free C ABI (include/int4gemv_b200.h) on torch's current stream. Nothing synchronises.
+#include <ATen/Parallel.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <torch/extension.h>
+
+#include "int4gemv_b200.h"
+#include "int4gemv_torch.h"
+
+namespace int4gemv {
+namespace {
+
+// Defaults from the reference's block sweep (csrc/bindings.cpp:8-12).
+constexpr int64_t kDefaultThreadsPerBlock = 128;
+constexpr int64_t kDefaultRowsPerWarp = 2;
+
+void check_status(int status) { TORCH_CHECK(status == INT4GEMV_OK, int4gemv_last_error()); }
+
+void* stream_of(const at::Tensor& t) {
+  return static_cast<void*>(c10::cuda::getCurrentCUDAStream(t.device().index()).stream());
+}
+
+using CudaGemv = int (*)(void*, const void*, const void*, const void*, const void*, int64_t,
+                         int64_t, int64_t, int64_t, void*);
+
+at::Tensor run_gemv(const char* name, CudaGemv fn, const at::Tensor& x, const at::Tensor& qweight,
+                    const at::Tensor& scales, const at::Tensor& zeros, int64_t group_size) {
+  check_inputs(name, x, qweight, scales, zeros, group_size, c10::DeviceType::CUDA);
+  const c10::cuda::CUDAGuard guard(x.device());
+  at::Tensor y = x.new_empty({x.size(0), qweight.size(0)});
+  check_status(fn(y.data_ptr(), x.data_ptr(), qweight.data_ptr(), scales.data_ptr(),
+                  zeros.data_ptr(), x.size(0), qweight.size(0), x.size(1), group_size,
+                  stream_of(x)));
+  return y;
+}
+
+KernelInfo info_of(const char* kernel, int64_t m, int64_t threads, int64_t rows_per_warp) {
+  int64_t v[6] = {};
+  check_status(int4gemv_kernel_info(kernel, m, threads, rows_per_warp, v));
+  return {{"registers", v[0]},       {"local_bytes", v[1]},
+          {"threads_per_block", v[2]}, {"max_threads_per_block", v[3]},
+          {"blocks_per_sm", v[4]},   {"warps_per_sm", v[5]}};
+}
+
+}  // namespace
+
+at::Tensor sequential(const at::Tensor& x, const at::Tensor& qweight, const at::Tensor& scales,
+                      const at::Tensor& zeros, int64_t group_size) {
+  check_inputs("sequential", x, qweight, scales, zeros, group_size, c10::DeviceType::CPU);
+  at::Tensor y = x.new_empty({x.size(0), qweight.size(0)});
+  check_status(int4gemv_sequential(y.data_ptr(), x.data_ptr(), qweight.data_ptr(),
+                                   scales.data_ptr(), zeros.data_ptr(), x.size(0),
+                                   qweight.size(0), x.size(1), group_size,
+                                   at::get_num_threads()));
+  return y;
+}
+
+at::Tensor naive(const at::Tensor& x, const at::Tensor& qweight, const at::Tensor& scales,
+                 const at::Tensor& zeros, int64_t group_size) {
+  return run_gemv("naive", &int4gemv_naive, x, qweight, scales, zeros, group_size);
+}
+
+at::Tensor coalesced(const at::Tensor& x, const at::Tensor& qweight, const at::Tensor& scales,
+                     const at::Tensor& zeros, int64_t group_size) {
+  return run_gemv("coalesced", &int4gemv_coalesced, x, qweight, scales, zeros, group_size);
+}
+
+at::Tensor vectorized(const at::Tensor& x, const at::Tensor& qweight, const at::Tensor& scales,
+                      const at::Tensor& zeros, int64_t group_size, int64_t threads_per_block,
+                      int64_t rows_per_warp) {
+  check_inputs("vectorized", x, qweight, scales, zeros, group_size, c10::DeviceType::CUDA);
+  const c10::cuda::CUDAGuard guard(x.device());
+  at::Tensor y = x.new_empty({x.size(0), qweight.size(0)});
+  check_status(int4gemv_vectorized(y.data_ptr(), x.data_ptr(), qweight.data_ptr(),
+                                   scales.data_ptr(), zeros.data_ptr(), x.size(0),
+                                   qweight.size(0), x.size(1), group_size, threads_per_block,
+                                   rows_per_warp, stream_of(x)));
+  return y;
+}
+
+at::Tensor load_only(const at::Tensor& x, const at::Tensor& qweight, const at::Tensor& scales,
+                     const at::Tensor& zeros, int64_t group_size, int64_t threads_per_block,
+                     int64_t rows_per_warp) {
+  check_inputs("load_only", x, qweight, scales, zeros, group_size, c10::DeviceType::CUDA);
+  const c10::cuda::CUDAGuard guard(x.device());
+  at::Tensor out = qweight.new_empty({qweight.size(0)});
+  check_status(int4gemv_load_only(out.data_ptr(), x.data_ptr(), qweight.data_ptr(),
+                                  scales.data_ptr(), zeros.data_ptr(), x.size(0),
+                                  qweight.size(0), x.size(1), group_size, threads_per_block,
+                                  rows_per_warp, stream_of(x)));
+  return out;
+}
+
+KernelInfo naive_info(int64_t m) { return info_of("naive", m, 0, 1); }
+KernelInfo coalesced_info(int64_t m) { return info_of("coalesced", m, 0, 1); }
+KernelInfo vectorized_info(int64_t m, int64_t threads_per_block, int64_t rows_per_warp) {
+  return info_of("vectorized", m, threads_per_block, rows_per_warp);
+}
+KernelInfo w4a16_info(int64_t m) { return info_of("w4a16", m, 0, 1); }
+
+at::Tensor w4a16(const at::Tensor& x, const at::Tensor& qweight, const at::Tensor& scales,
+                 const at::Tensor& zeros, int64_t group_size) {
+  check_inputs("w4a16", x, qweight, scales, zeros, group_size, c10::DeviceType::CUDA);
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t m = x.size(0), n = qweight.size(0), k = x.size(1);
+  at::Tensor y = x.new_empty({m, n});
+  const int64_t ws_bytes = int4gemv_w4a16_workspace_size(m, n, k, group_size);
+  at::Tensor ws;
+  if (ws_bytes > 0) ws = at::empty({ws_bytes}, x.options().dtype(at::kByte));
+  check_status(int4gemv_w4a16(y.data_ptr(), x.data_ptr(), qweight.data_ptr(), scales.data_ptr(),
+                              zeros.data_ptr(), m, n, k, group_size,
+                              ws_bytes > 0 ? ws.data_ptr() : nullptr, ws_bytes, stream_of(x)));
+  return y;
+}
+
+std::string w4a16_kernel(const at::Tensor& x, const at::Tensor& qweight, const at::Tensor& scales,
+                         const at::Tensor& zeros, int64_t group_size) {
+  check_inputs("w4a16", x, qweight, scales, zeros, group_size, c10::DeviceType::CUDA);
+  return int4gemv_w4a16_kernel_name(x.data_ptr(), qweight.data_ptr(), scales.data_ptr(),
+                                    zeros.data_ptr(), x.size(0), qweight.size(0), x.size(1),
+                                    group_size);
+}
+
+at::Tensor unpack(const at::Tensor& qweight) {
+  TORCH_CHECK(qweight.scalar_type() == at::kInt && qweight.dim() == 2 && qweight.is_contiguous() &&
+                  qweight.is_cuda(),
+              "unpack: expected a contiguous 2-D int32 CUDA qweight");
+  const c10::cuda::CUDAGuard guard(qweight.device());
+  at::Tensor q = qweight.new_empty({qweight.size(0), qweight.size(1) * 8});
+  check_status(int4gemv_unpack(q.data_ptr(), qweight.data_ptr(), qweight.size(0),
+                               qweight.size(1) * 8, stream_of(qweight)));
+  return q;
+}
+
+at::Tensor dequantize(const at::Tensor& qweight, const at::Tensor& scales, const at::Tensor& zeros,
+                      int64_t group_size) {
+  // Same checks as the GEMV, with an empty x of the right K standing in for the activations.
+  const int64_t k = qweight.dim() == 2 ? qweight.size(1) * 8 : 0;
+  const at::Tensor x = at::empty({0, k}, scales.options().dtype(at::kHalf));
+  check_inputs("dequantize", x, qweight, scales, zeros, group_size, c10::DeviceType::CUDA);
+  const c10::cuda::CUDAGuard guard(qweight.device());
+  at::Tensor w = at::empty({qweight.size(0), k}, scales.options().dtype(at::kFloat));
+  check_status(int4gemv_dequantize(w.data_ptr(), qweight.data_ptr(), scales.data_ptr(),
+                                   zeros.data_ptr(), qweight.size(0), k, group_size,
+                                   stream_of(qweight)));
+  return w;
+}
+
+}  // namespace int4gemv
+
+PYBIND11_MODULE(int4gemv_ops, m) {
+  using int4gemv::kDefaultRowsPerWarp;
+  using int4gemv::kDefaultThreadsPerBlock;
+  m.def("sequential", &int4gemv::sequential, py::arg("x"), py::arg("qweight"), py::arg("scales"),
+        py::arg("zeros"), py::arg("group_size"));
+  m.def("naive", &int4gemv::naive, py::arg("x"), py::arg("qweight"), py::arg("scales"),
+        py::arg("zeros"), py::arg("group_size"));
+  m.def("coalesced", &int4gemv::coalesced, py::arg("x"), py::arg("qweight"), py::arg("scales"),
+        py::arg("zeros"), py::arg("group_size"));
+  m.def("vectorized", &int4gemv::vectorized, py::arg("x"), py::arg("qweight"), py::arg("scales"),
+        py::arg("zeros"), py::arg("group_size"),
+        py::arg("threads_per_block") = kDefaultThreadsPerBlock,
+        py::arg("rows_per_warp") = kDefaultRowsPerWarp);
+  m.def("load_only", &int4gemv::load_only, py::arg("x"), py::arg("qweight"), py::arg("scales"),
+        py::arg("zeros"), py::arg("group_size"),
+        py::arg("threads_per_block") = kDefaultThreadsPerBlock,
+        py::arg("rows_per_warp") = kDefaultRowsPerWarp);
+  m.def("naive_info", &int4gemv::naive_info, py::arg("m"));
+  m.def("coalesced_info", &int4gemv::coalesced_info, py::arg("m"));
+  m.def("vectorized_info", &int4gemv::vectorized_info, py::arg("m"),
+        py::arg("threads_per_block") = kDefaultThreadsPerBlock,
+        py::arg("rows_per_warp") = kDefaultRowsPerWarp);
+
+  m.def("w4a16", &int4gemv::w4a16, py::arg("x"), py::arg("qweight"), py::arg("scales"),
+        py::arg("zeros"), py::arg("group_size"));
+  m.def("w4a16_info", &int4gemv::w4a16_info, py::arg("m"));
+  m.def("w4a16_kernel", &int4gemv::w4a16_kernel, py::arg("x"), py::arg("qweight"),
+        py::arg("scales"), py::arg("zeros"), py::arg("group_size"));
+  m.def("unpack", &int4gemv::unpack, py::arg("qweight"));
+  m.def("dequantize", &int4gemv::dequantize, py::arg("qweight"), py::arg("scales"),
+        py::arg("zeros"), py::arg("group_size"));
+  m.def(
+      "check_inputs",
+      [](const char* name, const at::Tensor& x, const at::Tensor& qweight,
+         const at::Tensor& scales, const at::Tensor& zeros, int64_t group_size, bool cuda) {
+        int4gemv::check_inputs(name, x, qweight, scales, zeros, group_size,
+                               cuda ? c10::DeviceType::CUDA : c10::DeviceType::CPU);
+      },
+      py::arg("name"), py::arg("x"), py::arg("qweight"), py::arg("scales"), py::arg("zeros"),
+      py::arg("group_size"), py::arg("cuda"));
+}

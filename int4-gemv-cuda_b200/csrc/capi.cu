@@ -1,0 +1,365 @@
+// The C ABI (include/int4gemv_b200.h): argument checks with the reference's messages, dispatch to
+// the launchers, and error reporting through int4gemv_last_error(). No torch, no allocation.
+#include <climits>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "int4gemv_b200.h"
+#include "kernels.h"
+
+namespace i4 {
+void sequential_cpu(uint16_t* y, const uint16_t* x, const uint32_t* q, const uint16_t* s,
+                    const uint16_t* z, int64_t m, int64_t n, int64_t k, int64_t group,
+                    int64_t threads);
+}  // namespace i4
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  std::vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int ok() {
+  g_last_error.clear();
+  return INT4GEMV_OK;
+}
+
+int cuda_fail(const char* name, cudaError_t err) {
+  return fail(INT4GEMV_ERR_CUDA, "%s: CUDA error %d: %s", name, static_cast<int>(err),
+              cudaGetErrorString(err));
+}
+
+// The size and group checks of csrc/checks.cpp:9-44 (reference), on raw sizes. The dtype, rank,
+// shape-consistency, contiguity and device checks are made by the torch binding, which sees
+// tensors; here the caller's sizes define the shapes.
+int check_sizes(const char* name, int64_t m, int64_t n, int64_t k, int64_t group) {
+  if (m < 0 || n < 0 || k < 0) {
+    return fail(INT4GEMV_ERR_INVALID, "%s: M = %lld, N = %lld, K = %lld must not be negative", name,
+                static_cast<long long>(m), static_cast<long long>(n), static_cast<long long>(k));
+  }
+  if (m > INT_MAX || n > INT_MAX || k > INT_MAX) {
+    return fail(INT4GEMV_ERR_INVALID, "%s: M = %lld, N = %lld, K = %lld must each fit in int", name,
+                static_cast<long long>(m), static_cast<long long>(n), static_cast<long long>(k));
+  }
+  if (!(group > 0 && group % 8 == 0 && k % group == 0)) {
+    return fail(INT4GEMV_ERR_INVALID,
+                "%s: group_size %lld must be a positive multiple of 8 dividing K = %lld", name,
+                static_cast<long long>(group), static_cast<long long>(k));
+  }
+  return INT4GEMV_OK;
+}
+
+int check_pointers(const char* name, int64_t m, int64_t n, int64_t k, const void* y,
+                   const void* x, const void* q, const void* s, const void* z) {
+  const bool need_y = m > 0 && n > 0;
+  const bool need_in = need_y && k > 0;
+  if ((need_y && !y) || (need_in && (!x || !q || !s || !z))) {
+    return fail(INT4GEMV_ERR_INVALID, "%s: null pointer for a non-empty tensor", name);
+  }
+  return INT4GEMV_OK;
+}
+
+// csrc/common.cuh:84-89 (reference).
+int check_threads(const char* name, int64_t threads) {
+  if (!(threads >= 32 && threads <= 1024 && threads % 32 == 0)) {
+    return fail(INT4GEMV_ERR_INVALID,
+                "%s: threads_per_block must be a multiple of 32 in [32, 1024], got %lld", name,
+                static_cast<long long>(threads));
+  }
+  return INT4GEMV_OK;
+}
+
+// csrc/common.cuh:94-101 (reference).
+int check_16_byte_loads(const char* name, const void* x, const void* q, int64_t group) {
+  if (group % 32 != 0) {
+    return fail(INT4GEMV_ERR_INVALID, "%s: group_size must be a multiple of 32, got %lld", name,
+                static_cast<long long>(group));
+  }
+  if (reinterpret_cast<uintptr_t>(x) % 16 != 0 || reinterpret_cast<uintptr_t>(q) % 16 != 0) {
+    return fail(INT4GEMV_ERR_INVALID, "%s: x and qweight must be 16-byte aligned", name);
+  }
+  return INT4GEMV_OK;
+}
+
+// csrc/common.cuh:67-82 (reference); the reference's message carries no operator name.
+int check_rows_per_warp(int64_t rpw) {
+  if (rpw != 1 && rpw != 2 && rpw != 4) {
+    return fail(INT4GEMV_ERR_INVALID, "rows_per_warp must be 1, 2 or 4, got %lld",
+                static_cast<long long>(rpw));
+  }
+  return INT4GEMV_OK;
+}
+
+// csrc/common.cuh:105-112 (reference): say clearly when registers limit the block size.
+int check_launchable(const char* name, int m, int threads, int rpw) {
+  int max_threads = 0;
+  const cudaError_t err = i4::vectorized_max_threads(m, rpw, &max_threads);
+  if (err != cudaSuccess) return cuda_fail(name, err);
+  if (threads > max_threads) {
+    i4::KernelAttrs at{};
+    i4::simt_attrs("vectorized", m, 32, rpw, &at);
+    return fail(INT4GEMV_ERR_INVALID,
+                "%s: this configuration uses %d registers per thread, so blocks of at most %d "
+                "threads fit, not %d",
+                name, at.registers, max_threads, threads);
+  }
+  return INT4GEMV_OK;
+}
+
+i4::GemvArgs make_args(void* y, const void* x, const void* q, const void* s, const void* z,
+                       int64_t m, int64_t n, int64_t k, int64_t group) {
+  return i4::GemvArgs{static_cast<half*>(y),
+                      static_cast<const half*>(x),
+                      static_cast<const uint32_t*>(q),
+                      static_cast<const half*>(s),
+                      static_cast<const half*>(z),
+                      static_cast<int>(m),
+                      static_cast<int>(n),
+                      static_cast<int>(k),
+                      static_cast<int>(group)};
+}
+
+// M or N = 0: nothing to do. K = 0: y is all zeros (an empty sum).
+int empty_cases(const char* name, void* y, int64_t m, int64_t n, int64_t k, cudaStream_t stream,
+                bool* done) {
+  *done = true;
+  if (m == 0 || n == 0) return ok();
+  if (k == 0) {
+    const cudaError_t err = cudaMemsetAsync(y, 0, static_cast<size_t>(m * n * 2), stream);
+    return err == cudaSuccess ? ok() : cuda_fail(name, err);
+  }
+  *done = false;
+  return INT4GEMV_OK;
+}
+
+int launched(const char* name, cudaError_t err) { return err == cudaSuccess ? ok() : cuda_fail(name, err); }
+
+enum class Pick { kMmaPipeline, kVectorized, kCoalesced };
+
+Pick pick_kernel(const i4::GemvArgs& a) {
+  if (i4::mma_pipeline_supported(a, nullptr)) return Pick::kMmaPipeline;
+  if (a.group % 32 == 0 && reinterpret_cast<uintptr_t>(a.x) % 16 == 0 &&
+      reinterpret_cast<uintptr_t>(a.q) % 16 == 0) {
+    return Pick::kVectorized;
+  }
+  return Pick::kCoalesced;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* int4gemv_last_error(void) { return g_last_error.c_str(); }
+
+int int4gemv_version(void) { return 100; }
+
+int int4gemv_naive(void* y, const void* x, const void* qweight, const void* scales,
+                   const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
+                   void* stream) {
+  const char* name = "naive";
+  if (int e = check_sizes(name, m, n, k, group_size)) return e;
+  if (int e = check_pointers(name, m, n, k, y, x, qweight, scales, zeros)) return e;
+  bool done;
+  const auto st = static_cast<cudaStream_t>(stream);
+  int e = empty_cases(name, y, m, n, k, st, &done);
+  if (done) return e;
+  return launched(name, i4::launch_naive(make_args(y, x, qweight, scales, zeros, m, n, k, group_size), st));
+}
+
+int int4gemv_coalesced(void* y, const void* x, const void* qweight, const void* scales,
+                       const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
+                       void* stream) {
+  const char* name = "coalesced";
+  if (int e = check_sizes(name, m, n, k, group_size)) return e;
+  if (int e = check_pointers(name, m, n, k, y, x, qweight, scales, zeros)) return e;
+  bool done;
+  const auto st = static_cast<cudaStream_t>(stream);
+  int e = empty_cases(name, y, m, n, k, st, &done);
+  if (done) return e;
+  return launched(name,
+                  i4::launch_coalesced(make_args(y, x, qweight, scales, zeros, m, n, k, group_size), st));
+}
+
+int int4gemv_vectorized(void* y, const void* x, const void* qweight, const void* scales,
+                        const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
+                        int64_t threads_per_block, int64_t rows_per_warp, void* stream) {
+  const char* name = "vectorized";
+  if (int e = check_sizes(name, m, n, k, group_size)) return e;
+  if (int e = check_threads(name, threads_per_block)) return e;
+  if (int e = check_16_byte_loads(name, x, qweight, group_size)) return e;
+  if (int e = check_pointers(name, m, n, k, y, x, qweight, scales, zeros)) return e;
+  bool done;
+  const auto st = static_cast<cudaStream_t>(stream);
+  int e = empty_cases(name, y, m, n, k, st, &done);
+  if (done) return e;
+  if (int e2 = check_rows_per_warp(rows_per_warp)) return e2;
+  if (int e2 = check_launchable(name, static_cast<int>(m), static_cast<int>(threads_per_block),
+                                static_cast<int>(rows_per_warp)))
+    return e2;
+  return launched(name, i4::launch_vectorized(
+                            make_args(y, x, qweight, scales, zeros, m, n, k, group_size),
+                            static_cast<int>(threads_per_block), static_cast<int>(rows_per_warp), st));
+}
+
+int int4gemv_load_only(void* out, const void* x, const void* qweight, const void* scales,
+                       const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
+                       int64_t threads_per_block, int64_t rows_per_warp, void* stream) {
+  const char* name = "load_only";
+  if (int e = check_sizes(name, m, n, k, group_size)) return e;
+  if (int e = check_threads(name, threads_per_block)) return e;
+  if (m != 1) return fail(INT4GEMV_ERR_INVALID, "load_only: needs M = 1, got %lld", static_cast<long long>(m));
+  if (int e = check_16_byte_loads(name, x, qweight, group_size)) return e;
+  if (int e = check_pointers(name, 1, n, k, out, x, qweight, scales, zeros)) return e;
+  const auto st = static_cast<cudaStream_t>(stream);
+  if (n == 0) return ok();
+  if (k == 0) {
+    const cudaError_t err = cudaMemsetAsync(out, 0, static_cast<size_t>(n * 4), st);
+    return err == cudaSuccess ? ok() : cuda_fail(name, err);
+  }
+  if (int e = check_rows_per_warp(rows_per_warp)) return e;
+  if (int e = check_launchable(name, 1, static_cast<int>(threads_per_block),
+                               static_cast<int>(rows_per_warp)))
+    return e;
+  return launched(name, i4::launch_load_only(static_cast<uint32_t*>(out),
+                                             make_args(nullptr, x, qweight, scales, zeros, 1, n, k,
+                                                       group_size),
+                                             static_cast<int>(threads_per_block),
+                                             static_cast<int>(rows_per_warp), st));
+}
+
+int int4gemv_kernel_info(const char* kernel, int64_t m, int64_t threads_per_block,
+                         int64_t rows_per_warp, int64_t* info) {
+  if (!kernel || !info) return fail(INT4GEMV_ERR_INVALID, "kernel_info: null argument");
+  if (m < 0 || m > INT_MAX) return fail(INT4GEMV_ERR_INVALID, "kernel_info: bad M = %lld", static_cast<long long>(m));
+  i4::KernelAttrs at{};
+  cudaError_t err;
+  if (std::strcmp(kernel, "vectorized") == 0) {
+    if (int e = check_threads("vectorized_info", threads_per_block)) return e;
+    if (int e = check_rows_per_warp(rows_per_warp)) return e;
+    err = i4::simt_attrs("vectorized", static_cast<int>(m), static_cast<int>(threads_per_block),
+                         static_cast<int>(rows_per_warp), &at);
+  } else if (std::strcmp(kernel, "naive") == 0 || std::strcmp(kernel, "coalesced") == 0) {
+    err = i4::simt_attrs(kernel, static_cast<int>(m), 0, 1, &at);
+  } else if (std::strcmp(kernel, "w4a16") == 0) {
+    err = i4::mma_pipeline_attrs(static_cast<int>(m <= 16 ? m : 16), &at);
+  } else {
+    return fail(INT4GEMV_ERR_INVALID, "kernel_info: unknown kernel '%s'", kernel);
+  }
+  if (err != cudaSuccess) return cuda_fail("kernel_info", err);
+  info[0] = at.registers;
+  info[1] = at.local_bytes;
+  info[2] = at.threads_per_block;
+  info[3] = at.max_threads_per_block;
+  info[4] = at.blocks_per_sm;
+  info[5] = static_cast<int64_t>(at.blocks_per_sm) * at.threads_per_block / 32;
+  return ok();
+}
+
+int int4gemv_sequential(void* y, const void* x, const void* qweight, const void* scales,
+                        const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
+                        int64_t threads) {
+  const char* name = "sequential";
+  if (int e = check_sizes(name, m, n, k, group_size)) return e;
+  if (int e = check_pointers(name, m, n, k, y, x, qweight, scales, zeros)) return e;
+  if (m == 0 || n == 0) return ok();
+  if (k == 0) {
+    std::memset(y, 0, static_cast<size_t>(m * n * 2));
+    return ok();
+  }
+  i4::sequential_cpu(static_cast<uint16_t*>(y), static_cast<const uint16_t*>(x),
+                     static_cast<const uint32_t*>(qweight), static_cast<const uint16_t*>(scales),
+                     static_cast<const uint16_t*>(zeros), m, n, k, group_size, threads);
+  return ok();
+}
+
+int64_t int4gemv_w4a16_workspace_size(int64_t m, int64_t n, int64_t k, int64_t group_size) {
+  (void)m, (void)n, (void)k, (void)group_size;
+  return 0;
+}
+
+int int4gemv_w4a16(void* y, const void* x, const void* qweight, const void* scales,
+                   const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
+                   void* workspace, int64_t workspace_bytes, void* stream) {
+  (void)workspace, (void)workspace_bytes;
+  const char* name = "w4a16";
+  if (int e = check_sizes(name, m, n, k, group_size)) return e;
+  if (int e = check_pointers(name, m, n, k, y, x, qweight, scales, zeros)) return e;
+  bool done;
+  const auto st = static_cast<cudaStream_t>(stream);
+  int e = empty_cases(name, y, m, n, k, st, &done);
+  if (done) return e;
+  const i4::GemvArgs a = make_args(y, x, qweight, scales, zeros, m, n, k, group_size);
+  switch (pick_kernel(a)) {
+    case Pick::kMmaPipeline:
+      return launched(name, i4::launch_mma_pipeline(a, st));
+    case Pick::kVectorized:
+      return launched(name, i4::launch_vectorized(a, 128, 2, st));
+    default:
+      return launched(name, i4::launch_coalesced(a, st));
+  }
+}
+
+const char* int4gemv_w4a16_kernel_name(const void* x, const void* qweight, const void* scales,
+                                       const void* zeros, int64_t m, int64_t n, int64_t k,
+                                       int64_t group_size) {
+  if (m <= 0 || n <= 0 || k <= 0 || m > INT_MAX || n > INT_MAX || k > INT_MAX ||
+      group_size <= 0 || group_size % 8 || k % group_size) {
+    return "none";
+  }
+  const i4::GemvArgs a = make_args(nullptr, x, qweight, scales, zeros, m, n, k, group_size);
+  switch (pick_kernel(a)) {
+    case Pick::kMmaPipeline:
+      return "mma_pipeline";
+    case Pick::kVectorized:
+      return "vectorized";
+    default:
+      return "coalesced";
+  }
+}
+
+int int4gemv_unpack(void* q, const void* qweight, int64_t n, int64_t k, void* stream) {
+  const char* name = "unpack";
+  if (n < 0 || k < 0 || k % 8 != 0) {
+    return fail(INT4GEMV_ERR_INVALID, "unpack: N = %lld, K = %lld: K must be a non-negative multiple of 8",
+                static_cast<long long>(n), static_cast<long long>(k));
+  }
+  if (n == 0 || k == 0) return ok();
+  if (!q || !qweight) return fail(INT4GEMV_ERR_INVALID, "unpack: null pointer");
+  if (reinterpret_cast<uintptr_t>(q) % 16 != 0) {
+    return fail(INT4GEMV_ERR_INVALID, "unpack: output must be 16-byte aligned");
+  }
+  return launched(name, i4::launch_unpack(static_cast<int32_t*>(q), static_cast<const uint32_t*>(qweight),
+                                          n, k, static_cast<cudaStream_t>(stream)));
+}
+
+int int4gemv_dequantize(void* w, const void* qweight, const void* scales, const void* zeros,
+                        int64_t n, int64_t k, int64_t group_size, void* stream) {
+  const char* name = "dequantize";
+  if (int e = check_sizes(name, 0, n, k, group_size)) return e;
+  if (n == 0 || k == 0) return ok();
+  if (!w || !qweight || !scales || !zeros) return fail(INT4GEMV_ERR_INVALID, "dequantize: null pointer");
+  if (reinterpret_cast<uintptr_t>(w) % 16 != 0) {
+    return fail(INT4GEMV_ERR_INVALID, "dequantize: output must be 16-byte aligned");
+  }
+  return launched(name, i4::launch_dequantize(static_cast<float*>(w), static_cast<const uint32_t*>(qweight),
+                                              static_cast<const half*>(scales), static_cast<const half*>(zeros),
+                                              n, k, group_size, static_cast<cudaStream_t>(stream)));
+}
+
+int int4gemv_device_status(int* status) {
+  if (!status) return fail(INT4GEMV_ERR_INVALID, "device_status: null argument");
+  const cudaError_t err = i4::read_and_clear_status(status);
+  return err == cudaSuccess ? ok() : cuda_fail("device_status", err);
+}
+
+}  // extern "C"

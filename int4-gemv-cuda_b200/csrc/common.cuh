@@ -1,0 +1,172 @@
+// Device helpers shared by the sm_100a kernels: nibble unpacking, warp reductions, and the
+// mbarrier / bulk-copy primitives of the TMA pipeline (inline PTX), with bounded waits.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace i4 {
+
+constexpr int kWarp = 32;
+
+// Status codes a kernel writes to the device status word when a bounded wait gives up.
+constexpr int kStatusFullBarrierTimeout = 1;
+constexpr int kStatusEmptyBarrierTimeout = 2;
+
+// About one second at B200 clocks. A correct pipeline never waits more than microseconds.
+constexpr long long kWaitLimitCycles = 2000000000LL;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---- Nibble unpacking -------------------------------------------------------------------------
+//
+// A packed word holds q0..q7 (q_j in bits 4j..4j+3). OR-ing a nibble into the mantissa of the
+// fp16 constant 1024 (0x6400, mantissa step 1) gives 1024 + q exactly; a nibble in mantissa bits
+// 4..7 gives 1024 + 16 q. One LOP3 per half2, one shift per word:
+//   h[0] = (1024 + q0,      1024 + q4)
+//   h[1] = (1024 + 16 q1,   1024 + 16 q5)
+//   h[2] = (1024 + q2,      1024 + q6)
+//   h[3] = (1024 + 16 q3,   1024 + 16 q7)
+__device__ __forceinline__ void unpack_x16(uint32_t w, uint32_t (&h)[4]) {
+  const uint32_t hi = w >> 8;
+  asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(h[0]) : "r"(w), "r"(0x000F000Fu), "r"(0x64006400u));
+  asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(h[1]) : "r"(w), "r"(0x00F000F0u), "r"(0x64006400u));
+  asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(h[2]) : "r"(hi), "r"(0x000F000Fu), "r"(0x64006400u));
+  asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(h[3]) : "r"(hi), "r"(0x00F000F0u), "r"(0x64006400u));
+}
+
+// Same trick without the factor 16: h[j] = (1024 + q_j, 1024 + q_{j+4}) for j = 0..3.
+__device__ __forceinline__ void unpack_pairs(uint32_t w, uint32_t (&h)[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    asm("lop3.b32 %0, %1, %2, %3, 0xea;"
+        : "=r"(h[j])
+        : "r"(w >> (4 * j)), "r"(0x000F000Fu), "r"(0x64006400u));
+  }
+}
+
+__device__ __forceinline__ float2 half2_bits_to_float2(uint32_t bits) {
+  __half2 h;
+  memcpy(&h, &bits, sizeof(h));
+  return __half22float2(h);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int off = kWarp / 2; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+__device__ __forceinline__ uint32_t warp_xor(uint32_t v) {
+#pragma unroll
+  for (int off = kWarp / 2; off > 0; off >>= 1) v ^= __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+// ---- Loads ------------------------------------------------------------------------------------
+
+// 16-byte streaming load: read once, keep it out of L1.
+__device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// ---- mbarrier and bulk copies (sm_90+ PTX, used here on sm_100a) ------------------------------
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Waits for the phase with the given parity to complete, for at most kWaitLimitCycles. Returns
+// false on timeout (the caller records a status and stops).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long start = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - start > kWaitLimitCycles) return false;
+  }
+  return true;
+}
+
+// L2 policy for data read exactly once (the packed weights): evict it first.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t policy;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+  return policy;
+}
+
+// 1-D bulk copy global -> shared, completion counted in bytes on `bar`. dst, src and bytes must
+// be multiples of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                         uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1], %2, [%3], %4;" ::"r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+
+// 4-byte asynchronous copy global -> shared (Ampere-style cp.async).
+__device__ __forceinline__ void cp_async_4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src)
+               : "memory");
+}
+
+// Arrive on `bar` once every cp.async this thread issued so far has landed. The arrival is one
+// of the barrier's expected arrivals (.noinc).
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+// Named barrier over `threads` threads (a multiple of 32), id 1..15.
+__device__ __forceinline__ void named_barrier(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// ---- Tensor core (warp-level) -------------------------------------------------------------------
+
+// D = A * B + C, m16n8k16, A row-major f16, B column-major f16, C / D f32.
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                          uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+}  // namespace i4

@@ -1,0 +1,59 @@
+// Internal interface between the C ABI (capi.cu) and the kernel launchers. Host-only types, no
+// torch. Every launcher assumes its arguments were validated by the C ABI layer and M, N > 0.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace i4 {
+
+struct GemvArgs {
+  half* y;             // [m, n]
+  const half* x;       // [m, k]
+  const uint32_t* q;   // [n, k / 8]
+  const half* s;       // [n, k / group]
+  const half* z;       // [n, k / group]
+  int m, n, k, group;
+};
+
+// Attributes of one compiled kernel, for the *_info entry points.
+struct KernelAttrs {
+  int registers;
+  int local_bytes;
+  int max_threads_per_block;
+  int blocks_per_sm;  // occupancy at the given block size and dynamic shared memory
+  int threads_per_block;
+};
+
+// SIMT kernels (simt.cu): the reference operators' mappings, rewritten for sm_100a.
+cudaError_t launch_naive(const GemvArgs& a, cudaStream_t stream);
+cudaError_t launch_coalesced(const GemvArgs& a, cudaStream_t stream);
+cudaError_t launch_vectorized(const GemvArgs& a, int threads_per_block, int rows_per_warp,
+                              cudaStream_t stream);
+cudaError_t launch_load_only(uint32_t* out, const GemvArgs& a, int threads_per_block,
+                             int rows_per_warp, cudaStream_t stream);
+// Registers etc. of the kernel instance the launcher would pick for (m, threads, rows_per_warp).
+cudaError_t simt_attrs(const char* kernel, int m, int threads_per_block, int rows_per_warp,
+                       KernelAttrs* out);
+// Largest block the vectorized instance for (m, rows_per_warp) can launch with (registers).
+cudaError_t vectorized_max_threads(int m, int rows_per_warp, int* max_threads);
+
+// TMA-bulk-fed tensor-core pipeline (mma_pipeline.cu). `why` gets a reason when unsupported.
+bool mma_pipeline_supported(const GemvArgs& a, const char** why);
+cudaError_t launch_mma_pipeline(const GemvArgs& a, cudaStream_t stream);
+cudaError_t mma_pipeline_attrs(int m, KernelAttrs* out);
+// Reads and clears the device status word of the current device (synchronous).
+cudaError_t read_and_clear_status(int* status);
+
+// Packed-format helpers (packed.cu).
+cudaError_t launch_unpack(int32_t* q, const uint32_t* qweight, int64_t n, int64_t k,
+                          cudaStream_t stream);
+cudaError_t launch_dequantize(float* w, const uint32_t* qweight, const half* s, const half* z,
+                              int64_t n, int64_t k, int64_t group, cudaStream_t stream);
+
+// SM count of the current device (cached per device).
+int sm_count();
+
+}  // namespace i4

@@ -1,0 +1,232 @@
+"""Parity of every CUDA kernel with the oracle, on a B200. Run with: pytest -m gpu.
+
+Tolerance (written here, applied by oracle.check_close): |y - ref| <= min(1e-2 * rms(ref), 1e-2)
++ 1e-2 * |ref|, i.e. both the reference's rule (int4gemv/reference.py:13-22) and the tier's
+rtol = atol = 1e-2. Unpack and dequantize are compared bit for bit.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from int4gemv import ops
+
+pytestmark = pytest.mark.gpu
+RTOL = 1e-2
+ATOL = 1e-2
+
+KERNELS = [
+    ("naive", {}),
+    ("coalesced", {}),
+    ("vectorized", {}),
+    ("vectorized", {"threads_per_block": 256, "rows_per_warp": 1}),
+    ("vectorized", {"threads_per_block": 64, "rows_per_warp": 4}),
+    ("w4a16", {}),
+]
+
+
+def cuda(*arrays):
+    return [torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in arrays]
+
+
+def run(name, cfg, args, g):
+    y = getattr(ops, name)(*args, g, **cfg)
+    torch.cuda.synchronize()
+    return y
+
+
+def assert_close(y, ref, what=""):
+    ok, msg = oracle.check_close(y.float().cpu().numpy() if isinstance(y, torch.Tensor) else y,
+                                 ref, RTOL, ATOL)
+    assert ok, f"{what}: {msg}"
+
+
+@pytest.mark.parametrize("name,cfg", KERNELS, ids=[f"{n}{c}" for n, c in KERNELS])
+def test_golden(golden, name, cfg):
+    g = int(golden["group_size"])
+    args = cuda(golden["x"], golden["qweight"], golden["scales"], golden["zeros"])
+    if name == "vectorized" and g % 32 != 0:
+        with pytest.raises(RuntimeError, match="group_size must be a multiple of 32"):
+            run(name, cfg, args, g)
+        return
+    y = run(name, cfg, args, g)
+    assert y.dtype == torch.float16 and tuple(y.shape) == golden["y_ref"].shape
+    assert_close(y, golden["y_ref"], f"{golden['name']} vs reference.py")
+    ref64 = oracle.reference(golden["x"], golden["qweight"], golden["scales"], golden["zeros"], g)
+    assert_close(y, ref64, f"{golden['name']} vs oracle")
+
+
+def test_unpack_dequantize_bit_exact(golden):
+    g = int(golden["group_size"])
+    qw, s, z = cuda(golden["qweight"], golden["scales"], golden["zeros"])
+    q = ops.unpack(qw).cpu().numpy()
+    np.testing.assert_array_equal(q, oracle.unpack(golden["qweight"]))
+    w = ops.dequantize(qw, s, z, g).cpu().numpy()
+    want = golden["deq"] if "deq" in golden else oracle.dequantize(
+        golden["qweight"], golden["scales"], golden["zeros"], g)
+    np.testing.assert_array_equal(w.view(np.uint32), want.view(np.uint32))
+
+
+# BASELINE.json configs at full size: M = 1 shapes, the M sweep, and the full sharded shapes.
+FULL = [
+    (1, 4096, 4096), (1, 8192, 8192), (1, 14336, 4096), (1, 4096, 14336),
+    (2, 8192, 8192), (4, 8192, 8192), (8, 8192, 8192), (16, 8192, 8192), (32, 8192, 8192),
+    (1, 28672, 8192), (1, 8192, 28672), (8, 28672, 8192), (8, 8192, 28672),
+]
+
+
+@pytest.mark.parametrize("m,n,k", FULL, ids=[f"m{m}_n{n}_k{k}" for m, n, k in FULL])
+def test_full_size_w4a16(m, n, k):
+    x, q, s, z = oracle.synthetic(m, n, k, 128, seed=m + n + k)
+    args = cuda(x, q, s, z)
+    y = ops.w4a16(*args, 128)
+    ref = oracle.reference(x, q, s, z, 128)
+    assert_close(y, ref, f"w4a16 {m}x{n}x{k} ({ops.w4a16_kernel(*args, 128)})")
+    if m <= 8:
+        assert ops.w4a16_kernel(*args, 128) == "mma_pipeline"
+
+
+@pytest.mark.parametrize("name,cfg", KERNELS[:3] + [("w4a16", {})])
+def test_config0_all_kernels(name, cfg):
+    x, q, s, z = oracle.synthetic(1, 4096, 4096, 128, seed=0)
+    y = run(name, cfg, cuda(x, q, s, z), 128)
+    assert_close(y, oracle.reference(x, q, s, z), name)
+    # and against the reference's own CPU path, bit-exact oracle of csrc/sequential.cpp
+    assert_close(y, oracle.sequential(x, q, s, z).astype(np.float32), name + " vs sequential")
+
+
+ODD = [
+    (1, 1, 256, 128), (1, 7, 384, 128), (3, 17, 640, 128), (5, 149, 1024, 64), (9, 150, 512, 32),
+    (16, 300, 2048, 128), (13, 37, 768, 256), (2, 148 * 130 + 5, 1024, 128), (1, 64, 8192, 128),
+    (7, 5000, 1152, 128), (12, 256, 4096, 128), (1, 19000, 256, 32), (2, 333, 896, 64),
+]
+
+
+@pytest.mark.parametrize("m,n,k,g", ODD, ids=[f"m{m}_n{n}_k{k}_g{g}" for m, n, k, g in ODD])
+def test_ragged_shapes(m, n, k, g):
+    x, q, s, z = oracle.synthetic(m, n, k, g, seed=n * 7 + k)
+    args = cuda(x, q, s, z)
+    ref = oracle.reference(x, q, s, z, g)
+    for name, cfg in KERNELS:
+        assert_close(run(name, cfg, args, g), ref, f"{name}{cfg}")
+
+
+def test_group_sizes_without_fast_path():
+    # group 8 and 16: only naive / coalesced / w4a16 (which falls back) apply
+    for g in (8, 16, 24):
+        x, q, s, z = oracle.synthetic(3, 40, 96 * (g // 8), g, seed=g)
+        args = cuda(x, q, s, z)
+        ref = oracle.reference(x, q, s, z, g)
+        for name in ("naive", "coalesced", "w4a16"):
+            assert_close(run(name, {}, args, g), ref, f"{name} g={g}")
+        assert ops.w4a16_kernel(*args, g) == "coalesced"
+
+
+def test_empty_and_zero_k():
+    for name, cfg in KERNELS:
+        x = torch.zeros(0, 256, dtype=torch.float16, device="cuda")
+        q = torch.zeros(8, 32, dtype=torch.int32, device="cuda")
+        s = torch.ones(8, 2, dtype=torch.float16, device="cuda")
+        assert run(name, cfg, (x, q, s, s), 128).shape == (0, 8)
+        x = torch.zeros(3, 256, dtype=torch.float16, device="cuda")
+        assert run(name, cfg, (x, q[:0], s[:0], s[:0]), 128).shape == (3, 0)
+        x = torch.zeros(3, 0, dtype=torch.float16, device="cuda")
+        q0 = torch.zeros(8, 0, dtype=torch.int32, device="cuda")
+        s0 = torch.zeros(8, 0, dtype=torch.float16, device="cuda")
+        y = run(name, cfg, (x, q0, s0, s0), 128)
+        assert y.shape == (3, 8) and bool((y == 0).all())
+
+
+def test_misaligned_inputs():
+    x, q, s, z = oracle.synthetic(2, 64, 512, 128, seed=5)
+    xs = torch.empty(x.size + 8, dtype=torch.float16, device="cuda")
+    xs = xs[1:1 + x.size].view(2, 512)  # 2-byte aligned only
+    xs.copy_(torch.from_numpy(x))
+    args = [xs] + cuda(q, s, z)
+    ref = oracle.reference(x, q, s, z)
+    assert ops.w4a16_kernel(*args, 128) == "coalesced"
+    assert_close(run("w4a16", {}, args, 128), ref, "w4a16 misaligned x")
+    assert_close(run("naive", {}, args, 128), ref, "naive misaligned x")
+    with pytest.raises(RuntimeError, match="x and qweight must be 16-byte aligned"):
+        run("vectorized", {}, args, 128)
+
+
+def test_deterministic():
+    x, q, s, z = oracle.synthetic(4, 8192, 8192, 128, seed=11)
+    args = cuda(x, q, s, z)
+    a = ops.w4a16(*args, 128)
+    b = ops.w4a16(*args, 128)
+    assert torch.equal(a, b)
+
+
+def test_noncontiguous_and_device_checks():
+    x, q, s, z = cuda(*oracle.synthetic(2, 64, 256, 128))
+    with pytest.raises(RuntimeError, match="w4a16: inputs must be contiguous"):
+        ops.w4a16(x, q.T.contiguous().T, s, z, 128)
+    with pytest.raises(RuntimeError, match="expected all inputs on one cuda device"):
+        ops.w4a16(x, q, s.cpu(), z, 128)
+
+
+def test_register_limit_message():
+    with pytest.raises(RuntimeError, match=r"vectorized: this configuration uses \d+ registers per "
+                                           r"thread, so blocks of at most \d+ threads fit, not 1024"):
+        x, q, s, z = cuda(*oracle.synthetic(8, 64, 256, 128))
+        ops.vectorized(x, q, s, z, 128, threads_per_block=1024, rows_per_warp=4)
+
+
+def load_only_oracle(x, q, s, z, g):
+    """out[r] = XOR of row r's words, of its scale / zero bit patterns (once per group), and of
+    the x words read with every 32-weight chunk."""
+    n, words = q.shape
+    k = words * 8
+    xw = np.ascontiguousarray(x[0]).view(np.uint32).reshape(k // 32, 16)
+    x_per_chunk = np.bitwise_xor.reduce(xw, axis=1)
+    x_all = np.bitwise_xor.reduce(x_per_chunk)
+    out = np.bitwise_xor.reduce(q.view(np.uint32), axis=1)
+    out ^= x_all
+    out ^= np.bitwise_xor.reduce(s.view(np.uint16).astype(np.uint32), axis=1)
+    out ^= np.bitwise_xor.reduce(z.view(np.uint16).astype(np.uint32), axis=1)
+    return out
+
+
+@pytest.mark.parametrize("tpb,rpw", [(128, 2), (32, 1), (256, 4)])
+def test_load_only(tpb, rpw):
+    x, q, s, z = oracle.synthetic(1, 333, 1024, 128, seed=2)
+    out = ops.load_only(*cuda(x, q, s, z), 128, threads_per_block=tpb, rows_per_warp=rpw)
+    np.testing.assert_array_equal(out.cpu().numpy().view(np.uint32), load_only_oracle(x, q, s, z, 128))
+
+
+def test_kernel_info():
+    for name, info in ops.KERNEL_INFO.items():
+        d = info(1)
+        assert set(d) == {"registers", "local_bytes", "threads_per_block", "max_threads_per_block",
+                          "blocks_per_sm", "warps_per_sm"}
+        assert d["registers"] > 0 and d["blocks_per_sm"] >= 1, (name, d)
+    d = ops.KERNEL_INFO["vectorized"](8, threads_per_block=256, rows_per_warp=4)
+    assert d["threads_per_block"] == 256
+
+
+def test_matches_reference_gpu_kernels():
+    """The reference's own CUDA kernels, built from its sources for sm_100a, agree with ours."""
+    import importlib.util
+    from pathlib import Path
+    so = sorted((Path(__file__).resolve().parents[1] / "oracle" / "_ref").glob("int4gemv_ref*.so"))
+    if not so:
+        pytest.skip("reference not built (oracle/_ref)")
+    spec = importlib.util.spec_from_file_location("int4gemv_ref", so[0])
+    ref = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ref)
+    for m in (1, 8):
+        x, q, s, z = oracle.synthetic(m, 4096, 4096, 128, seed=m)
+        args = cuda(x, q, s, z)
+        theirs = ref.vectorized(*args, 128).float().cpu().numpy()
+        assert_close(theirs, oracle.reference(x, q, s, z), "reference vectorized vs oracle")
+        ours = ops.w4a16(*args, 128).float().cpu().numpy()
+        assert_close(ours, oracle.reference(x, q, s, z), "w4a16 vs oracle")
+        assert np.max(np.abs(ours - theirs)) <= 0.02 * (1 + np.max(np.abs(theirs)))
+
+
+def test_device_status_clean():
+    from int4gemv import capi
+    assert capi.device_status() == 0
