@@ -493,8 +493,42 @@ def run_ours(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def run_profile_case(args):
+    """A few launches of one kernel for ncu (no timing, no JSON): --profile KERNEL."""
+    from int4gemv import ops
+    import torch.nn.functional as F
+
+    global M, N, K
+    M, N, K = args.m, args.n, args.k
+    torch.cuda.set_device(0)
+    set_bytes = N * K // 2 + 2 * N * (K // GROUP) * 2
+    n_sets = max(2, math.ceil(L2_BYTES / set_bytes) + 1)
+    sets, x = make_sets(n_sets, seed=7)
+    if args.profile == "cublas":
+        w16 = [torch.randn(N, K, device="cuda", dtype=torch.float16) for _ in range(2)]
+        fns = [lambda w=w: F.linear(x, w) for w in w16]
+    elif args.profile == "reference_vectorized":
+        ref = reference_module()
+        fns = [lambda i=i: ref.vectorized(x, *sets[i], GROUP) for i in range(n_sets)]
+    else:
+        fn = getattr(ops, args.profile)
+        fns = [lambda i=i: fn(x, *sets[i], GROUP) for i in range(n_sets)]
+    for i in range(args.calls):
+        fns[i % len(fns)]()
+    torch.cuda.synchronize()
+    print(f"profile case {args.profile} M={M} N={N} K={K}: {args.calls} calls, "
+          f"{n_sets} weight sets")
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--profile", default=None,
+                    help="run --calls launches of one kernel (w4a16, vectorized, naive, coalesced, "
+                         "load_only, cublas, reference_vectorized) for ncu, then exit")
+    ap.add_argument("--m", type=int, default=M)
+    ap.add_argument("--n", type=int, default=N)
+    ap.add_argument("--k", type=int, default=K)
+    ap.add_argument("--calls", type=int, default=6)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20000)
     ap.add_argument("--warmup", type=int, default=200)
@@ -503,6 +537,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    if args.profile:
+        run_profile_case(args)
+        return
     world, rank, local = (int(os.environ.get("WORLD_SIZE", "1")),
                           int(os.environ.get("RANK", "0")),
                           int(os.environ.get("LOCAL_RANK", "0")))

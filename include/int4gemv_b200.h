@@ -97,6 +97,13 @@ const char* int4gemv_w4a16_kernel_name(const void* x, const void* qweight, const
                                        const void* zeros, int64_t m, int64_t n, int64_t k,
                                        int64_t group_size);
 
+/* Runs one named kernel instead of the automatic choice: "tcgen05", "mma_pipeline", "vectorized"
+ * (128 threads, 2 rows per warp), "coalesced" or "naive". For tests and benchmarks. Fails with
+ * INT4GEMV_ERR_INVALID if that kernel does not support the shape or the pointers' alignment. */
+int int4gemv_w4a16_kernel(const char* kernel, void* y, const void* x, const void* qweight,
+                          const void* scales, const void* zeros, int64_t m, int64_t n, int64_t k,
+                          int64_t group_size, void* stream);
+
 /* ---- Packed-format helpers on the device (int4gemv/quant.py:40-53), bit-exact ---------------- */
 
 /* q [N, K] int32 = the 4-bit values of qweight [N, K/8]   (quant.py:40-44). */

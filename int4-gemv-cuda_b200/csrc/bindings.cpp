@@ -117,6 +117,18 @@ at::Tensor w4a16(const at::Tensor& x, const at::Tensor& qweight, const at::Tenso
   return y;
 }
 
+at::Tensor w4a16_with(const at::Tensor& x, const at::Tensor& qweight, const at::Tensor& scales,
+                      const at::Tensor& zeros, int64_t group_size, const std::string& kernel) {
+  check_inputs("w4a16", x, qweight, scales, zeros, group_size, c10::DeviceType::CUDA);
+  const c10::cuda::CUDAGuard guard(x.device());
+  at::Tensor y = x.new_empty({x.size(0), qweight.size(0)});
+  check_status(int4gemv_w4a16_kernel(kernel.c_str(), y.data_ptr(), x.data_ptr(),
+                                     qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(),
+                                     x.size(0), qweight.size(0), x.size(1), group_size,
+                                     stream_of(x)));
+  return y;
+}
+
 std::string w4a16_kernel(const at::Tensor& x, const at::Tensor& qweight, const at::Tensor& scales,
                          const at::Tensor& zeros, int64_t group_size) {
   check_inputs("w4a16", x, qweight, scales, zeros, group_size, c10::DeviceType::CUDA);
@@ -178,6 +190,8 @@ PYBIND11_MODULE(int4gemv_ops, m) {
   m.def("w4a16", &int4gemv::w4a16, py::arg("x"), py::arg("qweight"), py::arg("scales"),
         py::arg("zeros"), py::arg("group_size"));
   m.def("w4a16_info", &int4gemv::w4a16_info, py::arg("m"));
+  m.def("w4a16_with", &int4gemv::w4a16_with, py::arg("x"), py::arg("qweight"), py::arg("scales"),
+        py::arg("zeros"), py::arg("group_size"), py::arg("kernel"));
   m.def("w4a16_kernel", &int4gemv::w4a16_kernel, py::arg("x"), py::arg("qweight"),
         py::arg("scales"), py::arg("zeros"), py::arg("group_size"));
   m.def("unpack", &int4gemv::unpack, py::arg("qweight"));

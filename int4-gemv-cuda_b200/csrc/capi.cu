@@ -144,9 +144,10 @@ int empty_cases(const char* name, void* y, int64_t m, int64_t n, int64_t k, cuda
 
 int launched(const char* name, cudaError_t err) { return err == cudaSuccess ? ok() : cuda_fail(name, err); }
 
-enum class Pick { kMmaPipeline, kVectorized, kCoalesced };
+enum class Pick { kTcgen05, kMmaPipeline, kVectorized, kCoalesced };
 
 Pick pick_kernel(const i4::GemvArgs& a) {
+  if (i4::tc_gemv_supported(a, nullptr)) return Pick::kTcgen05;
   if (i4::mma_pipeline_supported(a, nullptr)) return Pick::kMmaPipeline;
   if (a.group % 32 == 0 && reinterpret_cast<uintptr_t>(a.x) % 16 == 0 &&
       reinterpret_cast<uintptr_t>(a.q) % 16 == 0) {
@@ -251,7 +252,8 @@ int int4gemv_kernel_info(const char* kernel, int64_t m, int64_t threads_per_bloc
   } else if (std::strcmp(kernel, "naive") == 0 || std::strcmp(kernel, "coalesced") == 0) {
     err = i4::simt_attrs(kernel, static_cast<int>(m), 0, 1, &at);
   } else if (std::strcmp(kernel, "w4a16") == 0) {
-    err = i4::mma_pipeline_attrs(static_cast<int>(m <= 16 ? m : 16), &at);
+    err = m <= 8 ? i4::tc_gemv_attrs(static_cast<int>(m), &at)
+                 : i4::mma_pipeline_attrs(static_cast<int>(m <= 16 ? m : 16), &at);
   } else {
     return fail(INT4GEMV_ERR_INVALID, "kernel_info: unknown kernel '%s'", kernel);
   }
@@ -300,6 +302,8 @@ int int4gemv_w4a16(void* y, const void* x, const void* qweight, const void* scal
   if (done) return e;
   const i4::GemvArgs a = make_args(y, x, qweight, scales, zeros, m, n, k, group_size);
   switch (pick_kernel(a)) {
+    case Pick::kTcgen05:
+      return launched(name, i4::launch_tc_gemv(a, st));
     case Pick::kMmaPipeline:
       return launched(name, i4::launch_mma_pipeline(a, st));
     case Pick::kVectorized:
@@ -318,6 +322,8 @@ const char* int4gemv_w4a16_kernel_name(const void* x, const void* qweight, const
   }
   const i4::GemvArgs a = make_args(nullptr, x, qweight, scales, zeros, m, n, k, group_size);
   switch (pick_kernel(a)) {
+    case Pick::kTcgen05:
+      return "tcgen05";
     case Pick::kMmaPipeline:
       return "mma_pipeline";
     case Pick::kVectorized:
@@ -325,6 +331,36 @@ const char* int4gemv_w4a16_kernel_name(const void* x, const void* qweight, const
     default:
       return "coalesced";
   }
+}
+
+int int4gemv_w4a16_kernel(const char* kernel, void* y, const void* x, const void* qweight,
+                          const void* scales, const void* zeros, int64_t m, int64_t n, int64_t k,
+                          int64_t group_size, void* stream) {
+  const char* name = "w4a16";
+  if (!kernel) return fail(INT4GEMV_ERR_INVALID, "w4a16: null kernel name");
+  if (int e = check_sizes(name, m, n, k, group_size)) return e;
+  if (int e = check_pointers(name, m, n, k, y, x, qweight, scales, zeros)) return e;
+  bool done;
+  const auto st = static_cast<cudaStream_t>(stream);
+  int e = empty_cases(name, y, m, n, k, st, &done);
+  if (done) return e;
+  const i4::GemvArgs a = make_args(y, x, qweight, scales, zeros, m, n, k, group_size);
+  const char* why = "unsupported shape";
+  if (std::strcmp(kernel, "tcgen05") == 0) {
+    if (!i4::tc_gemv_supported(a, &why)) return fail(INT4GEMV_ERR_INVALID, "tcgen05: %s", why);
+    return launched(name, i4::launch_tc_gemv(a, st));
+  }
+  if (std::strcmp(kernel, "mma_pipeline") == 0) {
+    if (!i4::mma_pipeline_supported(a, &why)) return fail(INT4GEMV_ERR_INVALID, "mma_pipeline: %s", why);
+    return launched(name, i4::launch_mma_pipeline(a, st));
+  }
+  if (std::strcmp(kernel, "vectorized") == 0) {
+    if (int e2 = check_16_byte_loads("vectorized", x, qweight, group_size)) return e2;
+    return launched(name, i4::launch_vectorized(a, 128, 2, st));
+  }
+  if (std::strcmp(kernel, "coalesced") == 0) return launched(name, i4::launch_coalesced(a, st));
+  if (std::strcmp(kernel, "naive") == 0) return launched(name, i4::launch_naive(a, st));
+  return fail(INT4GEMV_ERR_INVALID, "w4a16: unknown kernel '%s'", kernel);
 }
 
 int int4gemv_unpack(void* q, const void* qweight, int64_t n, int64_t k, void* stream) {

@@ -55,6 +55,9 @@ void check_inputs(const char* name, const at::Tensor& x, const at::Tensor& qweig
 at::Tensor w4a16(const at::Tensor& x, const at::Tensor& qweight, const at::Tensor& scales,
                  const at::Tensor& zeros, int64_t group_size);
 KernelInfo w4a16_info(int64_t m);
+// One named kernel ("tcgen05", "mma_pipeline", "vectorized", "coalesced", "naive"), for tests.
+at::Tensor w4a16_with(const at::Tensor& x, const at::Tensor& qweight, const at::Tensor& scales,
+                      const at::Tensor& zeros, int64_t group_size, const std::string& kernel);
 std::string w4a16_kernel(const at::Tensor& x, const at::Tensor& qweight, const at::Tensor& scales,
                          const at::Tensor& zeros, int64_t group_size);
 

@@ -40,10 +40,17 @@ cudaError_t simt_attrs(const char* kernel, int m, int threads_per_block, int row
 // Largest block the vectorized instance for (m, rows_per_warp) can launch with (registers).
 cudaError_t vectorized_max_threads(int m, int rows_per_warp, int* max_threads);
 
-// TMA-bulk-fed tensor-core pipeline (mma_pipeline.cu). `why` gets a reason when unsupported.
+// tcgen05 GEMV for M <= 8 (tc_gemv.cu): the fast path.
+bool tc_gemv_supported(const GemvArgs& a, const char** why);
+cudaError_t launch_tc_gemv(const GemvArgs& a, cudaStream_t stream);
+cudaError_t tc_gemv_attrs(int m, KernelAttrs* out);
+
+// TMA-bulk-fed mma.sync pipeline (mma_pipeline.cu). `why` gets a reason when unsupported.
 bool mma_pipeline_supported(const GemvArgs& a, const char** why);
 cudaError_t launch_mma_pipeline(const GemvArgs& a, cudaStream_t stream);
 cudaError_t mma_pipeline_attrs(int m, KernelAttrs* out);
+// Device address of the status word of the current device (cached per device), or null.
+int* device_status_word();
 // Reads and clears the device status word of the current device (synchronous).
 cudaError_t read_and_clear_status(int* status);
 

@@ -75,6 +75,8 @@ __device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, __half2 f) {
 
 __device__ __forceinline__ float h2f_bits(uint16_t b) { return __half2float(__ushort_as_half(b)); }
 
+constexpr int kStatusBadPlan = 3;
+
 // NT: n-tiles of 8 rows of x (M <= 8 NT). KSW: packed words per thread per k-step; 4 when
 // group % 128 == 0 (a thread reads 16 contiguous bytes per row), else 1 (group % 32 == 0).
 template <int NT, int KSW>
@@ -104,7 +106,8 @@ __global__ void __launch_bounds__(kThreads, 1) mma_pipeline_kernel(GemvArgs a, P
   const int row_begin = static_cast<int>(static_cast<int64_t>(cta) * a.n / p.ctas);
   const int row_end = static_cast<int>(static_cast<int64_t>(cta + 1) * a.n / p.ctas);
   const int rows = row_end - row_begin;
-  const int chunks = (rows + kMaxChunkRows - 1) / kMaxChunkRows;
+  // Chunks of at most p.rows_cap rows (the host sized the stage buffers for that many).
+  const int chunks = (rows + p.rows_cap - 1) / p.rows_cap;
   const int kwords = a.k / 8;
 
   if (warp == kConsumerWarps) {
@@ -116,6 +119,10 @@ __global__ void __launch_bounds__(kThreads, 1) mma_pipeline_kernel(GemvArgs a, P
       const int c0 = row_begin + static_cast<int>(static_cast<int64_t>(ci) * rows / chunks);
       const int c1 = row_begin + static_cast<int>(static_cast<int64_t>(ci + 1) * rows / chunks);
       const int crows = c1 - c0;
+      if (crows > p.rows_cap && ok) {  // never copy past a stage buffer
+        ok = false;
+        if (lane == 0) atomicExch(&g_status, kStatusBadPlan);
+      }
       for (int kbi = 0; kbi < p.num_kb; ++kbi, ++it) {
         const int slot = it % p.stages;
         const int use = it / p.stages;
@@ -177,22 +184,25 @@ __global__ void __launch_bounds__(kThreads, 1) mma_pipeline_kernel(GemvArgs a, P
       *reinterpret_cast<uint4*>(xperm + static_cast<int64_t>(b) * 8) = o;
     }
     named_barrier(kConsumerBarrier, kConsumerThreads);
-    // corr[m][grp] = (1024 * sum of B operands, sum of the x values they stand for).
-    const uint16_t* xp16 = reinterpret_cast<const uint16_t*>(xperm);
-    for (int idx = tid; idx < a.m * groups; idx += kConsumerThreads) {
+    // corr[m][grp] = (1024 * sum of B operands, sum of the x values they stand for): one warp
+    // per (row of x, group), lanes over 8-weight blocks, fixed shuffle tree (deterministic).
+    for (int idx = warp; idx < a.m * groups; idx += kConsumerWarps) {
       const int mrow = idx / groups;
       const int grp = idx % groups;
-      const uint16_t* blk = xp16 + static_cast<int64_t>(mrow) * a.k + grp * a.group;
+      const half* blk = xperm + static_cast<int64_t>(mrow) * a.k + grp * a.group;
       float bsum = 0.0f, xsum = 0.0f;
-      for (int j = 0; j < a.group; j += 8) {
-        const float b0 = h2f_bits(blk[j]), b1 = h2f_bits(blk[j + 1]);
-        const float b2 = h2f_bits(blk[j + 2]), b3 = h2f_bits(blk[j + 3]);
-        const float b4 = h2f_bits(blk[j + 4]), b5 = h2f_bits(blk[j + 5]);
-        const float b6 = h2f_bits(blk[j + 6]), b7 = h2f_bits(blk[j + 7]);
-        bsum += ((b0 + b1) + (b2 + b3)) + ((b4 + b5) + (b6 + b7));
-        xsum += ((b0 + b1) + 16.0f * (b2 + b3)) + ((b4 + b5) + 16.0f * (b6 + b7));
+      for (int j = lane; j < a.group / 8; j += kWarp) {
+        const uint4 v = *reinterpret_cast<const uint4*>(blk + 8 * j);
+        const float2 p0 = half2_bits_to_float2(v.x), p1 = half2_bits_to_float2(v.y);
+        const float2 p2 = half2_bits_to_float2(v.z), p3 = half2_bits_to_float2(v.w);
+        const float ones = (p0.x + p0.y) + (p2.x + p2.y);
+        const float sixteenths = (p1.x + p1.y) + (p3.x + p3.y);
+        bsum += ones + sixteenths;
+        xsum += ones + 16.0f * sixteenths;
       }
-      corr[idx] = make_float2(1024.0f * bsum, xsum);
+      bsum = warp_sum(bsum);
+      xsum = warp_sum(xsum);
+      if (lane == 0) corr[idx] = make_float2(1024.0f * bsum, xsum);
     }
     named_barrier(kConsumerBarrier, kConsumerThreads);
   }
@@ -204,6 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1) mma_pipeline_kernel(GemvArgs a, P
     const int c0 = row_begin + static_cast<int>(static_cast<int64_t>(ci) * rows / chunks);
     const int c1 = row_begin + static_cast<int>(static_cast<int64_t>(ci + 1) * rows / chunks);
     const int crows = c1 - c0;
+    if (crows > p.rows_cap) ok = false;  // the producer records the status
     const int tiles_used = (crows + 15) / 16;
     const int T = tiles_used <= 1 ? 1 : tiles_used <= 2 ? 2 : tiles_used <= 4 ? 4 : 8;
     const int tile = warp % T;
@@ -446,6 +457,18 @@ cudaError_t mma_pipeline_attrs(int m, KernelAttrs* out) {
     out->threads_per_block = kThreads;
     return cudaSuccess;
   });
+}
+
+int* device_status_word() {
+  static int* words[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  if (!words[dev & 63]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_status) != cudaSuccess) return nullptr;
+    words[dev & 63] = static_cast<int*>(p);
+  }
+  return words[dev & 63];
 }
 
 cudaError_t read_and_clear_status(int* status) {

@@ -62,6 +62,7 @@ vectorized = int4gemv_ops.vectorized
 load_only = int4gemv_ops.load_only
 w4a16 = int4gemv_ops.w4a16
 w4a16_kernel = int4gemv_ops.w4a16_kernel
+w4a16_with = int4gemv_ops.w4a16_with
 unpack = int4gemv_ops.unpack
 dequantize = int4gemv_ops.dequantize
 check_inputs = int4gemv_ops.check_inputs

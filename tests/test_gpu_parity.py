@@ -24,6 +24,7 @@ KERNELS = [
     ("vectorized", {"threads_per_block": 64, "rows_per_warp": 4}),
     ("w4a16", {}),
 ]
+FAST = ["tcgen05", "mma_pipeline"]
 
 
 def cuda(*arrays):
@@ -83,8 +84,8 @@ def test_full_size_w4a16(m, n, k):
     y = ops.w4a16(*args, 128)
     ref = oracle.reference(x, q, s, z, 128)
     assert_close(y, ref, f"w4a16 {m}x{n}x{k} ({ops.w4a16_kernel(*args, 128)})")
-    if m <= 8:
-        assert ops.w4a16_kernel(*args, 128) == "mma_pipeline"
+    if m <= 8 and 2 * m * k <= 128 * 1024:  # x must fit in shared memory for the tcgen05 path
+        assert ops.w4a16_kernel(*args, 128) == "tcgen05"
 
 
 @pytest.mark.parametrize("name,cfg", KERNELS[:3] + [("w4a16", {})])
@@ -110,6 +111,38 @@ def test_ragged_shapes(m, n, k, g):
     ref = oracle.reference(x, q, s, z, g)
     for name, cfg in KERNELS:
         assert_close(run(name, cfg, args, g), ref, f"{name}{cfg}")
+
+
+def fast_kernels_for(args, g):
+    """The fast kernels that accept this shape (the others raise a clear error)."""
+    out = []
+    for kern in FAST:
+        try:
+            y = ops.w4a16_with(*args, g, kern)
+            torch.cuda.synchronize()
+            out.append((kern, y))
+        except RuntimeError as e:
+            assert kern in str(e)
+    return out
+
+
+@pytest.mark.parametrize("m,n,k,g", ODD + [(m, n, k, 128) for m, n, k in FULL if m <= 8],
+                         ids=[f"m{m}_n{n}_k{k}_g{g}" for m, n, k, g in ODD] +
+                             [f"m{m}_n{n}_k{k}_g128" for m, n, k in FULL if m <= 8])
+def test_each_fast_kernel(m, n, k, g):
+    x, q, s, z = oracle.synthetic(m, n, k, g, seed=n + 3 * k + m)
+    args = cuda(x, q, s, z)
+    ref = oracle.reference(x, q, s, z, g)
+    for kern, y in fast_kernels_for(args, g):
+        assert_close(y, ref, f"{kern} {m}x{n}x{k} g{g}")
+
+
+def test_fast_kernel_coverage():
+    """tcgen05 takes every BASELINE M <= 8 shape; mma_pipeline takes group 32 / 64."""
+    x, q, s, z = cuda(*oracle.synthetic(1, 256, 8192, 128))
+    assert [k for k, _ in fast_kernels_for([x, q, s, z], 128)] == FAST
+    x, q, s, z = cuda(*oracle.synthetic(2, 256, 1024, 32))
+    assert [k for k, _ in fast_kernels_for([x, q, s, z], 32)] == ["mma_pipeline"]
 
 
 def test_group_sizes_without_fast_path():
