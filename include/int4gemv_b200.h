@@ -91,14 +91,15 @@ int int4gemv_w4a16(void* y, const void* x, const void* qweight, const void* scal
                    const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
                    void* workspace, int64_t workspace_bytes, void* stream);
 
-/* Name of the kernel int4gemv_w4a16 picks for this shape and these pointers ("mma_pipeline",
- * "vectorized", "naive"); for tests and the benchmark. Static storage. */
+/* Name of the kernel int4gemv_w4a16 picks for this shape and these pointers ("stream_mma",
+ * "mma_pipeline", "vectorized", "coalesced"); for tests and the benchmark. Static storage. */
 const char* int4gemv_w4a16_kernel_name(const void* x, const void* qweight, const void* scales,
                                        const void* zeros, int64_t m, int64_t n, int64_t k,
                                        int64_t group_size);
 
-/* Runs one named kernel instead of the automatic choice: "tcgen05", "mma_pipeline", "vectorized"
- * (128 threads, 2 rows per warp), "coalesced" or "naive". For tests and benchmarks. Fails with
+/* Runs one named kernel instead of the automatic choice: "stream_mma", "tcgen05", "mma_pipeline",
+ * "vectorized" (128 threads, 2 rows per warp), "coalesced" or "naive". For tests and benchmarks.
+ * Fails with
  * INT4GEMV_ERR_INVALID if that kernel does not support the shape or the pointers' alignment. */
 int int4gemv_w4a16_kernel(const char* kernel, void* y, const void* x, const void* qweight,
                           const void* scales, const void* zeros, int64_t m, int64_t n, int64_t k,

@@ -144,10 +144,10 @@ int empty_cases(const char* name, void* y, int64_t m, int64_t n, int64_t k, cuda
 
 int launched(const char* name, cudaError_t err) { return err == cudaSuccess ? ok() : cuda_fail(name, err); }
 
-enum class Pick { kTcgen05, kMmaPipeline, kVectorized, kCoalesced };
+enum class Pick { kStreamMma, kTcgen05, kMmaPipeline, kVectorized, kCoalesced };
 
 Pick pick_kernel(const i4::GemvArgs& a) {
-  if (i4::tc_gemv_supported(a, nullptr)) return Pick::kTcgen05;
+  if (i4::stream_mma_supported(a, nullptr)) return Pick::kStreamMma;
   if (i4::mma_pipeline_supported(a, nullptr)) return Pick::kMmaPipeline;
   if (a.group % 32 == 0 && reinterpret_cast<uintptr_t>(a.x) % 16 == 0 &&
       reinterpret_cast<uintptr_t>(a.q) % 16 == 0) {
@@ -252,8 +252,8 @@ int int4gemv_kernel_info(const char* kernel, int64_t m, int64_t threads_per_bloc
   } else if (std::strcmp(kernel, "naive") == 0 || std::strcmp(kernel, "coalesced") == 0) {
     err = i4::simt_attrs(kernel, static_cast<int>(m), 0, 1, &at);
   } else if (std::strcmp(kernel, "w4a16") == 0) {
-    err = m <= 8 ? i4::tc_gemv_attrs(static_cast<int>(m), &at)
-                 : i4::mma_pipeline_attrs(static_cast<int>(m <= 16 ? m : 16), &at);
+    err = m <= 32 ? i4::stream_mma_attrs(static_cast<int>(m), &at)
+                  : i4::mma_pipeline_attrs(16, &at);
   } else {
     return fail(INT4GEMV_ERR_INVALID, "kernel_info: unknown kernel '%s'", kernel);
   }
@@ -302,8 +302,10 @@ int int4gemv_w4a16(void* y, const void* x, const void* qweight, const void* scal
   if (done) return e;
   const i4::GemvArgs a = make_args(y, x, qweight, scales, zeros, m, n, k, group_size);
   switch (pick_kernel(a)) {
+    case Pick::kStreamMma:
+      return launched(name, i4::launch_stream_mma(a, st, false));
     case Pick::kTcgen05:
-      return launched(name, i4::launch_tc_gemv(a, st));
+      return launched(name, i4::launch_tc_gemv(a, st, false));
     case Pick::kMmaPipeline:
       return launched(name, i4::launch_mma_pipeline(a, st));
     case Pick::kVectorized:
@@ -322,6 +324,8 @@ const char* int4gemv_w4a16_kernel_name(const void* x, const void* qweight, const
   }
   const i4::GemvArgs a = make_args(nullptr, x, qweight, scales, zeros, m, n, k, group_size);
   switch (pick_kernel(a)) {
+    case Pick::kStreamMma:
+      return "stream_mma";
     case Pick::kTcgen05:
       return "tcgen05";
     case Pick::kMmaPipeline:
@@ -346,9 +350,13 @@ int int4gemv_w4a16_kernel(const char* kernel, void* y, const void* x, const void
   if (done) return e;
   const i4::GemvArgs a = make_args(y, x, qweight, scales, zeros, m, n, k, group_size);
   const char* why = "unsupported shape";
+  if (std::strcmp(kernel, "stream_mma") == 0) {
+    if (!i4::stream_mma_supported(a, &why)) return fail(INT4GEMV_ERR_INVALID, "stream_mma: %s", why);
+    return launched(name, i4::launch_stream_mma(a, st, false));
+  }
   if (std::strcmp(kernel, "tcgen05") == 0) {
     if (!i4::tc_gemv_supported(a, &why)) return fail(INT4GEMV_ERR_INVALID, "tcgen05: %s", why);
-    return launched(name, i4::launch_tc_gemv(a, st));
+    return launched(name, i4::launch_tc_gemv(a, st, false));
   }
   if (std::strcmp(kernel, "mma_pipeline") == 0) {
     if (!i4::mma_pipeline_supported(a, &why)) return fail(INT4GEMV_ERR_INVALID, "mma_pipeline: %s", why);

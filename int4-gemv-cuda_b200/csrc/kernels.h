@@ -40,10 +40,17 @@ cudaError_t simt_attrs(const char* kernel, int m, int threads_per_block, int row
 // Largest block the vectorized instance for (m, rows_per_warp) can launch with (registers).
 cudaError_t vectorized_max_threads(int m, int rows_per_warp, int* max_threads);
 
-// tcgen05 GEMV for M <= 8 (tc_gemv.cu): the fast path.
+// tcgen05 GEMV for M <= 8 (tc_gemv.cu). Launched with programmatic stream
+// serialization; strict = read the weights only after the previous kernel in the stream is done.
 bool tc_gemv_supported(const GemvArgs& a, const char** why);
-cudaError_t launch_tc_gemv(const GemvArgs& a, cudaStream_t stream);
+cudaError_t launch_tc_gemv(const GemvArgs& a, cudaStream_t stream, bool strict);
 cudaError_t tc_gemv_attrs(int m, KernelAttrs* out);
+
+// TMA-tile-fed mma.sync GEMV for M <= 32, group 128 (stream_mma.cu): the fast path. Launched
+// with programmatic stream serialization like launch_tc_gemv.
+bool stream_mma_supported(const GemvArgs& a, const char** why);
+cudaError_t launch_stream_mma(const GemvArgs& a, cudaStream_t stream, bool strict);
+cudaError_t stream_mma_attrs(int m, KernelAttrs* out);
 
 // TMA-bulk-fed mma.sync pipeline (mma_pipeline.cu). `why` gets a reason when unsupported.
 bool mma_pipeline_supported(const GemvArgs& a, const char** why);

@@ -1,64 +1,81 @@
-// The B200 fast path for M <= 8: a tcgen05 (5th-generation tensor core) W4A16 GEMV.
+// The B200 fast path for M <= 8: a TMA-fed tcgen05 (5th-generation tensor core) W4A16 GEMV.
 //
-// Mapping. One CTA per SM, two warpgroups. The CTA owns output rows [c N / P, (c + 1) N / P) (the
-// same number of weight bytes per SM, within a row). Its rows are cut into blocks of 32 and K into
-// S = 4 or 8 equal slices; a task is (block, four consecutive slices) and the warpgroups take the
-// tasks in turn. Inside a task one thread owns one (row, slice): TMEM lane 32 q + l is row l of the
-// block in slice 4 h + q, where q is the warp's quarter of the warpgroup. So every lane of the
-// 128-lane MMA does useful work even when a CTA owns only 28 or 56 rows.
+// Work split. Two CTAs per SM (grid = 2 x SMs). CTA c owns output rows [4 u0, 4 u1), an equal
+// share of 4-row units, so every CTA streams the same number of weight bytes to within 4 rows.
+// A CTA takes its rows in blocks of up to 32 and each row in stages of 8 items of 128 weights
+// (512 contiguous packed bytes).
 //
-// Per 128-weight step ("item") a thread
-//   1. has its 64 packed bytes (two 256-bit loads issued four items ahead, L1 bypassed) and its
-//      scale / zero,
-//   2. unpacks each 32-bit word with one shift and four LOP3s into fp16 1024 + q / 1024 + 16 q
-//      (exact) and stores the 64 fp16 pairs into its TMEM lane (the MMA's A operand),
-//   3. after a warpgroup barrier, one thread issues eight tcgen05.mma (M = 128, N = 16..64, K = 16,
-//      f16 x f16 -> f32) against x in shared memory (the B operand) and commits to an mbarrier,
-//   4. one item later the thread reads its accumulator column(s) back with tcgen05.ld and applies
-//      the group's scale and zero in fp32:
-//          sum_k (q_k - z) s x_k = s * (D - 1024 sum_k b_k - z sum_k x_k)
-//      (b_k are the B operands; both sums over x come from a per-CTA table).
-// The B operand holds, for every slice s and row m of x, the column n = s MT + m: x of that slice,
-// each 8-weight block permuted to [x0, x4, x1/16, x5/16, x2, x6, x3/16, x7/16] to match the unpacked
-// A operand, in the canonical no-swizzle K-major layout (8x16-byte core matrices). A lane of quarter
-// q reads only its own slice's column of D. The A and D buffers are double-buffered per warpgroup
-// in TMEM (the CTA allocates all 512 columns), so unpacking item i+1 overlaps the MMAs of item i.
+// Memory side. A producer warp streams every stage (rows x 512 bytes) with 2-D TMA tile copies
+// (cp.async.bulk.tensor, boxes of 32/16/8/4 rows x 128 bytes so a CTA never fetches rows it does
+// not own, completion counted in bytes on an mbarrier) into a ring of shared-memory buffers in the
+// 128-byte swizzled layout, so sixteen-byte loads by 32 threads of 32 different rows hit 32
+// different banks. (One 1-D bulk copy per row and stage, 512 bytes each, streams at less than half
+// the bandwidth of these tiles on B200.) The stage's scales and zeros (8 groups x rows) come in
+// the same way, as two more tiles per box.
 //
-// Partial sums per (row, slice) meet in shared memory and are added in a fixed order (so results
-// are deterministic) before the fp16 store. Every mbarrier wait is bounded; on timeout the kernel
-// records a status word, stops issuing work without leaving a barrier unmatched, and still frees
-// its TMEM.
+// Math side. One warpgroup (128 threads = the 128 lanes of TMEM). Thread l of warp q owns row l of
+// the block and every item i with i % 4 == q. Per item it unpacks the 16 packed words with one
+// shift and four LOP3s each into fp16 1024 + q / 1024 + 16 q (exact) and stores them into its TMEM
+// lane: the A operand of tcgen05.mma (M = 128, K = 16, f16 x f16 -> f32). Once all 128 lanes have
+// stored (a relaxed mbarrier arrival, so no thread waits for its own loads), one thread issues the
+// item's eight MMAs against x in shared memory (the B operand) and commits them to an mbarrier.
+// One item later each thread reads its accumulator back (tcgen05.ld) and applies the group's
+// scale and zero in fp32:
+//     sum_k (q_k - z) s x_k = s * (D - 1024 sum_k b_k - z sum_k x_k)
+// (b_k are the B operands; the two sums over x come from a per-CTA table). B holds one column per
+// (quarter q, row m of x): x of the items i = 4t + q, each 8-weight block permuted to
+// [x0, x4, x1/16, x5/16, x2, x6, x3/16, x7/16] to match the A operand, in the canonical no-swizzle
+// K-major layout (8x16-byte core matrices). A and D are double-buffered in TMEM (256 columns per
+// CTA, so two CTAs fit an SM), so unpacking one item overlaps the MMAs of the previous one.
+//
+// Launch overlap. The kernel is launched with programmatic stream serialization and triggers its
+// dependents early, so the next GEMV in the stream becomes resident while this one finishes and
+// starts streaming its weights. Everything that may have been produced by the previous kernel in
+// the stream (x) is read, and y is written, only after griddepcontrol.wait. Weights, scales and
+// zeros are read before it unless the caller asks for strict ordering.
+//
+// The four quarters' partial sums per row meet in shared memory and are added in a fixed order,
+// so results are deterministic. Every mbarrier wait is bounded; on timeout the kernel records a
+// status word, stops issuing work without leaving a barrier unmatched, and still frees its TMEM.
 #include <algorithm>
 #include <mutex>
 
-#include "common.cuh"
-#include "kernels.h"
+#include "weight_stream.cuh"
 
 namespace i4 {
-
 namespace {
 
-constexpr int kWarpgroups = 2;  // mbarriers: 4 per warpgroup in the first 64 bytes
-constexpr int kThreads = kWarpgroups * 128;
-constexpr int kTmemCols = 512;
-constexpr int kItemK = 128;        // weights per row per item (= one TMEM A buffer of 64 columns)
-constexpr int kPrefetch = 4;       // items of packed weights in flight per thread
+constexpr int kConsumerWarps = 4;  // one warpgroup: TMEM lanes 0..127
+constexpr int kThreads = (kConsumerWarps + 1) * kWarp;
+constexpr int kTmemCols = 256;
+constexpr int kMaxStages = 6;
+constexpr int kTwoPerSm = 113 * 1024;  // shared memory that still fits two CTAs per SM
 constexpr int kSmemLimit = 227 * 1024;
 constexpr int kStatusMmaTimeout = 4;
+constexpr int kStatusLoadTimeout = 5;
+constexpr int kConsumerBarrier = 1;
+
+// mbarrier slots (8 bytes each) at the start of shared memory
+constexpr int kBarFull = 0;                    // [kMaxStages] stage landed (bytes)
+constexpr int kBarEmpty = kMaxStages;          // [kMaxStages] stage consumed (4 warps)
+constexpr int kBarMma = 2 * kMaxStages;        // [2] MMAs of buffer b done (commit)
+constexpr int kBarA = 2 * kMaxStages + 2;      // [2] A operand of buffer b written (128 lanes)
+constexpr int kTmemSlot = 8 * (2 * kMaxStages + 4);
 
 struct TcPlan {
   int ctas;
-  int slices;       // S
-  int items_slice;  // items per slice = K / 128 / S
+  int units;        // 4-row units in N
   int nb;           // 8-column core-matrix groups in B
   int n_mma;        // MMA N
   uint32_t idesc;
   uint32_t lbo, sbo;  // B descriptor strides (bytes)
-  int rows_cap;     // max rows per CTA rounded up to 32
-  int group_shift;  // group_size = 128 << group_shift
-  int off_b, off_corr, off_red, smem_bytes;
-  int* status;      // device status word (int4gemv_device_status)
+  int rows_cap;     // max rows per CTA
+  int stages;
+  int off_b, off_corr, off_red, off_stage, smem_bytes;
+  int strict;       // 1: read weights only after griddepcontrol.wait
+  int* status;
 };
+
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t r;
@@ -73,15 +90,6 @@ __device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, __half2 f) {
   uint32_t r;
   memcpy(&r, &h, 4);
   return r;
-}
-
-// 32 bytes, read once: skip L1.
-__device__ __forceinline__ void ld_stream_v8(const void* p, uint32_t (&r)[8]) {
-  asm volatile(
-      "ld.global.nc.L1::no_allocate.v8.u32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7])
-      : "l"(p));
 }
 
 __device__ __forceinline__ void tc_fence_before() {
@@ -142,6 +150,11 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
       : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive_relaxed(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
 // Shared-memory matrix descriptor, no swizzle, K-major (sm_100 format, version 1).
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
   return static_cast<uint64_t>((addr >> 4) & 0x3FFF) |
@@ -150,57 +163,81 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
 }
 
 template <int MT>
-__global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(GemvArgs a, TcPlan p) {
+__global__ void __launch_bounds__(kThreads, 2)
+    tc_gemv_kernel(GemvArgs a, TcPlan p, const __grid_constant__ WeightMaps maps) {
   extern __shared__ __align__(1024) unsigned char smem[];
-  // [0, 64): mbarriers, per warpgroup 2 "MMAs done" and 2 "A operand written"; [64, 68): TMEM
-  // base address
-  uint64_t* mbar = reinterpret_cast<uint64_t*>(smem);
-  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(smem + 64);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kTmemSlot);
   unsigned char* bsm = smem + p.off_b;
   float2* corr = reinterpret_cast<float2*>(smem + p.off_corr);
   float* red = reinterpret_cast<float*>(smem + p.off_red);
+  unsigned char* stages = smem + p.off_stage;
 
   const int tid = threadIdx.x;
   const int warp = tid / kWarp;
   const int lane = tid % kWarp;
-  const int wg = warp / 4;
-  const int quarter = warp % 4;
-  const int groups = a.k / a.group;
   const int items_row = a.k / kItemK;
-  const int slice_k = a.k / p.slices;
+  const int steps = items_row / kItemsPerStage;  // stages per 32-row block
 
+  const int u0 = static_cast<int>(static_cast<int64_t>(blockIdx.x) * p.units / p.ctas);
+  const int u1 = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * p.units / p.ctas);
+  const int row_begin = 4 * u0;
+  const int rows = min(4 * u1, a.n) - row_begin;
+  const int blocks = (rows + kBlockRows - 1) / kBlockRows;
+
+  if (tid == kConsumerWarps * kWarp) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(&bars[kBarFull + s], 1);
+      mbar_init(&bars[kBarEmpty + s], kConsumerWarps);
+    }
+    mbar_init(&bars[kBarMma + 0], 1);
+    mbar_init(&bars[kBarMma + 1], 1);
+    mbar_init(&bars[kBarA + 0], 128);
+    mbar_init(&bars[kBarA + 1], 128);
+    fence_mbar_init();
+  }
   if (warp == 0) {
+    // TMEM before the dependents trigger: a next-kernel CTA must never hold TMEM this CTA needs.
     asm volatile(
         "tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-            smem_addr(tmem_base_slot)),
+            smem_addr(tmem_slot)),
         "r"(kTmemCols)
         : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  if (tid == 0) {
-    for (int w = 0; w < kWarpgroups; ++w) {
-      mbar_init(&mbar[4 * w + 0], 1);    // MMAs of buffer 0 done (tcgen05.commit)
-      mbar_init(&mbar[4 * w + 1], 1);    // MMAs of buffer 1 done
-      mbar_init(&mbar[4 * w + 2], 128);  // A operand of buffer 0 written by all 128 lanes
-      mbar_init(&mbar[4 * w + 3], 128);  // A operand of buffer 1 written
-    }
-    fence_mbar_init();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (tid == 0) launch_dependents();  // the next GEMV may become resident as SMs free up
+
+  if (warp == kConsumerWarps) {
+    // ---------------- producer warp ----------------
+    if (p.strict) grid_dependency_wait();
+    produce_weight_stages(maps, row_begin, rows, steps, steps, stages, p.stages, &bars[kBarFull],
+                          &bars[kBarEmpty], p.status);
+    return;
   }
 
-  // ---- B operand: x, permuted per 8-weight block, one column per (slice, row of x) -------------
+  // ---------------- consumer warpgroup ----------------
+  const int quarter = warp;  // TMEM lanes 32 q .. 32 q + 31
+  grid_dependency_wait();  // x may be the previous kernel's output
+
+  // B operand: for item-step t and quarter q, column n = q MT + m holds x[m] of item 4 t + q.
   {
     const __half2 sixteenth = __float2half2_rn(0.0625f);
     const int ncols = p.nb * 8;
-    const int kc_count = slice_k / 8;
-    for (int idx = tid; idx < kc_count * ncols; idx += kThreads) {
+    const int kc_count = (items_row / 4) * (kItemK / 8);
+    for (int idx = tid; idx < kc_count * ncols; idx += kConsumerWarps * kWarp) {
       const int kc = idx / ncols;
       const int n = idx % ncols;
-      const int s = n / MT;
+      const int q = n / MT;
       const int m = n % MT;
       uint4 o = make_uint4(0, 0, 0, 0);
-      if (s < p.slices && m < a.m) {
-        const uint4 v = *reinterpret_cast<const uint4*>(
-            a.x + static_cast<int64_t>(m) * a.k + s * slice_k + 8 * kc);
+      if (q < 4 && m < a.m) {
+        const int t = kc / (kItemK / 8);
+        const int k0 = (4 * t + q) * kItemK + 8 * (kc % (kItemK / 8));
+        const uint4 v =
+            *reinterpret_cast<const uint4*>(a.x + static_cast<int64_t>(m) * a.k + k0);
         o.x = prmt(v.x, v.z, 0x5410);
         o.y = hmul2_bits(prmt(v.x, v.z, 0x7632), sixteenth);
         o.z = prmt(v.y, v.w, 0x5410);
@@ -209,15 +246,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(GemvArgs a, TcPlan
       *reinterpret_cast<uint4*>(bsm + (kc * p.nb + n / 8) * 128 + 16 * (n % 8)) = o;
     }
   }
-  __syncthreads();
-  // corr[m][g] = (1024 * sum of B operands, sum of the x values they stand for), per 128 weights;
+  named_barrier(kConsumerBarrier, kConsumerWarps * kWarp);
+  // corr[m][i] = (1024 * sum of the B operands of item i, sum of the x values they stand for);
   // one warp per entry, fixed reduction order.
-  for (int idx = warp; idx < a.m * items_row; idx += kThreads / kWarp) {
+  for (int idx = warp; idx < a.m * items_row; idx += kConsumerWarps) {
     const int m = idx / items_row;
     const int item = idx % items_row;
-    const int s = item / p.items_slice;
-    const int kc0 = (item % p.items_slice) * (kItemK / 8);
-    const int n = s * MT + m;
+    const int kc0 = (item / 4) * (kItemK / 8);
+    const int n = (item % 4) * MT + m;
     float bsum = 0.0f, xsum = 0.0f;
     if (lane < kItemK / 8) {
       const uint4 v = *reinterpret_cast<const uint4*>(bsm + ((kc0 + lane) * p.nb + n / 8) * 128 +
@@ -235,143 +271,110 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(GemvArgs a, TcPlan
   }
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // B visible to the tensor core
   tc_fence_before();
-  __syncthreads();
+  named_barrier(kConsumerBarrier, kConsumerWarps * kWarp);
   tc_fence_after();
-  const uint32_t tmem = *tmem_base_slot;
+  const uint32_t tmem = *tmem_slot;
 
-  // ---- work list of this warpgroup ----------------------------------------------------------
-  const int row_begin = static_cast<int>(static_cast<int64_t>(blockIdx.x) * a.n / p.ctas);
-  const int row_end = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * a.n / p.ctas);
-  const int rows = row_end - row_begin;
-  const int blocks = (rows + 31) / 32;
-  const int quads = p.slices / 4;
-  const int tasks = blocks * quads;
-  const int my_tasks = tasks > wg ? (tasks - wg + kWarpgroups - 1) / kWarpgroups : 0;
-  const int items = my_tasks * p.items_slice;
+  bool ok = true;
 
   const uint32_t lane_addr = static_cast<uint32_t>(32 * quarter) << 16;
-  const uint32_t a_col0 = static_cast<uint32_t>(wg * 2) * (kItemK / 2);
-  const uint32_t d_col0 = 256u + static_cast<uint32_t>(wg * 2) * p.n_mma;
-  uint64_t* bar = mbar + 4 * wg;        // bar[buf]: MMAs done
-  uint64_t* a_ready = mbar + 4 * wg + 2;  // a_ready[buf]: A operand complete
   const uint32_t b_base = smem_addr(bsm);
-  const bool issuer = (tid % 128) == 0;
-  const int64_t row_bytes = a.k / 2;
-
-  // The warpgroup's items in order: task tl covers block (t / quads), slices (t % quads) * 4 + q
-  // with t = wg + tl * kWarpgroups; an item is one 128-weight step of the thread's slice. Cursors
-  // advance by one item without divisions (quads is 1 or 2).
-  const int quad_shift = quads == 2 ? 1 : 0;
-  const int gshift = p.group_shift;  // group = 128 << gshift
-  int ld_task = 0, ld_j = 0, ld_rl = 0, ld_sl = 0;
-  bool ld_valid = false;
-  const unsigned char* ld_src = nullptr;
-  const half* ld_s = nullptr;
-  const half* ld_z = nullptr;
-  auto start_task = [&](int tl) {
-    const int t = wg + tl * kWarpgroups;
-    const int blk = t >> quad_shift;
-    ld_sl = (t & (quads - 1)) * 4 + quarter;
-    ld_rl = 32 * blk + lane;
-    ld_valid = ld_rl < rows;
-    const int64_t row = row_begin + (ld_valid ? ld_rl : 0);
-    const int item0 = ld_sl * p.items_slice;
-    ld_src = reinterpret_cast<const unsigned char*>(a.q) + row * row_bytes + item0 * (kItemK / 2);
-    ld_s = a.s + row * groups + (item0 >> gshift);
-    ld_z = a.z + row * groups + (item0 >> gshift);
-  };
-  if (my_tasks > 0) start_task(0);
-
-  uint32_t qbuf[kPrefetch][16];
-  uint32_t szbuf[kPrefetch];  // scale bits | zero bits << 16
-  int meta_j[kPrefetch];      // item within the slice
-  int meta_sl[kPrefetch];     // slice
-  int meta_rl[kPrefetch];     // row within the CTA (or -1 for a lane past the last row)
-
-  // Loads the loader cursor's item into `slot`, then advances the cursor.
-  auto issue_load = [&](int slot) {
-    if (ld_task >= my_tasks) return;
-    if (ld_valid) {
-      uint32_t lo[8], hi[8];
-      ld_stream_v8(ld_src, lo);
-      ld_stream_v8(ld_src + 32, hi);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        qbuf[slot][j] = lo[j];
-        qbuf[slot][8 + j] = hi[j];
-      }
-      const int gi = ((ld_sl * p.items_slice + ld_j) >> gshift) -
-                     ((ld_sl * p.items_slice) >> gshift);
-      szbuf[slot] = static_cast<uint32_t>(__half_as_ushort(ld_s[gi])) |
-                    (static_cast<uint32_t>(__half_as_ushort(ld_z[gi])) << 16);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 16; ++j) qbuf[slot][j] = 0;
-      szbuf[slot] = 0;
-    }
-    meta_j[slot] = ld_j;
-    meta_sl[slot] = ld_sl;
-    meta_rl[slot] = ld_valid ? ld_rl : -1;
-    ld_src += kItemK / 2;
-    if (++ld_j == p.items_slice) {
-      ld_j = 0;
-      if (++ld_task < my_tasks) start_task(ld_task);
-    }
-  };
+  const bool issuer = tid == 0;
 
   float yacc[MT];
 #pragma unroll
   for (int m = 0; m < MT; ++m) yacc[m] = 0.0f;
-  bool ok = true;
 
-  // Epilogue of an item whose MMAs were committed to bar[buf] (use `use`): scale, zero,
-  // accumulate; park the partial sum at the end of a task.
-  auto epilogue = [&](int buf, int use, int j, int sl, int rl, uint32_t sz) {
-    if (ok && !mbar_wait_bounded(&bar[buf], use & 1)) {
+  // Epilogue of item-step `it` (buffer it & 1): scale, zero, accumulate; park at block end.
+  auto epilogue = [&](int it, int item, int row_local, bool valid, bool block_end, uint32_t sz) {
+    const int buf = it & 1;
+    if (ok && !mbar_wait_bounded(&bars[kBarMma + buf], (it >> 1) & 1)) {
       ok = false;
       atomicExch(p.status, kStatusMmaTimeout);
     }
     tc_fence_after();
     float d[MT];
-    tmem_ld<MT>(tmem + lane_addr + d_col0 + buf * p.n_mma + sl * MT, d);
+    tmem_ld<MT>(tmem + lane_addr + 128 + buf * p.n_mma + quarter * MT, d);
     const float sc = __half2float(__ushort_as_half(static_cast<uint16_t>(sz & 0xFFFF)));
     const float zp = __half2float(__ushort_as_half(static_cast<uint16_t>(sz >> 16)));
-    const int ir = sl * p.items_slice + j;
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
-      const float2 cr = corr[min(m, a.m - 1) * items_row + ir];
+      const float2 cr = corr[min(m, a.m - 1) * items_row + item];
       yacc[m] = fmaf(sc, fmaf(-zp, cr.y, d[m] - cr.x), yacc[m]);
     }
-    if (j == p.items_slice - 1) {
-      if (rl >= 0) {
+    if (block_end) {
+      if (valid) {
 #pragma unroll
-        for (int m = 0; m < MT; ++m) red[(sl * p.rows_cap + rl) * MT + m] = yacc[m];
+        for (int m = 0; m < MT; ++m) red[(quarter * p.rows_cap + row_local) * MT + m] = yacc[m];
       }
 #pragma unroll
       for (int m = 0; m < MT; ++m) yacc[m] = 0.0f;
     }
   };
 
-#pragma unroll
-  for (int i = 0; i < kPrefetch; ++i) issue_load(i);
-
+  int it = 0;  // item-steps issued by this CTA
+  int prev_item = 0, prev_row = 0;
+  bool prev_valid = false, prev_end = false;
   uint32_t prev_sz = 0;
-  int prev_j = 0, prev_sl = 0, prev_rl = -1;
-  for (int base = 0; base < items; base += kPrefetch) {
+  int sit = 0;  // stages consumed
+  for (int blk = 0; blk < blocks; ++blk) {
+    const int rows_b = min(kBlockRows, rows - blk * kBlockRows);
+    const int row_local = blk * kBlockRows + lane;
+    const bool valid = lane < rows_b;
+    for (int j = 0; j < steps; ++j, ++sit) {
+      const int slot = sit % p.stages;
+      if (ok && !mbar_wait_bounded(&bars[kBarFull + slot], (sit / p.stages) & 1)) {
+        ok = false;
+        atomicExch(p.status, kStatusLoadTimeout);
+      }
+      // This thread's two items of the stage: 4 t + quarter, t = 0, 1. Item i of the stage is
+      // 16-byte granules (i % 2) * 4 + c of column chunk i / 2; the swizzle XORs the granule with
+      // the row's index mod 8.
+      uint32_t qw[2][16];
+      const unsigned char* rowp = stages + slot * kStageBytes + lane * 128;
 #pragma unroll
-    for (int u = 0; u < kPrefetch; ++u) {
-      const int it = base + u;
-      if (it < items) {
+      for (int t = 0; t < 2; ++t) {
+        const int item_s = 4 * t + quarter;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int granule = ((item_s & 1) * 4 + c) ^ (lane & 7);
+          const uint4 v = *reinterpret_cast<const uint4*>(rowp + (item_s >> 1) * kChunkBytes +
+                                                          granule * 16);
+          qw[t][4 * c + 0] = v.x;
+          qw[t][4 * c + 1] = v.y;
+          qw[t][4 * c + 2] = v.z;
+          qw[t][4 * c + 3] = v.w;
+        }
+      }
+      // Scale and zero of the two items (row-major [row][8 groups] in the stage).
+      uint32_t szw[2];
+      {
+        const uint16_t* ss = reinterpret_cast<const uint16_t*>(stages + slot * kStageBytes +
+                                                               kStageQBytes) +
+                             lane * kItemsPerStage;
+        const uint16_t* zz = ss + kBlockRows * kItemsPerStage;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          szw[t] = static_cast<uint32_t>(ss[4 * t + quarter]) |
+                   (static_cast<uint32_t>(zz[4 * t + quarter]) << 16);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[kBarEmpty + slot]);  // stage may be refilled
+
+#pragma unroll
+      for (int t = 0; t < 2; ++t, ++it) {
         const int buf = it & 1;
-        // 2. unpack into this lane's TMEM row (A operand, 64 columns = 128 weights)
-        const uint32_t a_addr = tmem + lane_addr + a_col0 + buf * (kItemK / 2);
+        const int tstep = 2 * j + t;           // item-step within the row
+        const int item = 4 * tstep + quarter;  // this thread's item (= group)
+        const uint32_t a_addr = tmem + lane_addr + buf * (kItemK / 2);
 #pragma unroll
         for (int c4 = 0; c4 < 4; ++c4) {
           uint32_t v[16];
 #pragma unroll
           for (int w = 0; w < 4; ++w) {
             uint32_t h[4];
-            unpack_x16(qbuf[u][4 * c4 + w], h);
+            unpack_x16(qw[t][4 * c4 + w], h);
             v[4 * w + 0] = h[0];
             v[4 * w + 1] = h[1];
             v[4 * w + 2] = h[2];
@@ -379,51 +382,45 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(GemvArgs a, TcPlan
           }
           tmem_st16(a_addr + 16 * c4, v);
         }
-        const uint32_t sz = szbuf[u];
-        const int cur_j = meta_j[u], cur_sl = meta_sl[u], cur_rl = meta_rl[u];
-        issue_load(u);
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         tc_fence_before();
-        // Relaxed arrival: a bar.sync here would first wait for this thread's prefetch loads.
-        asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(
-                         smem_addr(&a_ready[buf]))
-                     : "memory");
-        // 3. one thread issues the item's 8 MMAs once all 128 lanes wrote their A rows
-        if (issuer && ok && !mbar_wait_bounded(&a_ready[buf], (it >> 1) & 1)) {
+        mbar_arrive_relaxed(&bars[kBarA + buf]);
+        if (issuer && ok && !mbar_wait_bounded(&bars[kBarA + buf], (it >> 1) & 1)) {
           ok = false;
           atomicExch(p.status, kStatusMmaTimeout);
         }
         if (issuer && ok) {
           tc_fence_after();
-          const uint32_t d_addr = tmem + d_col0 + buf * p.n_mma;
-          const uint32_t a_base = tmem + a_col0 + buf * (kItemK / 2);
-          const uint32_t b_item = b_base + cur_j * (kItemK / 8) * p.nb * 128;
+          const uint32_t d_addr = tmem + 128 + buf * p.n_mma;
+          const uint32_t a_base = tmem + buf * (kItemK / 2);
+          const uint32_t b_step = b_base + tstep * (kItemK / 8) * p.nb * 128;
 #pragma unroll
-          for (int j = 0; j < kItemK / 16; ++j) {
-            const uint64_t bdesc = smem_desc(b_item + 2 * j * p.nb * 128, p.lbo, p.sbo);
-            mma_f16(d_addr, a_base + 8 * j, bdesc, p.idesc, j > 0);
+          for (int kk = 0; kk < kItemK / 16; ++kk) {
+            const uint64_t bdesc = smem_desc(b_step + 2 * kk * p.nb * 128, p.lbo, p.sbo);
+            mma_f16(d_addr, a_base + 8 * kk, bdesc, p.idesc, kk > 0);
           }
-          mma_commit(&bar[buf]);
+          mma_commit(&bars[kBarMma + buf]);
         }
-        // 4. epilogue of the previous item (its MMAs had a whole item of time to finish)
-        if (it > 0) epilogue((it - 1) & 1, (it - 1) >> 1, prev_j, prev_sl, prev_rl, prev_sz);
-        prev_sz = sz;
-        prev_j = cur_j;
-        prev_sl = cur_sl;
-        prev_rl = cur_rl;
+        if (it > 0) epilogue(it - 1, prev_item, prev_row, prev_valid, prev_end, prev_sz);
+        prev_sz = szw[t];
+        prev_item = item;
+        prev_row = row_local;
+        prev_valid = valid;
+        prev_end = (j == steps - 1) && (t == 1);
       }
     }
   }
-  if (items > 0) epilogue((items - 1) & 1, (items - 1) >> 1, prev_j, prev_sl, prev_rl, prev_sz);
+  if (it > 0) epilogue(it - 1, prev_item, prev_row, prev_valid, prev_end, prev_sz);
 
-  // ---- add the slices of every (row, column of x) in a fixed order and store fp16 ---------------
+  // ---- add the four quarters of every (row, row of x) in a fixed order and store fp16 ---------
   tc_fence_before();
-  __syncthreads();
-  for (int o = tid; o < rows * a.m; o += kThreads) {
+  named_barrier(kConsumerBarrier, kConsumerWarps * kWarp);
+  for (int o = tid; o < rows * a.m; o += kConsumerWarps * kWarp) {
     const int r = o % rows;
     const int m = o / rows;
     float sum = 0.0f;
-    for (int s = 0; s < p.slices; ++s) sum += red[(s * p.rows_cap + r) * MT + m];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) sum += red[(q * p.rows_cap + r) * MT + m];
     if (ok) a.y[static_cast<int64_t>(m) * a.n + row_begin + r] = __float2half_rn(sum);
   }
   if (warp == 0) {
@@ -438,51 +435,56 @@ int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
 int tile_m(int m) { return m <= 1 ? 1 : m <= 2 ? 2 : m <= 4 ? 4 : 8; }
 
+bool plan_smem(const GemvArgs& a, TcPlan* p, int limit, int min_stages);
+
 bool make_plan(const GemvArgs& a, TcPlan* p, const char** why) {
   auto fail = [&](const char* reason) {
     if (why) *why = reason;
     return false;
   };
   if (a.m < 1 || a.m > 8) return fail("M must be in [1, 8]");
-  if (a.group % kItemK != 0) return fail("group_size must be a multiple of 128");
-  p->group_shift = 0;
-  while ((kItemK << p->group_shift) < a.group) ++p->group_shift;
-  if ((kItemK << p->group_shift) != a.group) return fail("group_size must be 128 times a power of 2");
-  if (reinterpret_cast<uintptr_t>(a.q) % 32 != 0) return fail("qweight must be 32-byte aligned");
-  if (reinterpret_cast<uintptr_t>(a.x) % 16 != 0) return fail("x must be 16-byte aligned");
-  const int items_row = a.k / kItemK;
+  if (a.group != kItemK) return fail("group_size must be 128");
+  if (a.k % (kItemK * kItemsPerStage) != 0) return fail("K must be a multiple of 1024");
+  if (reinterpret_cast<uintptr_t>(a.q) % 16 || reinterpret_cast<uintptr_t>(a.x) % 16 ||
+      reinterpret_cast<uintptr_t>(a.s) % 16 || reinterpret_cast<uintptr_t>(a.z) % 16)
+    return fail("x, qweight, scales and zeros must be 16-byte aligned");
   const int mt = tile_m(a.m);
-  int slices = 0;
-  for (int s : {8, 4}) {
-    if (items_row % s == 0 && s * mt <= 64) {
-      slices = s;
-      break;
-    }
-  }
-  if (!slices) return fail("K / 128 must be a multiple of 4");
-  p->slices = slices;
-  p->items_slice = items_row / slices;
-  p->nb = (slices * mt + 7) / 8;
-  p->n_mma = std::max(16, round_up(slices * mt, 16));
-  if (2 * kWarpgroups * p->n_mma + 2 * kWarpgroups * (kItemK / 2) > kTmemCols)
-    return fail("TMEM budget");
+  p->nb = (4 * mt + 7) / 8;
+  p->n_mma = std::max(16, round_up(4 * mt, 16));
+  if (128 + 2 * p->n_mma > kTmemCols) return fail("TMEM budget");
   p->lbo = static_cast<uint32_t>(p->nb * 128);
-  p->sbo = p->nb * 8 >= p->n_mma ? 128u : (p->nb == 1 ? 0u : 128u);
-  if (p->nb * 8 < p->n_mma && p->nb != 1) return fail("B column padding");
+  p->sbo = p->nb * 8 >= p->n_mma ? 128u : 0u;  // N = 16 over 8 stored columns: alias them
   p->idesc = (1u << 4) | (static_cast<uint32_t>(p->n_mma >> 3) << 17) | ((128u >> 4) << 24);
-  p->ctas = std::min(sm_count(), a.n);
-  const int rows_max = (a.n + p->ctas - 1) / p->ctas;
-  p->rows_cap = round_up(rows_max, 32);
-  const int64_t b_bytes = static_cast<int64_t>(a.k / slices / 8) * p->nb * 128;
-  p->off_b = 1024;
-  p->off_corr = static_cast<int>(round_up(static_cast<int>(std::min<int64_t>(b_bytes, kSmemLimit)) + p->off_b, 128));
-  p->off_red = round_up(p->off_corr + a.m * items_row * 8, 128);
-  const int64_t end = static_cast<int64_t>(p->off_red) +
-                      static_cast<int64_t>(slices) * p->rows_cap * mt * 4;
-  if (b_bytes > kSmemLimit || end > kSmemLimit) return fail("x does not fit in shared memory");
-  // At least half of the SM's shared memory, so two CTAs never share an SM (each takes all of
-  // TMEM).
-  p->smem_bytes = static_cast<int>(std::max<int64_t>(end, 120 * 1024));
+  p->units = (a.n + 3) / 4;
+  // Two CTAs per SM when x, the tables and >= 3 stages fit in half the shared memory.
+  p->ctas = std::min(2 * sm_count(), p->units);
+  p->rows_cap = 4 * ((p->units + p->ctas - 1) / p->ctas);
+  if (!plan_smem(a, p, kTwoPerSm, 3)) {
+    p->ctas = std::min(sm_count(), p->units);
+    p->rows_cap = 4 * ((p->units + p->ctas - 1) / p->ctas);
+    if (!plan_smem(a, p, kSmemLimit, 2)) return fail("x does not fit in shared memory");
+  }
+  p->strict = 0;
+  return true;
+}
+
+// Lays out shared memory for the plan; true if it fits `limit` with at least `min_stages` stages.
+bool plan_smem(const GemvArgs& a, TcPlan* p, int limit, int min_stages) {
+  const int mt = tile_m(a.m);
+  const int items_row = a.k / kItemK;
+  const int64_t b_bytes = static_cast<int64_t>(items_row / 4) * (kItemK / 8) * p->nb * 128;
+  int64_t off = 1024;
+  p->off_b = static_cast<int>(off);
+  off = (off + b_bytes + 127) / 128 * 128;
+  p->off_corr = static_cast<int>(off);
+  off = (off + static_cast<int64_t>(a.m) * items_row * 8 + 127) / 128 * 128;
+  p->off_red = static_cast<int>(off);
+  off = (off + static_cast<int64_t>(4) * p->rows_cap * mt * 4 + 1023) / 1024 * 1024;
+  p->off_stage = static_cast<int>(off);
+  const int64_t stages = std::min<int64_t>((limit - off) / kStageBytes, kMaxStages);
+  if (off > limit || stages < min_stages) return false;
+  p->stages = static_cast<int>(stages);
+  p->smem_bytes = static_cast<int>(off + stages * kStageBytes);
   return true;
 }
 
@@ -523,16 +525,29 @@ bool tc_gemv_supported(const GemvArgs& a, const char** why) {
   return make_plan(a, &p, why);
 }
 
-cudaError_t launch_tc_gemv(const GemvArgs& a, cudaStream_t stream) {
+cudaError_t launch_tc_gemv(const GemvArgs& a, cudaStream_t stream, bool strict) {
   TcPlan p;
   if (!make_plan(a, &p, nullptr)) return cudaErrorInvalidValue;
+  p.strict = strict ? 1 : 0;
   p.status = device_status_word();
   if (!p.status) return cudaErrorInvalidSymbol;
+  WeightMaps maps;
+  const cudaError_t merr = weight_maps_for(a, &maps);
+  if (merr != cudaSuccess) return merr;
   return with_mt(a.m, [&]<int MT>() {
     cudaError_t err = ensure_smem_attr<MT>();
     if (err != cudaSuccess) return err;
-    tc_gemv_kernel<MT><<<p.ctas, kThreads, p.smem_bytes, stream>>>(a, p);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.ctas);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = p.smem_bytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, tc_gemv_kernel<MT>, a, p, maps);
   });
 }
 
@@ -544,7 +559,7 @@ cudaError_t tc_gemv_attrs(int m, KernelAttrs* out) {
     out->registers = fa.numRegs;
     out->local_bytes = static_cast<int>(fa.localSizeBytes);
     out->max_threads_per_block = fa.maxThreadsPerBlock;
-    out->blocks_per_sm = 1;
+    out->blocks_per_sm = 2;  // when x, the tables and the stages fit in half the SM
     out->threads_per_block = kThreads;
     return cudaSuccess;
   });

@@ -32,7 +32,7 @@ def test_w4a16_through_c_abi(m, n, k):
     torch.cuda.synchronize()
     ok, msg = oracle.check_close(y.float().cpu().numpy(), oracle.reference(x, q, s, z))
     assert ok, msg
-    assert capi.w4a16_kernel_name(*ptrs(tx, tq, ts, tz), m, n, k, 128) in ("tcgen05", "mma_pipeline")
+    assert capi.w4a16_kernel_name(*ptrs(tx, tq, ts, tz), m, n, k, 128) == "stream_mma"
 
 
 def test_every_gemv_entry_point():

@@ -24,7 +24,7 @@ KERNELS = [
     ("vectorized", {"threads_per_block": 64, "rows_per_warp": 4}),
     ("w4a16", {}),
 ]
-FAST = ["tcgen05", "mma_pipeline"]
+FAST = ["stream_mma", "tcgen05", "mma_pipeline"]
 
 
 def cuda(*arrays):
@@ -84,8 +84,7 @@ def test_full_size_w4a16(m, n, k):
     y = ops.w4a16(*args, 128)
     ref = oracle.reference(x, q, s, z, 128)
     assert_close(y, ref, f"w4a16 {m}x{n}x{k} ({ops.w4a16_kernel(*args, 128)})")
-    if m <= 8 and 2 * m * k <= 128 * 1024:  # x must fit in shared memory for the tcgen05 path
-        assert ops.w4a16_kernel(*args, 128) == "tcgen05"
+    assert ops.w4a16_kernel(*args, 128) == "stream_mma"
 
 
 @pytest.mark.parametrize("name,cfg", KERNELS[:3] + [("w4a16", {})])
@@ -126,9 +125,9 @@ def fast_kernels_for(args, g):
     return out
 
 
-@pytest.mark.parametrize("m,n,k,g", ODD + [(m, n, k, 128) for m, n, k in FULL if m <= 8],
+@pytest.mark.parametrize("m,n,k,g", ODD + [(m, n, k, 128) for m, n, k in FULL],
                          ids=[f"m{m}_n{n}_k{k}_g{g}" for m, n, k, g in ODD] +
-                             [f"m{m}_n{n}_k{k}_g128" for m, n, k in FULL if m <= 8])
+                             [f"m{m}_n{n}_k{k}_g128" for m, n, k in FULL])
 def test_each_fast_kernel(m, n, k, g):
     x, q, s, z = oracle.synthetic(m, n, k, g, seed=n + 3 * k + m)
     args = cuda(x, q, s, z)
@@ -138,11 +137,57 @@ def test_each_fast_kernel(m, n, k, g):
 
 
 def test_fast_kernel_coverage():
-    """tcgen05 takes every BASELINE M <= 8 shape; mma_pipeline takes group 32 / 64."""
+    """stream_mma takes every BASELINE shape; mma_pipeline takes group 32 / 64."""
     x, q, s, z = cuda(*oracle.synthetic(1, 256, 8192, 128))
     assert [k for k, _ in fast_kernels_for([x, q, s, z], 128)] == FAST
     x, q, s, z = cuda(*oracle.synthetic(2, 256, 1024, 32))
     assert [k for k, _ in fast_kernels_for([x, q, s, z], 32)] == ["mma_pipeline"]
+
+
+# stream_mma edge cases: rows per CTA that leave a 16-row tile empty or partly filled, N not a
+# multiple of 4, every M tile count (1..4 tiles of 8 rows of x, partly filled), and K large
+# enough (for the M) that x is taken in several k-panels, including a shorter last panel.
+STREAM = [
+    (1, 1, 1024), (1, 5, 1024), (3, 33, 2048), (8, 17, 3072), (9, 100, 1024), (17, 301, 2048),
+    (24, 64, 1024), (31, 148 * 4 + 3, 1024), (32, 4099, 8192), (16, 8192, 14336),
+    (8, 1000, 28672), (1, 14336, 16384), (2, 4096, 32768), (5, 148 * 36 + 2, 5120),
+    (12, 777, 7168), (1, 148 * 28, 1024),
+]
+
+
+@pytest.mark.parametrize("m,n,k", STREAM, ids=[f"m{m}_n{n}_k{k}" for m, n, k in STREAM])
+def test_stream_mma_shapes(m, n, k):
+    x, q, s, z = oracle.synthetic(m, n, k, 128, seed=11 * m + n + k)
+    args = cuda(x, q, s, z)
+    assert ops.w4a16_kernel(*args, 128) == "stream_mma"
+    y = ops.w4a16_with(*args, 128, "stream_mma")
+    torch.cuda.synchronize()
+    assert_close(y, oracle.reference(x, q, s, z, 128), f"stream_mma {m}x{n}x{k}")
+
+
+def test_stream_mma_chained_calls():
+    """Back-to-back launches overlap (programmatic stream serialization): each GEMV reads the
+    previous one's output as x, so an early read of x or a late write of y shows up here. Every
+    layer is checked against the oracle run on that layer's actual input."""
+    n = 4096
+    rng = np.random.default_rng(3)
+    layers = [oracle.synthetic(1, n, n, 128, seed=100 + i)[1:] for i in range(6)]
+    dev_layers = [cuda(q, s, z) for q, s, z in layers]
+    for rep in range(3):
+        x0 = (rng.standard_normal((2, n)) * 0.5).astype(np.float16)
+        hs = [cuda(x0)[0]]
+        for q, s, z in dev_layers:
+            hs.append(ops.w4a16(hs[-1], q, s, z, 128))
+        torch.cuda.synchronize()
+        for i, (q, s, z) in enumerate(layers):
+            h_in = hs[i].cpu().numpy()
+            assert_close(hs[i + 1], oracle.reference(h_in, q, s, z, 128), f"rep {rep} layer {i}")
+    assert capi_status() == 0
+
+
+def capi_status():
+    from int4gemv import capi
+    return capi.device_status()
 
 
 def test_group_sizes_without_fast_path():
