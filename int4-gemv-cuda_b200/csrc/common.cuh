@@ -128,6 +128,13 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   return policy;
 }
 
+// L2 policy for data many CTAs read (x): keep it.
+__device__ __forceinline__ uint64_t l2_evict_last_policy() {
+  uint64_t policy;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(policy));
+  return policy;
+}
+
 // 1-D bulk copy global -> shared, completion counted in bytes on `bar`. dst, src and bytes must
 // be multiples of 16.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
@@ -159,14 +166,25 @@ __device__ __forceinline__ void named_barrier(int id, int threads) {
 
 // ---- Tensor core (warp-level) -------------------------------------------------------------------
 
-// D = A * B + C, m16n8k16, A row-major f16, B column-major f16, C / D f32.
+// D = A * B + C, m16n8k16, A row-major f16, B column-major f16, C / D f32. Not volatile: the
+// compiler may interleave independent MMAs (a dependent one waits ~21 cycles on B200).
 __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                           uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
       "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// D = A * B (C = 0): starts an accumulator without zeroing its registers first.
+__device__ __forceinline__ void mma_16816_first(float (&d)[4], const uint32_t (&a)[4],
+                                                uint32_t b0, uint32_t b1) {
+  asm(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%10, %10, %10, %10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.0f));
 }
 
 }  // namespace i4

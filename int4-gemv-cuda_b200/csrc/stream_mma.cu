@@ -2,37 +2,45 @@
 // MMAs (mma.sync m16n8k16, f16 x f16 -> f32) on the nibbles unpacked in registers.
 //
 // Why warp MMAs at small M. Per packed 32-bit word (8 weights) a thread spends one shift and four
-// LOP3s to turn the nibbles into the A fragments of two m16n8k16 MMAs (the magic-number trick:
-// 1024 + q and 1024 + 16 q in fp16, exact), and each MMA covers 256 weights x 8 rows of x. That
-// is about 6 warp instructions per 256 weights, flat in M up to 8 and + 2 MMAs per 8 more rows of
-// x, far below what streaming 4-bit weights at HBM speed leaves per SM. A 128-row tcgen05 MMA
-// has a fixed issue cost per 16 k that makes it the slower choice at M <= 32.
+// LOP3s to turn the nibbles into fp16 A-fragment registers (the magic-number trick: 1024 + q and
+// 1024 + 16 q, exact); one m16n8k16 MMA then covers 256 weights. A 128-row tcgen05 MMA has a
+// fixed issue cost per 16 k that makes it the slower choice at M <= 32 (measured).
 //
-// Work split. One CTA per SM (grid = SMs), with at most 113 KB of shared memory when it fits, so
-// the next GEMV in the stream (launched with programmatic stream serialization) becomes resident
-// beside it and starts streaming its own weights while this one drains. CTA c owns rows
-// [4 u0, 4 u1), an equal share of 4-row units. Its rows are taken in k-panels (all of K when x
-// fits) x blocks of 32 rows x stages of 8 items (an item = 128 weights = one group).
+// Work split. One CTA per SM (grid = SMs) using the SM's shared memory for a deep ring of stages.
+// CTA c owns rows [4 u0, 4 u1), an equal share of 4-row units. Its rows are taken in k-panels
+// (all of K when x fits) x blocks of 32 rows x stages of 8 items (an item = 128 weights = one
+// group). A producer warp fills the ring with 2-D TMA tiles (weight_stream.cuh) and, right after
+// the dependency on the previous kernel in the stream resolves, copies each panel of x into
+// shared memory with a bulk copy ahead of the remaining weight tiles, so x does not queue behind
+// them. Eight consumer warps split each stage.
 //
-// Warps. One producer warp (weight_stream.cuh) fills a ring of stages with 2-D TMA tiles. Eight
-// consumer warps split each stage: warp w takes rows 16 (w % 2) .. + 15 of the block and items
-// 2 (w / 2), 2 (w / 2) + 1. MMA row g (and g + 8) is block row rho(g) = (g >> 1) | ((g & 1) << 2)
-// (and + 8), so the 8 threads of one shared-memory phase read two rows whose 128-byte swizzle
-// puts their 16-byte granules in different banks.
+// Narrow path (M <= 4, MP = 2 or 4 rows of x per item in the 8 MMA columns). The eight MMA
+// columns hold 8 / MP different items x MP rows of x: both k-slot pairs of thread c (2c, 2c+1 and
+// 2c+8, 2c+9) take two adjacent words of one item, and its B values are non-zero only in that
+// item's columns. So an MMA still covers 256 weights, but scales are applied once per stage
+// instead of once per item. Warp w takes MMA rows 16 (w % 2) .. + 15 of the block and word
+// quarter q = w / 2 of every item (rotated by thread, below); the item's correction is applied by
+// the q = 0 warp.
 //
-// x. Per panel the consumers copy x into shared memory, each 8-weight block permuted to
-// [x0, x4, x1/16, x5/16, x2, x6, x3/16, x7/16] (matching the unpacked A halves) and laid out so
-// that the B fragment a thread needs for word j of an item is one 16-byte load, conflict-free:
-//     xs[m][item][j][c][8 halves], row stride = panel bytes + 64.
-// The same pass builds corr[item][m] = (1024 * sum of the B values, sum of the x they stand for),
-// so for each (row, item) the MMA result D gives
+// Wide path (5 <= M <= 32: MT = ceil(M / 8) tiles of 8 rows of x). Warp w takes rows 16 (w % 2)
+// .. + 15 and items 2 (w / 2), 2 (w / 2) + 1; each item's MMAs accumulate from zero, and its
+// scale and correction are applied per item.
+//
+// Both paths: MMA row g (and g + 8) is block row mma_row(g) (and + 8), and in the narrow path the
+// word quarter a thread reads is rotated by its k-slot group, so the sixteen-byte loads of one
+// shared-memory phase hit distinct banks under the 128-byte swizzle. Each panel of x is permuted
+// in shared memory, each 8-weight block to [x0, x4, x1/16, x5/16, x2, x6, x3/16, x7/16]
+// (matching the unpacked A halves), and laid out so that one 16-byte load gives a thread its B
+// register pairs for two MMAs; lanes whose B values are zero read a zeroed block instead. The
+// same pass builds corr[item][m] = (1024 * sum of the B values, sum of the x they stand for), so
+// for each (row, item)
 //     sum_k (q_k - z) s x_k = s * (D - 1024 sum_k b_k - z sum_k x_k).
 // The weights are bit-exact; the arithmetic is fp32 accumulation of exact fp16 products.
 //
-// Results. Each warp keeps per-row fp32 partials for its items; at the end of a block they go to
-// shared memory, and after the last block the four item-pair partials of each output are added
-// in a fixed order, so results are deterministic. Every mbarrier wait is bounded; on timeout the
-// kernel records a status word and runs to completion without writing y.
+// Results. Per-thread fp32 partials go to shared memory at the end of each block; after the last
+// block the partials of each output are added in a fixed order, so results are deterministic.
+// Every mbarrier wait is bounded; on timeout the kernel records a status word and runs to
+// completion without writing y.
 #include <algorithm>
 #include <mutex>
 
@@ -41,14 +49,19 @@
 namespace i4 {
 namespace {
 
-constexpr int kConsumerWarps = 8;
-constexpr int kConsumerThreads = kConsumerWarps * kWarp;
-constexpr int kThreads = kConsumerThreads + kWarp;
-constexpr int kMaxStages = 8;
-constexpr int kCoResident = 113 * 1024;  // leaves room for the next kernel's CTA on the SM
+constexpr int kMaxStages = 12;
 constexpr int kSmemLimit = 227 * 1024;
 constexpr int kConsumerBarrier = 1;
 constexpr int kMaxM = 32;
+constexpr int kNarrowItemBytes = 272;  // one item of one x row, narrow layout (256 + 16 pad)
+constexpr int kZeroBytes = 2048;       // zeroed block read by lanes whose B values are zero
+constexpr int kPreStages = 2;          // weight stages issued before the dependency wait
+
+// mbarriers at the start of shared memory
+constexpr int kBarFull = 0;                   // [kMaxStages] stage landed
+constexpr int kBarEmpty = kMaxStages;         // [kMaxStages] stage consumed (8 warps)
+constexpr int kBarXFull = 2 * kMaxStages;     // x panel landed
+constexpr int kBarXEmpty = 2 * kMaxStages + 1;  // x panel permuted: its raw buffer is free
 
 struct MmaPlan {
   int ctas;
@@ -56,10 +69,11 @@ struct MmaPlan {
   int rows_cap;     // rows of the largest CTA share
   int steps;        // stages per row: K / 1024
   int panel_steps;  // stages per k-panel
-  int xs_stride;    // bytes per row of x in the panel buffer
+  int xs_stride;    // bytes per row of x in the permuted panel buffer
   int mc;           // columns of the corr table: M rounded up to even
   int stages;
-  int off_xs, off_corr, off_red, off_stage, smem_bytes;
+  int pre_stages;   // weight stages the producer issues before the dependency wait
+  int off_xr, off_xs, off_corr, off_red, off_stage, smem_bytes;
   int strict;       // 1: read the weights only after griddepcontrol.wait
   int* status;
 };
@@ -86,50 +100,480 @@ __device__ __forceinline__ float half_hi(uint32_t v) {
   return __half2float(__ushort_as_half(static_cast<uint16_t>(v >> 16)));
 }
 
-// Copies x[:, k0 : k0 + pk] into the permuted panel layout and builds the corr table.
-__device__ __forceinline__ void load_x_panel(const GemvArgs& a, const MmaPlan& p, int k0, int pk,
-                                             unsigned char* xs, float2* corr, int tid) {
+__device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+// MMA row g -> block row: the two rows of one shared-memory phase (g = 2p, 2p + 1) differ in
+// bit 1, which the 128-byte swizzle turns into different banks.
+__device__ __forceinline__ int mma_row(int g) {
+  return (g & 4) | ((g & 1) << 1) | ((g >> 1) & 1);
+}
+
+// x0..x7 (one 8-weight block) -> the B halves matching unpack_x16: (x0, x4), (x1/16, x5/16),
+// (x2, x6), (x3/16, x7/16); adds the block's B values to bsum and the x they stand for to xsum.
+__device__ __forceinline__ uint4 permute_block(const uint4& v, float& bsum, float& xsum) {
   const __half2 sixteenth = __float2half2_rn(0.0625f);
-  const int blocks8 = pk / 8;         // 8-weight blocks per row of x in this panel
-  const int count = a.m * blocks8;    // a multiple of 16: sixteen lanes share one (m, item)
+  uint4 o;
+  o.x = prmt(v.x, v.z, 0x5410);
+  o.y = hmul2_bits(prmt(v.x, v.z, 0x7632), sixteenth);
+  o.z = prmt(v.y, v.w, 0x5410);
+  o.w = hmul2_bits(prmt(v.y, v.w, 0x7632), sixteenth);
+  const float ones = (half_lo(o.x) + half_hi(o.x)) + (half_lo(o.z) + half_hi(o.z));
+  const float sixteenths = (half_lo(o.y) + half_hi(o.y)) + (half_lo(o.w) + half_hi(o.w));
+  bsum += ones + sixteenths;
+  xsum += ones + 16.0f * sixteenths;
+  return o;
+}
+
+// Permutes the raw x panel xr[m][pk] (as landed) into the consumers' layout and builds the corr
+// table. Each thread takes two adjacent words (16 weights) of one row of x; eight threads cover
+// an item. Narrow layout: xs[m][item][word pair t][half h][word 2t + i][2 halves]: the 16 bytes
+// at (t, h) are the B registers (word 2t, word 2t+1) of MMAs 2h and 2h + 1. Wide layout:
+// xs[m][item][j][c][8 halves] for word 4 c + j, item stride 256.
+template <bool NARROW, int kConsumerThreads>
+__device__ __forceinline__ void permute_x_panel(const GemvArgs& a, const MmaPlan& p, int pk,
+                                                const unsigned char* xr, unsigned char* xs,
+                                                float2* corr, int tid) {
+  const int pairs = pk / 16;        // word pairs per row of x in this panel
+  const int count = a.m * pairs;    // a multiple of 8: eight lanes share one (m, item)
   for (int base = 0; base < count; base += kConsumerThreads) {
     const int idx = base + tid;
     const bool active = idx < count;
     float bsum = 0.0f, xsum = 0.0f;
-    int m = 0, b = 0;
+    int m = 0, v = 0;
     if (active) {
-      m = idx / blocks8;
-      b = idx - m * blocks8;
-      const uint4 v = *reinterpret_cast<const uint4*>(a.x + static_cast<int64_t>(m) * a.k + k0 + 8 * b);
-      uint4 o;
-      o.x = prmt(v.x, v.z, 0x5410);                          // x0, x4
-      o.y = hmul2_bits(prmt(v.x, v.z, 0x7632), sixteenth);   // x1/16, x5/16
-      o.z = prmt(v.y, v.w, 0x5410);                          // x2, x6
-      o.w = hmul2_bits(prmt(v.y, v.w, 0x7632), sixteenth);   // x3/16, x7/16
-      const int item = b >> 4, w = b & 15;
-      *reinterpret_cast<uint4*>(xs + m * p.xs_stride + item * 256 + ((w & 3) * 4 + (w >> 2)) * 16) = o;
-      const float ones = (half_lo(o.x) + half_hi(o.x)) + (half_lo(o.z) + half_hi(o.z));
-      const float sixteenths = (half_lo(o.y) + half_hi(o.y)) + (half_lo(o.w) + half_hi(o.w));
-      bsum = ones + sixteenths;
-      xsum = ones + 16.0f * sixteenths;
+      m = idx / pairs;
+      v = idx - m * pairs;
+      const uint4* src = reinterpret_cast<const uint4*>(xr + (static_cast<int64_t>(m) * pk + 16 * v) * 2);
+      const uint4 o0 = permute_block(src[0], bsum, xsum);
+      const uint4 o1 = permute_block(src[1], bsum, xsum);
+      const int item = v >> 3, t = v & 7;
+      unsigned char* row = xs + m * p.xs_stride;
+      if (NARROW) {
+        uint4* dst = reinterpret_cast<uint4*>(row + item * kNarrowItemBytes + t * 32);
+        dst[0] = make_uint4(o0.x, o1.x, o0.y, o1.y);
+        dst[1] = make_uint4(o0.z, o1.z, o0.w, o1.w);
+      } else {
+        const int w0 = 2 * t, w1 = 2 * t + 1;
+        *reinterpret_cast<uint4*>(row + item * 256 + ((w0 & 3) * 4 + (w0 >> 2)) * 16) = o0;
+        *reinterpret_cast<uint4*>(row + item * 256 + ((w1 & 3) * 4 + (w1 >> 2)) * 16) = o1;
+      }
     }
 #pragma unroll
-    for (int off = 1; off < 16; off <<= 1) {
+    for (int off = 1; off < 8; off <<= 1) {
       bsum += __shfl_xor_sync(0xffffffffu, bsum, off);
       xsum += __shfl_xor_sync(0xffffffffu, xsum, off);
     }
-    if (active && (b & 15) == 0) corr[(b >> 4) * p.mc + m] = make_float2(1024.0f * bsum, xsum);
+    if (active && (v & 7) == 0) corr[(v >> 3) * p.mc + m] = make_float2(1024.0f * bsum, xsum);
   }
 }
 
-// At M <= 8, two CTAs' worth of registers per SM: this kernel's and the next one's. Larger M
-// needs the registers for its extra accumulators.
+// The consumers' side of the stage ring (slot and phase kept incrementally: no division).
+struct StageRing {
+  uint64_t* full;
+  int stages;
+  int* status;
+  bool ok;
+  int slot;
+  uint32_t phase;
+  // Waits (bounded) for the next stage to land; returns its buffer index.
+  __device__ __forceinline__ int next() {
+    const int s = slot;
+    if (ok && !mbar_wait_bounded(&full[s], phase)) {
+      ok = false;
+      atomicExch(status, kStatusFullBarrierTimeout);
+    }
+    if (++slot == stages) {
+      slot = 0;
+      phase ^= 1u;
+    }
+    return s;
+  }
+};
+
+// ---- producer ----------------------------------------------------------------------------------
+__device__ __forceinline__ void issue_x_panel(const GemvArgs& a, int k0, int pk, unsigned char* xr,
+                                              uint64_t* xfull, uint64_t policy, int lane) {
+  if (lane == 0) mbar_arrive_expect_tx(xfull, static_cast<uint32_t>(a.m * pk * 2));
+  __syncwarp();
+  for (int m = lane; m < a.m; m += kWarp) {
+    bulk_g2s(xr + static_cast<int64_t>(m) * pk * 2, a.x + static_cast<int64_t>(m) * a.k + k0,
+             static_cast<uint32_t>(pk * 2), xfull, policy);
+  }
+}
+
+// Streams the CTA's weights (panel by panel, block by block, stage by stage) and, per panel, its
+// raw x. The first p.pre_stages weight stages go out before the dependency wait (unless strict);
+// x for panel 0 right after it, ahead of the remaining weight stages.
+__device__ __forceinline__ void produce(const GemvArgs& a, const MmaPlan& p, const WeightMaps& maps,
+                                        int row_begin, int rows, unsigned char* smem) {
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* full = bars + kBarFull;
+  uint64_t* empty = bars + kBarEmpty;
+  unsigned char* stages = smem + p.off_stage;
+  unsigned char* xr = smem + p.off_xr;
+  const int lane = threadIdx.x % kWarp;
+  const uint64_t wpolicy = l2_evict_first_policy();
+  const uint64_t xpolicy = l2_evict_last_policy();
+  const int blocks = (rows + kBlockRows - 1) / kBlockRows;
+  const int pre = p.strict ? 0 : p.pre_stages;  // < the stages of panel 0
+  if (p.strict) grid_dependency_wait();
+  bool x0_sent = false;
+  if (pre == 0) {
+    if (!p.strict) grid_dependency_wait();
+    issue_x_panel(a, 0, min(p.panel_steps, p.steps) * kItemsPerStage * kItemK, xr,
+                  &bars[kBarXFull], xpolicy, lane);
+    x0_sent = true;
+  }
+  bool ok = true;
+  int it = 0, slot = 0, use = 0;
+  for (int pi = 0, p0 = 0; p0 < p.steps; ++pi, p0 += p.panel_steps) {
+    const int p1 = min(p.steps, p0 + p.panel_steps);
+    if (pi > 0) {
+      if (ok && !mbar_wait_bounded(&bars[kBarXEmpty], (pi - 1) & 1)) {
+        ok = false;
+        if (lane == 0) atomicExch(p.status, kStatusEmptyBarrierTimeout);
+      }
+      if (ok) {
+        issue_x_panel(a, p0 * kItemsPerStage * kItemK, (p1 - p0) * kItemsPerStage * kItemK, xr,
+                      &bars[kBarXFull], xpolicy, lane);
+      }
+    }
+    for (int blk = 0; blk < blocks; ++blk) {
+      const int rows4 = (min(kBlockRows, rows - blk * kBlockRows) + 3) & ~3;
+      LaneBox b;
+      const bool has_box = lane_box(maps, lane, rows4, row_begin + blk * kBlockRows, &b);
+      for (int j = p0; j < p1; ++j, ++it) {
+        if (!x0_sent && it == pre) {
+          grid_dependency_wait();
+          issue_x_panel(a, 0, (p1 - p0) * kItemsPerStage * kItemK, xr, &bars[kBarXFull], xpolicy,
+                        lane);
+          x0_sent = true;
+        }
+        if (ok && use > 0 && !mbar_wait_bounded(&empty[slot], (use - 1) & 1)) {
+          ok = false;
+          if (lane == 0) atomicExch(p.status, kStatusEmptyBarrierTimeout);
+        }
+        if (ok) {
+          issue_stage(b, has_box, j, rows4, stages + slot * kStageBytes, &full[slot], wpolicy,
+                      lane);
+        }
+        if (++slot == p.stages) {
+          slot = 0;
+          ++use;
+        }
+      }
+    }
+  }
+  // Do not leave while copies into this CTA's shared memory may be in flight: the last weight
+  // stages and the last x panel.
+  if (ok) {
+    for (int back = 1; back <= min(it, p.stages); ++back) {
+      const int j = it - back;
+      if (!mbar_wait_bounded(&full[j % p.stages], (j / p.stages) & 1)) break;
+    }
+    const int panels = (p.steps + p.panel_steps - 1) / p.panel_steps;
+    mbar_wait_bounded(&bars[kBarXFull], (panels - 1) & 1);
+  }
+}
+
+// ---- narrow path ---------------------------------------------------------------------------------
+// MP = 2 or 4. A stage's work per 16-row tile is four rounds j = 0..3 over four word quarters. In
+// round j thread (g, c) processes words w and w + 1 (k-slot pairs 2c, 2c+1 and 2c+8, 2c+9) of one
+// item, rows r_lo and r_hi:
+//   MP = 2: item c + 4 (j / 2), w = 4 qc + 2 (j % 2); accumulator columns 2 c + m.
+//   MP = 4: item 4 (c / 2) + j, w = 4 qc + 2 (c % 2); accumulator columns 4 (c / 2) + m.
+// qc = (q + c / 2) % 4 is the thread's rotated word quarter. D sets (one accumulator set per
+// group of items): MP = 2: j / 2, MP = 4: j. With NR = 2 rounds per warp, warps w and w + 8 share
+// a (tile, quarter) and take rounds 0, 1 and 2, 3 (hs = w / 8). Every load offset below is a
+// per-thread base plus a compile-time constant.
+template <int MP, int NR>
+struct NarrowThread {
+  static constexpr int kSets = MP == 4 ? NR : NR / 2;  // D sets per warp and stage
+  int c, q, hs;
+  int r_lo, r_hi;
+  int item0;       // stage item of the thread's D set 0 (epilogue columns 2 c, 2 c + 1)
+  int a_base;      // stage offset of the A granule of (the first item, row r_lo)
+  int a_base_odd;  // MP 4: the same for the odd round (granule half flipped)
+  int b_base;      // x offset of the lane's B values in the stage's first item, or of the zeros
+  int b_step;      // x bytes per stage for lanes with B values, 0 for the others
+
+  __device__ __forceinline__ void init(int warp, int lane, int m_rows, int xs_stride,
+                                       int zero_rel) {
+    const int g = lane >> 2;
+    c = lane & 3;
+    q = (warp >> 1) & 3;
+    hs = NR == 4 ? 0 : warp >> 3;
+    const int qc = (q + (c >> 1)) & 3;
+    r_lo = 16 * (warp & 1) + mma_row(g);
+    r_hi = r_lo + 8;
+    const int r7 = r_lo & 7;
+    bool on;
+    if (MP == 4) {
+      // items 4 (c / 2) + NR hs + round
+      const int row_off = r_lo * 128 + 8 * (c & 1) + ((c >> 1) * 2 + (NR / 2) * hs) * kChunkBytes;
+      a_base = row_off + ((qc ^ r7) * 16);
+      a_base_odd = row_off + (((4 + qc) ^ r7) * 16);
+      const int m = g & 3;
+      on = (g >> 2) == (c >> 1) && m < m_rows;
+      item0 = 4 * (c >> 1) + NR * hs;
+      b_base = m * xs_stride + (4 * (c >> 1) + NR * hs) * kNarrowItemBytes +
+               (2 * qc + (c & 1)) * 32;
+    } else {
+      // items c + 4 (hs + round / 2)
+      a_base = ((c >> 1) + 2 * hs) * kChunkBytes + r_lo * 128 + ((((c & 1) * 4 + qc) ^ r7) * 16);
+      a_base_odd = 0;
+      const int m = g & 1;
+      on = (g >> 1) == c && m < m_rows;
+      item0 = c + 4 * hs;
+      b_base = m * xs_stride + (c + 4 * hs) * kNarrowItemBytes + 2 * qc * 32;
+    }
+    if (!on) b_base = zero_rel;
+    b_step = on ? kItemsPerStage * kNarrowItemBytes : 0;
+  }
+  // Stage offset of A load i (MP 2: item sel i; MP 4: round i) of row h.
+  __device__ __forceinline__ int a_off(int i, int h) const {
+    if (MP == 4) return ((i & 1) ? a_base_odd : a_base) + (i >> 1) * kChunkBytes + h * 1024;
+    return a_base + i * 2 * kChunkBytes + h * 1024;
+  }
+  // Offset of the B loads of round j (half h: MMAs 2h, 2h + 1) from the lane's stage base.
+  __device__ __forceinline__ static constexpr int b_off(int j, int h) {
+    return MP == 2 ? (j >> 1) * 4 * kNarrowItemBytes + (j & 1) * 32 + 16 * h
+                   : j * kNarrowItemBytes + 16 * h;
+  }
+  __device__ __forceinline__ int col_m(int e) const { return (2 * c + e) % MP; }
+  // Stage item of the thread's accumulator columns in D set `set`.
+  __device__ __forceinline__ int col_item(int set) const {
+    return MP == 2 ? item0 + 4 * set : item0 + set;
+  }
+};
+
+// Raw fp16 scale (or zero) bits of the thread's epilogue items (col_item(set)) for one row of a
+// landed stage.
+template <int MP, int NR>
+struct SzBits {
+  static constexpr int kSets = NarrowThread<MP, NR>::kSets;
+  uint32_t w[2];
+  __device__ __forceinline__ void load(const unsigned char* row_base, int item0) {
+    if (MP == 2) {
+#pragma unroll
+      for (int s = 0; s < kSets; ++s) {
+        w[s] = *reinterpret_cast<const uint16_t*>(row_base + 2 * (item0 + 4 * s));
+      }
+    } else if (kSets == 2) {
+      w[0] = *reinterpret_cast<const uint32_t*>(row_base + 2 * item0);
+    } else {
+      const uint2 v = *reinterpret_cast<const uint2*>(row_base + 2 * item0);
+      w[0] = v.x;
+      w[1] = v.y;
+    }
+  }
+  __device__ __forceinline__ float get(int set) const {
+    if (MP == 2) return half_lo(w[set]);
+    return (set & 1) ? half_hi(w[set >> 1]) : half_lo(w[set >> 1]);
+  }
+};
+
+// One stage of one warp: load the A words, scales and zeros, release the stage, then 4 NR MMAs and
+// the epilogue into acc[row lo / hi][e].
+template <int MP, int NR>
+__device__ __forceinline__ void narrow_stage(const NarrowThread<MP, NR>& t,
+                                             const unsigned char* st, const unsigned char* xb,
+                                             const float2* corr_stage, int mc, int m_rows,
+                                             float (&acc)[2][2], uint64_t* empty_bar, int lane) {
+  constexpr int kSets = NarrowThread<MP, NR>::kSets;
+  uint4 wa[2][2];  // MP 2: [item sel][row] = the 4 words of the granule
+  uint2 wb[4][2];  // MP 4: [round][row] = words w, w + 1
+  if (MP == 4) {
+#pragma unroll
+    for (int j = 0; j < NR; ++j)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) wb[j][h] = *reinterpret_cast<const uint2*>(st + t.a_off(j, h));
+  } else {
+#pragma unroll
+    for (int i = 0; i < NR / 2; ++i)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) wa[i][h] = *reinterpret_cast<const uint4*>(st + t.a_off(i, h));
+  }
+  SzBits<MP, NR> sb[2], zb[2];  // [row]
+  const unsigned char* sp = st + kStageQBytes;
+  const unsigned char* zp = sp + kBlockRows * kSzRowBytes;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int row = h ? t.r_hi : t.r_lo;
+    sb[h].load(sp + row * kSzRowBytes, t.item0);
+    if (t.q == 0) zb[h].load(zp + row * kSzRowBytes, t.item0);
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(empty_bar);  // the stage may be refilled
+
+  // Accumulators: MP 2: [set][hh]; MP 4: [set][hh % 2]. Consecutive MMAs in program order never
+  // share an accumulator; the first MMA into each starts it (C = 0).
+  constexpr int kAcc = MP == 4 ? 2 : 4;
+  float d[kSets][kAcc][4];
+#pragma unroll
+  for (int j = 0; j < NR; ++j) {
+    uint32_t w0r0, w0r1, w1r0, w1r1;  // words w, w + 1 of rows r_lo, r_hi
+    if (MP == 2) {
+      const int w = 2 * (j & 1);
+      w0r0 = word_of(wa[j >> 1][0], w);
+      w0r1 = word_of(wa[j >> 1][1], w);
+      w1r0 = word_of(wa[j >> 1][0], w + 1);
+      w1r1 = word_of(wa[j >> 1][1], w + 1);
+    } else {
+      w0r0 = wb[j][0].x;
+      w0r1 = wb[j][1].x;
+      w1r0 = wb[j][0].y;
+      w1r1 = wb[j][1].y;
+    }
+    uint32_t u00[4], u01[4], u10[4], u11[4];
+    unpack_x16(w0r0, u00);
+    unpack_x16(w0r1, u01);
+    unpack_x16(w1r0, u10);
+    unpack_x16(w1r1, u11);
+    const uint4 bx0 = *reinterpret_cast<const uint4*>(xb + NarrowThread<MP, NR>::b_off(j, 0));
+    const uint4 bx1 = *reinterpret_cast<const uint4*>(xb + NarrowThread<MP, NR>::b_off(j, 1));
+    const int set = MP == 2 ? (j >> 1) : j;
+#pragma unroll
+    for (int hh = 0; hh < 4; ++hh) {
+      const uint32_t afr[4] = {u00[hh], u01[hh], u10[hh], u11[hh]};
+      const uint4& bx = hh < 2 ? bx0 : bx1;
+      const uint32_t b0 = (hh & 1) ? bx.z : bx.x;
+      const uint32_t b1 = (hh & 1) ? bx.w : bx.y;
+      const bool first = MP == 2 ? (j & 1) == 0 : hh < 2;
+      if (first) {
+        mma_16816_first(d[set][hh % kAcc], afr, b0, b1);
+      } else {
+        mma_16816(d[set][hh % kAcc], afr, b0, b1);
+      }
+    }
+  }
+#pragma unroll
+  for (int set = 0; set < kSets; ++set) {
+    float dsum[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float v = d[set][0][e];
+#pragma unroll
+      for (int i = 1; i < kAcc; ++i) v += d[set][i][e];
+      dsum[e] = v;
+    }
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int m = t.col_m(e);
+      if (m >= m_rows) continue;
+      float2 cr = make_float2(0.0f, 0.0f);
+      if (t.q == 0) cr = corr_stage[t.col_item(set) * mc + m];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float z = t.q == 0 ? zb[h].get(set) : 0.0f;
+        const float v = dsum[2 * h + e] - fmaf(z, cr.y, cr.x);
+        acc[h][e] = fmaf(sb[h].get(set), v, acc[h][e]);
+      }
+    }
+  }
+}
+
+// ---- wide path: one stage of one warp -----------------------------------------------------------
+// The warp takes NI items (item0, item0 + 1, ...) of its 16-row tile.
+template <int MT, int NI>
+__device__ __forceinline__ void wide_stage(const unsigned char* st, const unsigned char* xs,
+                                           const float2* corr, int xs_stride, int mc, int m_rows,
+                                           int j_panel, int item0, int g, int c, int r_lo,
+                                           int r_hi, float (&acc)[2][MT][2], uint64_t* empty_bar,
+                                           int lane) {
+  uint4 aw[NI][2];
+  uint32_t sz[NI][2];  // scale bits | zero bits << 16 of item item0 + ii, rows r_lo and r_hi
+#pragma unroll
+  for (int ii = 0; ii < NI; ++ii) {
+    aw[ii][0] = stage_words(st, r_lo, item0 + ii, c);
+    aw[ii][1] = stage_words(st, r_hi, item0 + ii, c);
+    sz[ii][0] = stage_sz(st, r_lo, item0 + ii);
+    sz[ii][1] = stage_sz(st, r_hi, item0 + ii);
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(empty_bar);  // the stage may be refilled
+
+#pragma unroll(MT == 1 ? NI : 1)
+  for (int ii = 0; ii < NI; ++ii) {
+    const int item_p = j_panel * kItemsPerStage + item0 + ii;  // item within the panel
+    // [tile][jw % 2][a0 / a1]: consecutive MMAs never share an accumulator.
+    float d[MT][2][2][4];
+    // Selects rather than indexing, so a rolled loop keeps aw in registers.
+    const uint4 al = ii == 0 ? aw[0][0] : aw[NI - 1][0];
+    const uint4 ah = ii == 0 ? aw[0][1] : aw[NI - 1][1];
+#pragma unroll
+    for (int jw = 0; jw < 4; ++jw) {
+      uint32_t hl[4], hh[4];
+      unpack_x16(word_of(al, jw), hl);
+      unpack_x16(word_of(ah, jw), hh);
+      const uint32_t a0[4] = {hl[0], hh[0], hl[1], hh[1]};
+      const uint32_t a1[4] = {hl[2], hh[2], hl[3], hh[3]};
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        const int m = g + 8 * mt;
+        uint4 xb = make_uint4(0, 0, 0, 0);
+        if (m < m_rows) {
+          xb = *reinterpret_cast<const uint4*>(xs + m * xs_stride + item_p * 256 +
+                                               (jw * 4 + c) * 16);
+        }
+        if (jw < 2) {
+          mma_16816_first(d[mt][jw & 1][0], a0, xb.x, xb.y);
+          mma_16816_first(d[mt][jw & 1][1], a1, xb.z, xb.w);
+        } else {
+          mma_16816(d[mt][jw & 1][0], a0, xb.x, xb.y);
+          mma_16816(d[mt][jw & 1][1], a1, xb.z, xb.w);
+        }
+      }
+    }
+    const uint32_t szl = ii == 0 ? sz[0][0] : sz[NI - 1][0];
+    const uint32_t szh = ii == 0 ? sz[0][1] : sz[NI - 1][1];
+    const float s_lo = half_lo(szl), z_lo = half_hi(szl);
+    const float s_hi = half_lo(szh), z_hi = half_hi(szh);
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      const int m0 = 8 * mt + 2 * c;
+      const float4 cr =
+          *reinterpret_cast<const float4*>(corr + item_p * mc + (m0 < m_rows ? m0 : 0));
+      float dd[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        dd[e] = (d[mt][0][0][e] + d[mt][0][1][e]) + (d[mt][1][0][e] + d[mt][1][1][e]);
+      }
+      acc[0][mt][0] = fmaf(s_lo, fmaf(-z_lo, cr.y, dd[0] - cr.x), acc[0][mt][0]);
+      acc[0][mt][1] = fmaf(s_lo, fmaf(-z_lo, cr.w, dd[1] - cr.z), acc[0][mt][1]);
+      acc[1][mt][0] = fmaf(s_hi, fmaf(-z_hi, cr.y, dd[2] - cr.x), acc[1][mt][0]);
+      acc[1][mt][1] = fmaf(s_hi, fmaf(-z_hi, cr.w, dd[3] - cr.z), acc[1][mt][1]);
+    }
+  }
+}
+
+// Consumer warps per CTA: 16 when M <= 8 (at most 96 registers: 17 warps, at most 5 per SM
+// sub-partition, fit its 16384 registers), else 8 (168 registers: 3 warps per sub-partition).
 template <int MT>
-__global__ void __launch_bounds__(kThreads, MT == 1 ? 2 : 1)
+__host__ __device__ constexpr int consumer_warps() {
+  return MT == 1 ? 16 : 8;
+}
+
+// MP: M rounded up to 2 or 4 (narrow path) or 8 (wide path, MT tiles of 8 rows of x).
+template <int MP, int MT>
+__global__ void __maxnreg__(MT == 1 ? 96 : 168)
     stream_mma_kernel(GemvArgs a, MmaPlan p, const __grid_constant__ WeightMaps maps) {
+  constexpr bool kNarrow = MP < 8;
+  constexpr int kCW = consumer_warps<MT>();
+  constexpr int kConsumerThreads = kCW * kWarp;
+  constexpr int kThreads = kConsumerThreads + kWarp;
+  constexpr int kSplit = kCW / 8;      // warps sharing one (tile, word quarter or item pair)
+  constexpr int kNR = 4 / kSplit;      // narrow: rounds per warp and stage
+  constexpr int kNI = 2 / kSplit;      // wide: items per warp and stage
+  constexpr int kRedCols = 8;          // narrow path: accumulator columns per row
   extern __shared__ __align__(1024) unsigned char smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty = full + kMaxStages;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* full = bars + kBarFull;
+  uint64_t* empty = bars + kBarEmpty;
+  unsigned char* zero = smem + 1024;
+  const unsigned char* xr = smem + p.off_xr;
   unsigned char* xs = smem + p.off_xs;
   float2* corr = reinterpret_cast<float2*>(smem + p.off_corr);
   float* red = reinterpret_cast<float*>(smem + p.off_red);
@@ -148,137 +592,102 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? 2 : 1)
   if (tid == kConsumerThreads) {
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumerWarps);
+      mbar_init(&empty[s], kCW);
     }
+    mbar_init(&bars[kBarXFull], 1);
+    mbar_init(&bars[kBarXEmpty], 1);
     fence_mbar_init();
   }
+  for (int i = tid; i < kZeroBytes / 16; i += kThreads) {
+    reinterpret_cast<uint4*>(zero)[i] = make_uint4(0, 0, 0, 0);
+  }
   __syncthreads();
-  if (tid == 0) launch_dependents();  // the next GEMV may become resident beside this CTA
+  if (tid == 0) launch_dependents();  // the next GEMV may launch as SMs free up
 
-  if (warp == kConsumerWarps) {
-    if (p.strict) grid_dependency_wait();
-    produce_weight_stages(maps, row_begin, rows, p.steps, p.panel_steps, stages, p.stages, full,
-                          empty, p.status);
+  if (warp == kCW) {
+    produce(a, p, maps, row_begin, rows, smem);
     return;
   }
 
   // ---------------- consumers ----------------
-  const int g = lane >> 2;
-  const int c = lane & 3;
   const int tile = warp & 1;
-  const int pair = warp >> 1;
-  const int r_lo = 16 * tile + ((g >> 1) | ((g & 1) << 2));  // block rows of MMA rows g, g + 8
+  const int g = lane >> 2, c = lane & 3;
+  const int group = (warp >> 1) & 3;  // word quarter (narrow) or item pair (wide)
+  const int hs = warp >> 3;           // which half of the group's work, when split
+  const int src = hs * 4 + group;     // partial-sum source of this warp
+  const int r_lo = 16 * tile + mma_row(g);
   const int r_hi = r_lo + 8;
-  grid_dependency_wait();  // x may be the previous kernel's output; y is written below
+  NarrowThread<kNarrow ? MP : 2, kNR> nt;
+  if constexpr (kNarrow) nt.init(warp, lane, a.m, p.xs_stride, static_cast<int>(zero - xs));
 
-  bool ok = true;
-  int sit = 0;  // stages consumed
-  for (int p0 = 0; p0 < p.steps; p0 += p.panel_steps) {
+  StageRing in{full, p.stages, p.status, true, 0, 0u};
+  for (int pi = 0, p0 = 0; p0 < p.steps; ++pi, p0 += p.panel_steps) {
     const int psteps = min(p.panel_steps, p.steps - p0);
-    if (p0 > 0) named_barrier(kConsumerBarrier, kConsumerThreads);  // done with the last panel
-    load_x_panel(a, p, p0 * kItemsPerStage * kItemK, psteps * kItemsPerStage * kItemK, xs, corr,
-                 tid);
+    if (pi > 0) named_barrier(kConsumerBarrier, kConsumerThreads);  // done with the last panel
+    if (in.ok && !mbar_wait_bounded(&bars[kBarXFull], pi & 1)) {
+      in.ok = false;
+      atomicExch(p.status, kStatusFullBarrierTimeout);
+    }
+    permute_x_panel<kNarrow, kConsumerThreads>(a, p, psteps * kItemsPerStage * kItemK, xr, xs,
+                                               corr, tid);
     named_barrier(kConsumerBarrier, kConsumerThreads);
+    if (tid == 0) mbar_arrive(&bars[kBarXEmpty]);  // the raw x buffer may be refilled
 
     for (int blk = 0; blk < blocks; ++blk) {
       const int rows_b = min(kBlockRows, rows - blk * kBlockRows);
       const bool active = 16 * tile < rows_b;
-      float acc[2][MT][2];
-#pragma unroll
-      for (int h = 0; h < 2; ++h)
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) acc[h][mt][0] = acc[h][mt][1] = 0.0f;
-
-      for (int j = 0; j < psteps; ++j, ++sit) {
-        const int slot = sit % p.stages;
-        if (ok && !mbar_wait_bounded(&full[slot], (sit / p.stages) & 1)) {
-          ok = false;
-          atomicExch(p.status, kStatusFullBarrierTimeout);
+      if constexpr (kNarrow) {
+        float acc[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
+        for (int j = 0; j < psteps; ++j) {
+          const int slot = in.next();
+          if (!active) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            continue;
+          }
+          narrow_stage<MP, kNR>(nt, stages + slot * kStageBytes, xs + nt.b_base + j * nt.b_step,
+                                corr + j * kItemsPerStage * p.mc, p.mc, a.m, acc, &empty[slot],
+                                lane);
         }
-        const unsigned char* st = stages + slot * kStageBytes;
-        uint4 aw[2][2];
-        uint32_t s2[2], z2[2];  // scales / zeros of the warp's two items, rows r_lo and r_hi
         if (active) {
 #pragma unroll
-          for (int ii = 0; ii < 2; ++ii) {
-            aw[ii][0] = stage_words(st, r_lo, 2 * pair + ii, c);
-            aw[ii][1] = stage_words(st, r_hi, 2 * pair + ii, c);
+          for (int h = 0; h < 2; ++h) {
+            const int r = h ? r_hi : r_lo;
+            if (r >= rows_b) continue;
+            float* dst = red + (src * p.rows_cap + blk * kBlockRows + r) * kRedCols + 2 * c;
+#pragma unroll
+            for (int e = 0; e < 2; ++e) dst[e] = pi == 0 ? acc[h][e] : dst[e] + acc[h][e];
           }
-          const unsigned char* sp = st + kStageQBytes + 4 * pair;
-          s2[0] = *reinterpret_cast<const uint32_t*>(sp + r_lo * kSzRowBytes);
-          s2[1] = *reinterpret_cast<const uint32_t*>(sp + r_hi * kSzRowBytes);
-          z2[0] = *reinterpret_cast<const uint32_t*>(sp + (kBlockRows + r_lo) * kSzRowBytes);
-          z2[1] = *reinterpret_cast<const uint32_t*>(sp + (kBlockRows + r_hi) * kSzRowBytes);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);  // the stage may be refilled
-        if (!active) continue;
-
-#pragma unroll(MT == 1 ? 2 : 1)
-        for (int ii = 0; ii < 2; ++ii) {
-          const int item_p = j * kItemsPerStage + 2 * pair + ii;  // item within the panel
-          float d[MT][2][4];
+      } else {
+        float acc[2][MT][2];
 #pragma unroll
-          for (int mt = 0; mt < MT; ++mt)
+        for (int h = 0; h < 2; ++h)
 #pragma unroll
-            for (int ch = 0; ch < 2; ++ch)
+          for (int mt = 0; mt < MT; ++mt) acc[h][mt][0] = acc[h][mt][1] = 0.0f;
+        for (int j = 0; j < psteps; ++j) {
+          const int slot = in.next();
+          if (!active) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            continue;
+          }
+          wide_stage<MT, kNI>(stages + slot * kStageBytes, xs, corr, p.xs_stride, p.mc, a.m, j,
+                              2 * group + hs, g, c, r_lo, r_hi, acc, &empty[slot], lane);
+        }
+        if (active) {
 #pragma unroll
-              for (int e = 0; e < 4; ++e) d[mt][ch][e] = 0.0f;
-          // Selects rather than indexing, so a rolled loop keeps aw in registers.
-          const uint4 al = ii == 0 ? aw[0][0] : aw[1][0];
-          const uint4 ah = ii == 0 ? aw[0][1] : aw[1][1];
-          const uint32_t wl[4] = {al.x, al.y, al.z, al.w};
-          const uint32_t wh[4] = {ah.x, ah.y, ah.z, ah.w};
-#pragma unroll
-          for (int jw = 0; jw < 4; ++jw) {
-            uint32_t hl[4], hh[4];
-            unpack_x16(wl[jw], hl);
-            unpack_x16(wh[jw], hh);
-            const uint32_t a0[4] = {hl[0], hh[0], hl[1], hh[1]};
-            const uint32_t a1[4] = {hl[2], hh[2], hl[3], hh[3]};
+          for (int h = 0; h < 2; ++h) {
+            const int r = h ? r_hi : r_lo;
+            if (r >= rows_b) continue;
+            float* dst = red + (src * p.rows_cap + blk * kBlockRows + r) * a.m;
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt) {
-              const int m = g + 8 * mt;
-              uint4 xb = make_uint4(0, 0, 0, 0);
-              if (m < a.m) {
-                xb = *reinterpret_cast<const uint4*>(xs + m * p.xs_stride + item_p * 256 +
-                                                     (jw * 4 + c) * 16);
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const int m = 8 * mt + 2 * c + e;
+                if (m < a.m) dst[m] = pi == 0 ? acc[h][mt][e] : dst[m] + acc[h][mt][e];
               }
-              mma_16816(d[mt][jw & 1], a0, xb.x, xb.y);
-              mma_16816(d[mt][jw & 1], a1, xb.z, xb.w);
-            }
-          }
-          const float s_lo = ii ? half_hi(s2[0]) : half_lo(s2[0]);
-          const float s_hi = ii ? half_hi(s2[1]) : half_lo(s2[1]);
-          const float z_lo = ii ? half_hi(z2[0]) : half_lo(z2[0]);
-          const float z_hi = ii ? half_hi(z2[1]) : half_lo(z2[1]);
-#pragma unroll
-          for (int mt = 0; mt < MT; ++mt) {
-            const int m0 = 8 * mt + 2 * c;
-            const float4 cr = *reinterpret_cast<const float4*>(corr + item_p * p.mc +
-                                                               (m0 < a.m ? m0 : 0));
-            const float d0 = d[mt][0][0] + d[mt][1][0], d1 = d[mt][0][1] + d[mt][1][1];
-            const float d2 = d[mt][0][2] + d[mt][1][2], d3 = d[mt][0][3] + d[mt][1][3];
-            acc[0][mt][0] = fmaf(s_lo, fmaf(-z_lo, cr.y, d0 - cr.x), acc[0][mt][0]);
-            acc[0][mt][1] = fmaf(s_lo, fmaf(-z_lo, cr.w, d1 - cr.z), acc[0][mt][1]);
-            acc[1][mt][0] = fmaf(s_hi, fmaf(-z_hi, cr.y, d2 - cr.x), acc[1][mt][0]);
-            acc[1][mt][1] = fmaf(s_hi, fmaf(-z_hi, cr.w, d3 - cr.z), acc[1][mt][1]);
-          }
-        }
-      }
-      // Block end: this warp's partials of (rows r_lo / r_hi, columns 8 mt + 2 c + e).
-      if (active) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int r = h ? r_hi : r_lo;
-          if (r >= rows_b) continue;
-          float* dst = red + (pair * p.rows_cap + blk * kBlockRows + r) * a.m;
-#pragma unroll
-          for (int mt = 0; mt < MT; ++mt) {
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int m = 8 * mt + 2 * c + e;
-              if (m < a.m) dst[m] = p0 == 0 ? acc[h][mt][e] : dst[m] + acc[h][mt][e];
             }
           }
         }
@@ -286,40 +695,53 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? 2 : 1)
     }
   }
 
-  // ---- add the four item-pair partials of every output in a fixed order; store fp16 ----------
+  // ---- add the partials of every output in a fixed order; store fp16 -------------------------
   named_barrier(kConsumerBarrier, kConsumerThreads);
   for (int o = tid; o < rows * a.m; o += kConsumerThreads) {
     const int m = o / rows;
     const int r = o - m * rows;
     float sum = 0.0f;
+    if constexpr (kNarrow) {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) sum += red[(q * p.rows_cap + r) * a.m + m];
-    if (ok) a.y[static_cast<int64_t>(m) * a.n + row_begin + r] = __float2half_rn(sum);
+      for (int q = 0; q < 4 * kSplit; ++q)
+#pragma unroll
+        for (int f = 0; f < 8 / MP; ++f) sum += red[(q * p.rows_cap + r) * kRedCols + f * MP + m];
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4 * kSplit; ++q) sum += red[(q * p.rows_cap + r) * a.m + m];
+    }
+    if (in.ok) a.y[static_cast<int64_t>(m) * a.n + row_begin + r] = __float2half_rn(sum);
   }
 }
 
-int tile_count(int m) { return (m + 7) / 8; }
+int pad_of(int m) { return m <= 2 ? 2 : m <= 4 ? 4 : 8; }
 
-// Lays out shared memory for `panel_steps` stages per panel; true if it fits `limit` with at
-// least `min_stages` stages.
-bool plan_smem(const GemvArgs& a, MmaPlan* p, int limit, int min_stages) {
+// Lays out shared memory for `panel_steps` stages per panel; true if it fits with at least
+// `min_stages` stages.
+bool plan_smem(const GemvArgs& a, MmaPlan* p, int min_stages) {
+  const bool narrow = pad_of(a.m) < 8;
   const int pk = p->panel_steps * kItemsPerStage * kItemK;
-  p->xs_stride = pk * 2 + 64;
-  int64_t off = 1024;  // mbarriers
+  const int items = pk / kItemK;
+  p->xs_stride = narrow ? (items * kNarrowItemBytes + 127) / 128 * 128 + 16 : pk * 2 + 64;
+  int64_t off = 1024 + kZeroBytes;  // mbarriers, zeros
+  p->off_xr = static_cast<int>(off);
+  off += static_cast<int64_t>(a.m) * pk * 2;
   p->off_xs = static_cast<int>(off);
   off += static_cast<int64_t>(a.m) * p->xs_stride;
   off = (off + 15) / 16 * 16;
   p->off_corr = static_cast<int>(off);
-  off += static_cast<int64_t>(pk / kItemK) * p->mc * 8;
+  off += static_cast<int64_t>(items) * p->mc * 8;
   p->off_red = static_cast<int>(off);
-  off += static_cast<int64_t>(4) * p->rows_cap * a.m * 4;
+  const int sources = 4 * (a.m <= 8 ? 2 : 1);  // partial sums per output row: 4 x warp split
+  off += static_cast<int64_t>(sources) * p->rows_cap * (narrow ? 8 : a.m) * 4;
   off = (off + 1023) / 1024 * 1024;
   p->off_stage = static_cast<int>(off);
-  if (off > limit) return false;
-  const int64_t stages = std::min<int64_t>((limit - off) / kStageBytes, kMaxStages);
+  if (off > kSmemLimit) return false;
+  const int64_t stages = std::min<int64_t>((kSmemLimit - off) / kStageBytes, kMaxStages);
   if (stages < min_stages) return false;
   p->stages = static_cast<int>(stages);
   p->smem_bytes = static_cast<int>(off + stages * kStageBytes);
+  p->pre_stages = std::min({kPreStages, p->panel_steps - 1, p->stages});
   return true;
 }
 
@@ -336,49 +758,33 @@ bool make_plan(const GemvArgs& a, MmaPlan* p, const char** why) {
   p->rows_cap = 4 * ((p->units + p->ctas - 1) / p->ctas);
   p->steps = a.k / (kItemK * kItemsPerStage);
   p->mc = (a.m + 1) & ~1;
-  // Prefer room for the next kernel's CTA, then fewer k-panels.
-  const int limits[3] = {kCoResident, kSmemLimit, kSmemLimit};
-  const int min_stages[3] = {4, 4, 3};
-  for (int t = 0; t < 3; ++t) {
+  p->strict = 0;
+  // Fewest k-panels that leave a deep ring; then accept a shallower one.
+  for (const int min_stages : {8, 4, 3}) {
     for (int panels = 1; panels <= p->steps; ++panels) {
       p->panel_steps = (p->steps + panels - 1) / panels;
-      if (plan_smem(a, p, limits[t], min_stages[t])) {
-        p->strict = 0;
-        return true;
-      }
+      if (plan_smem(a, p, min_stages)) return true;
     }
   }
   return fail("x does not fit in shared memory");
 }
 
-std::once_flag g_attr_once[4][64];
-
-template <int MT>
-cudaError_t ensure_smem_attr() {
-  int dev = 0;
-  cudaError_t err = cudaGetDevice(&dev);
-  if (err != cudaSuccess) return err;
-  cudaError_t result = cudaSuccess;
-  std::call_once(g_attr_once[MT - 1][dev & 63], [&] {
-    result = cudaFuncSetAttribute(stream_mma_kernel<MT>,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-  });
-  return result;
-}
-
+// Kernel instances (MP, MT) for M = 1..2, 3..4, 5..8, 9..16, 17..24, 25..32.
 template <typename F>
-cudaError_t with_mt(int m, F&& f) {
-  switch (tile_count(m)) {
-    case 1:
-      return f.template operator()<1>();
-    case 2:
-      return f.template operator()<2>();
-    case 3:
-      return f.template operator()<3>();
-    default:
-      return f.template operator()<4>();
-  }
+cudaError_t with_shape(int m, F&& f) {
+  if (m <= 2) return f.template operator()<2, 1>();
+  if (m <= 4) return f.template operator()<4, 1>();
+  if (m <= 8) return f.template operator()<8, 1>();
+  if (m <= 16) return f.template operator()<8, 2>();
+  if (m <= 24) return f.template operator()<8, 3>();
+  return f.template operator()<8, 4>();
 }
+
+int shape_index(int m) {
+  return m <= 2 ? 0 : m <= 4 ? 1 : m <= 8 ? 2 : m <= 16 ? 3 : m <= 24 ? 4 : 5;
+}
+
+std::once_flag g_attr_once[6][64];
 
 }  // namespace
 
@@ -396,12 +802,19 @@ cudaError_t launch_stream_mma(const GemvArgs& a, cudaStream_t stream, bool stric
   WeightMaps maps;
   const cudaError_t merr = weight_maps_for(a, &maps);
   if (merr != cudaSuccess) return merr;
-  return with_mt(a.m, [&]<int MT>() {
-    cudaError_t err = ensure_smem_attr<MT>();
-    if (err != cudaSuccess) return err;
+  int dev = 0;
+  const cudaError_t derr = cudaGetDevice(&dev);
+  if (derr != cudaSuccess) return derr;
+  return with_shape(a.m, [&]<int MP, int MT>() {
+    cudaError_t result = cudaSuccess;
+    std::call_once(g_attr_once[shape_index(a.m)][dev & 63], [&] {
+      result = cudaFuncSetAttribute(stream_mma_kernel<MP, MT>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    });
+    if (result != cudaSuccess) return result;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.ctas);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3((consumer_warps<MT>() + 1) * kWarp);
     cfg.dynamicSmemBytes = p.smem_bytes;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -409,20 +822,36 @@ cudaError_t launch_stream_mma(const GemvArgs& a, cudaStream_t stream, bool stric
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, stream_mma_kernel<MT>, a, p, maps);
+    return cudaLaunchKernelEx(&cfg, stream_mma_kernel<MP, MT>, a, p, maps);
   });
 }
 
+// Occupancy is reported for the shared memory the kernel uses at N = K = 8192.
 cudaError_t stream_mma_attrs(int m, KernelAttrs* out) {
-  return with_mt(m < 1 ? 1 : m, [&]<int MT>() {
+  const int mm = m < 1 ? 1 : m > kMaxM ? kMaxM : m;
+  return with_shape(mm, [&]<int MP, int MT>() {
     cudaFuncAttributes fa;
-    cudaError_t err = cudaFuncGetAttributes(&fa, stream_mma_kernel<MT>);
+    cudaError_t err = cudaFuncGetAttributes(&fa, stream_mma_kernel<MP, MT>);
     if (err != cudaSuccess) return err;
+    err = cudaFuncSetAttribute(stream_mma_kernel<MP, MT>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    if (err != cudaSuccess) return err;
+    GemvArgs a{};
+    a.m = mm;
+    a.n = a.k = 8192;
+    a.group = kItemK;
+    MmaPlan p;
+    int blocks = 0;
+    if (make_plan(a, &p, nullptr)) {
+      err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+          &blocks, stream_mma_kernel<MP, MT>, (consumer_warps<MT>() + 1) * kWarp, p.smem_bytes);
+      if (err != cudaSuccess) return err;
+    }
     out->registers = fa.numRegs;
     out->local_bytes = static_cast<int>(fa.localSizeBytes);
     out->max_threads_per_block = fa.maxThreadsPerBlock;
-    out->blocks_per_sm = 1;  // plus, when it fits in 113 KB, the next kernel's CTA
-    out->threads_per_block = kThreads;
+    out->blocks_per_sm = blocks;
+    out->threads_per_block = (consumer_warps<MT>() + 1) * kWarp;
     return cudaSuccess;
   });
 }

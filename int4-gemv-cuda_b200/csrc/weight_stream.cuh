@@ -48,11 +48,70 @@ bool weight_stream_supported(const GemvArgs& a, const char** why);
 // Encoded maps for this call's tensors (cached per device and pointer set).
 cudaError_t weight_maps_for(const GemvArgs& a, WeightMaps* out);
 
+// The tile this lane copies for a block of up to 32 rows: lane l copies weight column chunk l % 4
+// of box l / 4 (lanes 0..15), or the scales (lanes 16..19) or zeros (lanes 20..23) of box l % 4.
+// Boxes are the binary decomposition of the block's row count (rounded up to 4), largest first.
+// Returns false if the lane has no box in this block.
+struct LaneBox {
+  const CUtensorMap* map;
+  int dst_off;  // byte offset inside a stage
+  int y;        // first row
+  int kind;     // 0 weights, 1 scales, 2 zeros
+  int chunk;
+};
+
+__device__ __forceinline__ bool lane_box(const WeightMaps& maps, int lane, int rows4, int block_row0,
+                                         LaneBox* b) {
+  const int box_idx = lane < 16 ? lane / 4 : lane % 4;
+  int box_map = -1, box_off = 0;
+  int n = 0, off = 0;
+  for (int hi = 0; hi < 4; ++hi) {
+    if (rows4 & box_height(hi)) {
+      if (n == box_idx) {
+        box_map = hi;
+        box_off = off;
+      }
+      ++n;
+      off += box_height(hi);
+    }
+  }
+  if (lane >= 24 || box_map < 0) return false;
+  b->kind = lane < 16 ? 0 : lane < 20 ? 1 : 2;
+  b->chunk = lane % 4;
+  b->y = block_row0 + box_off;
+  b->map = b->kind == 0 ? &maps.q[box_map] : b->kind == 1 ? &maps.s[box_map] : &maps.z[box_map];
+  b->dst_off = b->kind == 0   ? b->chunk * kChunkBytes + box_off * 128
+               : b->kind == 1 ? kStageQBytes + box_off * kSzRowBytes
+                              : kStageQBytes + (kBlockRows + box_off) * kSzRowBytes;
+  return true;
+}
+
+__device__ __forceinline__ int box_x(const LaneBox& b, int j) {
+  return b.kind == 0 ? j * kStageRowBytes + b.chunk * 128 : j * kItemsPerStage;
+}
+
+// One stage of one block: lane 0 arms full_bar with the stage's bytes, then every lane with a box
+// copies its tile into `stage`.
+__device__ __forceinline__ void issue_stage(const LaneBox& b, bool has_box, int j, int rows4,
+                                            unsigned char* stage, uint64_t* full_bar,
+                                            uint64_t policy, int lane) {
+  if (lane == 0) mbar_arrive_expect_tx(full_bar, static_cast<uint32_t>(rows4 * kStageTx));
+  __syncwarp();
+  if (has_box) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_addr(stage + b.dst_off)),
+        "l"(b.map), "r"(box_x(b, j)), "r"(b.y), "r"(smem_addr(full_bar)), "l"(policy)
+        : "memory");
+  }
+}
+
 // The producer warp's loop. Streams the CTA's `rows` rows (from row_begin) in k-panels of
-// `panel_steps` stages (the last panel may be shorter; panel_steps >= steps gives one panel):
-// for each panel, for each block of 32 rows, the panel's stages in k order, through `n_stages`
-// ring buffers. full[s] expects one arrival (lane 0's expect_tx) plus the bytes; empty[s] is
-// released by the consumers. Returns after its last copies have landed.
+// `panel_steps` stages (panel_steps >= steps gives one panel): for each panel, for each block of
+// 32 rows, the panel's stages in k order, through `n_stages` ring buffers. full[s] expects one
+// arrival (lane 0's expect_tx) plus the bytes; empty[s] is released by the consumers. Returns
+// after its last copies have landed. (Requesting the stages beyond the ring into L2 ahead of time
+// was measured slower on B200: it delays other CTAs' tiles more than it hides latency.)
 __device__ __forceinline__ void produce_weight_stages(const WeightMaps& maps, int row_begin,
                                                       int rows, int steps, int panel_steps,
                                                       unsigned char* stages, int n_stages,
@@ -61,11 +120,6 @@ __device__ __forceinline__ void produce_weight_stages(const WeightMaps& maps, in
   const int lane = threadIdx.x % kWarp;
   const uint64_t policy = l2_evict_first_policy();
   const int blocks = (rows + kBlockRows - 1) / kBlockRows;
-  const int kind = lane < 16 ? 0 : lane < 20 ? 1 : 2;  // weights, scales, zeros
-  const int chunk = lane % 4;
-  // Lane l copies weight column chunk l % 4 of box l / 4 (lanes 0..15), or the scales
-  // (lanes 16..19) or zeros (lanes 20..23) of box l % 4.
-  const int box_idx = lane < 16 ? lane / 4 : lane % 4;
   bool ok = true;
   int it = 0;
   int slot = 0, use = 0;
@@ -73,48 +127,15 @@ __device__ __forceinline__ void produce_weight_stages(const WeightMaps& maps, in
     const int p1 = min(steps, p0 + panel_steps);
     for (int blk = 0; blk < blocks; ++blk) {
       const int rows4 = (min(kBlockRows, rows - blk * kBlockRows) + 3) & ~3;
-      int box_map = -1, box_off = 0;
-      {
-        int b = 0, off = 0;
-        for (int hi = 0; hi < 4; ++hi) {
-          if (rows4 & box_height(hi)) {
-            if (b == box_idx) {
-              box_map = hi;
-              box_off = off;
-            }
-            ++b;
-            off += box_height(hi);
-          }
-        }
-      }
-      if (lane >= 24) box_map = -1;
-      const int y = row_begin + blk * kBlockRows + box_off;
-      const CUtensorMap* map = box_map < 0 ? nullptr
-                               : kind == 0 ? &maps.q[box_map]
-                               : kind == 1 ? &maps.s[box_map]
-                                           : &maps.z[box_map];
-      const int dst_off = kind == 0   ? chunk * kChunkBytes + box_off * 128
-                          : kind == 1 ? kStageQBytes + box_off * kSzRowBytes
-                                      : kStageQBytes + (kBlockRows + box_off) * kSzRowBytes;
+      LaneBox b;
+      const bool has_box = lane_box(maps, lane, rows4, row_begin + blk * kBlockRows, &b);
       for (int j = p0; j < p1; ++j, ++it) {
         if (ok && use > 0 && !mbar_wait_bounded(&empty[slot], (use - 1) & 1)) {
           ok = false;
           if (lane == 0) atomicExch(status, kStatusEmptyBarrierTimeout);
         }
         if (ok) {
-          if (lane == 0) {
-            mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(rows4 * kStageTx));
-          }
-          __syncwarp();
-          if (box_map >= 0) {
-            unsigned char* dst = stages + slot * kStageBytes + dst_off;
-            const int x = kind == 0 ? j * kStageRowBytes + chunk * 128 : j * kItemsPerStage;
-            asm volatile(
-                "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
-                ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_addr(dst)),
-                "l"(map), "r"(x), "r"(y), "r"(smem_addr(&full[slot])), "l"(policy)
-                : "memory");
-          }
+          issue_stage(b, has_box, j, rows4, stages + slot * kStageBytes, &full[slot], policy, lane);
         }
         if (++slot == n_stages) {
           slot = 0;
