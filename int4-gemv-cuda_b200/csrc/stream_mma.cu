@@ -408,9 +408,10 @@ __device__ __forceinline__ void narrow_stage(const NarrowThread<MP, NR>& t,
   __syncwarp();
   if (lane == 0) mbar_arrive(empty_bar);  // the stage may be refilled
 
-  // Accumulators: MP 2: [set][hh]; MP 4: [set][hh % 2]. Consecutive MMAs in program order never
-  // share an accumulator; the first MMA into each starts it (C = 0).
-  constexpr int kAcc = MP == 4 ? 2 : 4;
+  // Accumulators: MP 2: one per set; MP 4: [set][hh % 2]. The first MMA into each starts it
+  // (C = 0). A single chain per set measured fastest for MP 2: the other warps hide its latency
+  // and the stage saves the adds of separate chains.
+  constexpr int kAcc = MP == 4 ? 2 : 1;
   float d[kSets][kAcc][4];
 #pragma unroll
   for (int j = 0; j < NR; ++j) {
@@ -441,7 +442,7 @@ __device__ __forceinline__ void narrow_stage(const NarrowThread<MP, NR>& t,
       const uint4& bx = hh < 2 ? bx0 : bx1;
       const uint32_t b0 = (hh & 1) ? bx.z : bx.x;
       const uint32_t b1 = (hh & 1) ? bx.w : bx.y;
-      const bool first = MP == 2 ? (j & 1) == 0 : hh < 2;
+      const bool first = MP == 2 ? ((j & 1) == 0 && hh == 0) : hh < 2;
       if (first) {
         mma_16816_first(d[set][hh % kAcc], afr, b0, b1);
       } else {
@@ -549,19 +550,15 @@ __device__ __forceinline__ void wide_stage(const unsigned char* st, const unsign
   }
 }
 
-// Consumer warps per CTA: 16 when M <= 8 (at most 96 registers: 17 warps, at most 5 per SM
-// sub-partition, fit its 16384 registers), else 8 (168 registers: 3 warps per sub-partition).
-template <int MT>
-__host__ __device__ constexpr int consumer_warps() {
-  return MT == 1 ? 16 : 8;
-}
-
-// MP: M rounded up to 2 or 4 (narrow path) or 8 (wide path, MT tiles of 8 rows of x).
-template <int MP, int MT>
-__global__ void __maxnreg__(MT == 1 ? 96 : 168)
+// MP: M rounded up to 2 or 4 (narrow path) or 8 (wide path, MT tiles of 8 rows of x). CW:
+// consumer warps, 8 or 16. With 16 (17 warps, at most 5 per SM sub-partition) a thread may use
+// 96 registers, so the sub-partition's 16384 registers hold them; with 8 (3 per sub-partition),
+// 168. Measured on B200: M = 1 is fastest with 8 consumer warps, 2 <= M <= 8 with 16.
+template <int MP, int MT, int CW>
+__global__ void __maxnreg__(CW == 16 ? 96 : 168)
     stream_mma_kernel(GemvArgs a, MmaPlan p, const __grid_constant__ WeightMaps maps) {
   constexpr bool kNarrow = MP < 8;
-  constexpr int kCW = consumer_warps<MT>();
+  constexpr int kCW = CW;
   constexpr int kConsumerThreads = kCW * kWarp;
   constexpr int kThreads = kConsumerThreads + kWarp;
   constexpr int kSplit = kCW / 8;      // warps sharing one (tile, word quarter or item pair)
@@ -716,6 +713,8 @@ __global__ void __maxnreg__(MT == 1 ? 96 : 168)
 
 int pad_of(int m) { return m <= 2 ? 2 : m <= 4 ? 4 : 8; }
 
+int consumer_warps_for(int m) { return m == 1 || m > 8 ? 8 : 16; }
+
 // Lays out shared memory for `panel_steps` stages per panel; true if it fits with at least
 // `min_stages` stages.
 bool plan_smem(const GemvArgs& a, MmaPlan* p, int min_stages) {
@@ -732,7 +731,7 @@ bool plan_smem(const GemvArgs& a, MmaPlan* p, int min_stages) {
   p->off_corr = static_cast<int>(off);
   off += static_cast<int64_t>(items) * p->mc * 8;
   p->off_red = static_cast<int>(off);
-  const int sources = 4 * (a.m <= 8 ? 2 : 1);  // partial sums per output row: 4 x warp split
+  const int sources = 4 * (consumer_warps_for(a.m) / 8);  // partial sums per output row
   off += static_cast<int64_t>(sources) * p->rows_cap * (narrow ? 8 : a.m) * 4;
   off = (off + 1023) / 1024 * 1024;
   p->off_stage = static_cast<int>(off);
@@ -769,22 +768,23 @@ bool make_plan(const GemvArgs& a, MmaPlan* p, const char** why) {
   return fail("x does not fit in shared memory");
 }
 
-// Kernel instances (MP, MT) for M = 1..2, 3..4, 5..8, 9..16, 17..24, 25..32.
+// Kernel instances (MP, MT, CW) for M = 1, 2, 3..4, 5..8, 9..16, 17..24, 25..32.
 template <typename F>
 cudaError_t with_shape(int m, F&& f) {
-  if (m <= 2) return f.template operator()<2, 1>();
-  if (m <= 4) return f.template operator()<4, 1>();
-  if (m <= 8) return f.template operator()<8, 1>();
-  if (m <= 16) return f.template operator()<8, 2>();
-  if (m <= 24) return f.template operator()<8, 3>();
-  return f.template operator()<8, 4>();
+  if (m <= 1) return f.template operator()<2, 1, 8>();
+  if (m <= 2) return f.template operator()<2, 1, 16>();
+  if (m <= 4) return f.template operator()<4, 1, 16>();
+  if (m <= 8) return f.template operator()<8, 1, 16>();
+  if (m <= 16) return f.template operator()<8, 2, 8>();
+  if (m <= 24) return f.template operator()<8, 3, 8>();
+  return f.template operator()<8, 4, 8>();
 }
 
 int shape_index(int m) {
-  return m <= 2 ? 0 : m <= 4 ? 1 : m <= 8 ? 2 : m <= 16 ? 3 : m <= 24 ? 4 : 5;
+  return m <= 1 ? 0 : m <= 2 ? 1 : m <= 4 ? 2 : m <= 8 ? 3 : m <= 16 ? 4 : m <= 24 ? 5 : 6;
 }
 
-std::once_flag g_attr_once[6][64];
+std::once_flag g_attr_once[7][64];
 
 }  // namespace
 
@@ -805,16 +805,16 @@ cudaError_t launch_stream_mma(const GemvArgs& a, cudaStream_t stream, bool stric
   int dev = 0;
   const cudaError_t derr = cudaGetDevice(&dev);
   if (derr != cudaSuccess) return derr;
-  return with_shape(a.m, [&]<int MP, int MT>() {
+  return with_shape(a.m, [&]<int MP, int MT, int CW>() {
     cudaError_t result = cudaSuccess;
     std::call_once(g_attr_once[shape_index(a.m)][dev & 63], [&] {
-      result = cudaFuncSetAttribute(stream_mma_kernel<MP, MT>,
+      result = cudaFuncSetAttribute(stream_mma_kernel<MP, MT, CW>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
     });
     if (result != cudaSuccess) return result;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.ctas);
-    cfg.blockDim = dim3((consumer_warps<MT>() + 1) * kWarp);
+    cfg.blockDim = dim3((CW + 1) * kWarp);
     cfg.dynamicSmemBytes = p.smem_bytes;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -822,18 +822,18 @@ cudaError_t launch_stream_mma(const GemvArgs& a, cudaStream_t stream, bool stric
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, stream_mma_kernel<MP, MT>, a, p, maps);
+    return cudaLaunchKernelEx(&cfg, stream_mma_kernel<MP, MT, CW>, a, p, maps);
   });
 }
 
 // Occupancy is reported for the shared memory the kernel uses at N = K = 8192.
 cudaError_t stream_mma_attrs(int m, KernelAttrs* out) {
   const int mm = m < 1 ? 1 : m > kMaxM ? kMaxM : m;
-  return with_shape(mm, [&]<int MP, int MT>() {
+  return with_shape(mm, [&]<int MP, int MT, int CW>() {
     cudaFuncAttributes fa;
-    cudaError_t err = cudaFuncGetAttributes(&fa, stream_mma_kernel<MP, MT>);
+    cudaError_t err = cudaFuncGetAttributes(&fa, stream_mma_kernel<MP, MT, CW>);
     if (err != cudaSuccess) return err;
-    err = cudaFuncSetAttribute(stream_mma_kernel<MP, MT>,
+    err = cudaFuncSetAttribute(stream_mma_kernel<MP, MT, CW>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
     if (err != cudaSuccess) return err;
     GemvArgs a{};
@@ -844,14 +844,14 @@ cudaError_t stream_mma_attrs(int m, KernelAttrs* out) {
     int blocks = 0;
     if (make_plan(a, &p, nullptr)) {
       err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-          &blocks, stream_mma_kernel<MP, MT>, (consumer_warps<MT>() + 1) * kWarp, p.smem_bytes);
+          &blocks, stream_mma_kernel<MP, MT, CW>, (CW + 1) * kWarp, p.smem_bytes);
       if (err != cudaSuccess) return err;
     }
     out->registers = fa.numRegs;
     out->local_bytes = static_cast<int>(fa.localSizeBytes);
     out->max_threads_per_block = fa.maxThreadsPerBlock;
     out->blocks_per_sm = blocks;
-    out->threads_per_block = (consumer_warps<MT>() + 1) * kWarp;
+    out->threads_per_block = (CW + 1) * kWarp;
     return cudaSuccess;
   });
 }
