@@ -375,58 +375,69 @@ struct SzBits {
   }
 };
 
-// One stage of one warp: load the A words, scales and zeros, release the stage, then 4 NR MMAs and
-// the epilogue into acc[row lo / hi][e].
+// One landed stage's operands in registers: the A words, scales and zeros of the warp's share.
 template <int MP, int NR>
-__device__ __forceinline__ void narrow_stage(const NarrowThread<MP, NR>& t,
-                                             const unsigned char* st, const unsigned char* xb,
-                                             const float2* corr_stage, int mc, int m_rows,
-                                             float (&acc)[2][2], uint64_t* empty_bar, int lane) {
-  constexpr int kSets = NarrowThread<MP, NR>::kSets;
-  uint4 wa[2][2];  // MP 2: [item sel][row] = the 4 words of the granule
-  uint2 wb[4][2];  // MP 4: [round][row] = words w, w + 1
+struct NarrowRegs {
+  uint4 wa[2][2];              // MP 2: [item sel][row] = the 4 words of the granule
+  uint2 wb[4][2];              // MP 4: [round][row] = words w, w + 1
+  SzBits<MP, NR> sb[2], zb[2];  // [row]
+};
+
+template <int MP>
+__host__ __device__ constexpr int narrow_acc() {  // accumulator chains per D set
+  return MP == 4 ? 2 : 1;
+}
+
+// Loads the warp's share of a landed stage into registers and releases the stage.
+template <int MP, int NR>
+__device__ __forceinline__ void narrow_load(const NarrowThread<MP, NR>& t, const unsigned char* st,
+                                            NarrowRegs<MP, NR>& r, uint64_t* empty_bar,
+                                            int lane) {
   if (MP == 4) {
 #pragma unroll
     for (int j = 0; j < NR; ++j)
 #pragma unroll
-      for (int h = 0; h < 2; ++h) wb[j][h] = *reinterpret_cast<const uint2*>(st + t.a_off(j, h));
+      for (int h = 0; h < 2; ++h) r.wb[j][h] = *reinterpret_cast<const uint2*>(st + t.a_off(j, h));
   } else {
 #pragma unroll
     for (int i = 0; i < NR / 2; ++i)
 #pragma unroll
-      for (int h = 0; h < 2; ++h) wa[i][h] = *reinterpret_cast<const uint4*>(st + t.a_off(i, h));
+      for (int h = 0; h < 2; ++h) r.wa[i][h] = *reinterpret_cast<const uint4*>(st + t.a_off(i, h));
   }
-  SzBits<MP, NR> sb[2], zb[2];  // [row]
   const unsigned char* sp = st + kStageQBytes;
   const unsigned char* zp = sp + kBlockRows * kSzRowBytes;
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const int row = h ? t.r_hi : t.r_lo;
-    sb[h].load(sp + row * kSzRowBytes, t.item0);
-    if (t.q == 0) zb[h].load(zp + row * kSzRowBytes, t.item0);
+    r.sb[h].load(sp + row * kSzRowBytes, t.item0);
+    if (t.q == 0) r.zb[h].load(zp + row * kSzRowBytes, t.item0);
   }
   __syncwarp();
   if (lane == 0) mbar_arrive(empty_bar);  // the stage may be refilled
+}
 
-  // Accumulators: MP 2: one per set; MP 4: [set][hh % 2]. The first MMA into each starts it
-  // (C = 0). A single chain per set measured fastest for MP 2: the other warps hide its latency
-  // and the stage saves the adds of separate chains.
-  constexpr int kAcc = MP == 4 ? 2 : 1;
-  float d[kSets][kAcc][4];
+// The stage's 4 NR MMAs. Accumulators: MP 2: one chain per set; MP 4: [set][hh % 2]. The first MMA
+// into each chain starts it (C = 0). A single chain per set measured fastest for MP 2: the other
+// warps and the overlapped loads of the next stage hide its latency.
+template <int MP, int NR>
+__device__ __forceinline__ void narrow_mma(const NarrowRegs<MP, NR>& r, const unsigned char* xb,
+                                           float (&d)[NarrowThread<MP, NR>::kSets]
+                                                     [narrow_acc<MP>()][4]) {
+  constexpr int kAcc = narrow_acc<MP>();
 #pragma unroll
   for (int j = 0; j < NR; ++j) {
     uint32_t w0r0, w0r1, w1r0, w1r1;  // words w, w + 1 of rows r_lo, r_hi
     if (MP == 2) {
       const int w = 2 * (j & 1);
-      w0r0 = word_of(wa[j >> 1][0], w);
-      w0r1 = word_of(wa[j >> 1][1], w);
-      w1r0 = word_of(wa[j >> 1][0], w + 1);
-      w1r1 = word_of(wa[j >> 1][1], w + 1);
+      w0r0 = word_of(r.wa[j >> 1][0], w);
+      w0r1 = word_of(r.wa[j >> 1][1], w);
+      w1r0 = word_of(r.wa[j >> 1][0], w + 1);
+      w1r1 = word_of(r.wa[j >> 1][1], w + 1);
     } else {
-      w0r0 = wb[j][0].x;
-      w0r1 = wb[j][1].x;
-      w1r0 = wb[j][0].y;
-      w1r1 = wb[j][1].y;
+      w0r0 = r.wb[j][0].x;
+      w0r1 = r.wb[j][1].x;
+      w1r0 = r.wb[j][0].y;
+      w1r1 = r.wb[j][1].y;
     }
     uint32_t u00[4], u01[4], u10[4], u11[4];
     unpack_x16(w0r0, u00);
@@ -450,6 +461,20 @@ __device__ __forceinline__ void narrow_stage(const NarrowThread<MP, NR>& t,
       }
     }
   }
+}
+
+// Scale (and, in the q == 0 warps, the group correction) of the stage's D sets into
+// acc[row lo / hi][e]. kCorr and the x row count are compile-time where the kernel instance
+// allows, so the epilogue has no selects.
+template <int MP, int NR, bool kCorr>
+__device__ __forceinline__ void narrow_epilogue_impl(const NarrowThread<MP, NR>& t,
+                                                     const NarrowRegs<MP, NR>& r,
+                                                     const float (&d)[NarrowThread<MP, NR>::kSets]
+                                                                     [narrow_acc<MP>()][4],
+                                                     const float2* corr_stage, int mc, int m_rows,
+                                                     float (&acc)[2][2]) {
+  constexpr int kSets = NarrowThread<MP, NR>::kSets;
+  constexpr int kAcc = narrow_acc<MP>();
 #pragma unroll
   for (int set = 0; set < kSets; ++set) {
     float dsum[4];
@@ -464,15 +489,32 @@ __device__ __forceinline__ void narrow_stage(const NarrowThread<MP, NR>& t,
     for (int e = 0; e < 2; ++e) {
       const int m = t.col_m(e);
       if (m >= m_rows) continue;
-      float2 cr = make_float2(0.0f, 0.0f);
-      if (t.q == 0) cr = corr_stage[t.col_item(set) * mc + m];
+      if (kCorr) {
+        const float2 cr = corr_stage[t.col_item(set) * mc + m];
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const float z = t.q == 0 ? zb[h].get(set) : 0.0f;
-        const float v = dsum[2 * h + e] - fmaf(z, cr.y, cr.x);
-        acc[h][e] = fmaf(sb[h].get(set), v, acc[h][e]);
+        for (int h = 0; h < 2; ++h) {
+          const float v = dsum[2 * h + e] - fmaf(r.zb[h].get(set), cr.y, cr.x);
+          acc[h][e] = fmaf(r.sb[h].get(set), v, acc[h][e]);
+        }
+      } else {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) acc[h][e] = fmaf(r.sb[h].get(set), dsum[2 * h + e], acc[h][e]);
       }
     }
+  }
+}
+
+template <int MP, int NR>
+__device__ __forceinline__ void narrow_epilogue(const NarrowThread<MP, NR>& t,
+                                                const NarrowRegs<MP, NR>& r,
+                                                const float (&d)[NarrowThread<MP, NR>::kSets]
+                                                                [narrow_acc<MP>()][4],
+                                                const float2* corr_stage, int mc, int m_rows,
+                                                float (&acc)[2][2]) {
+  if (t.q == 0) {  // warp-uniform
+    narrow_epilogue_impl<MP, NR, true>(t, r, d, corr_stage, mc, m_rows, acc);
+  } else {
+    narrow_epilogue_impl<MP, NR, false>(t, r, d, corr_stage, mc, m_rows, acc);
   }
 }
 
@@ -550,14 +592,15 @@ __device__ __forceinline__ void wide_stage(const unsigned char* st, const unsign
   }
 }
 
-// MP: M rounded up to 2 or 4 (narrow path) or 8 (wide path, MT tiles of 8 rows of x). CW:
-// consumer warps, 8 or 16. With 16 (17 warps, at most 5 per SM sub-partition) a thread may use
+// MP: M rounded up to 2 or 4 (narrow path) or 8 (wide path, MT tiles of 8 rows of x). MC: M when
+// the instance serves a single M (else 0: read at run time). CW: consumer warps, 8 or 16. With 16 (17 warps, at most 5 per SM sub-partition) a thread may use
 // 96 registers, so the sub-partition's 16384 registers hold them; with 8 (3 per sub-partition),
 // 168. Measured on B200: M = 1 is fastest with 8 consumer warps, 2 <= M <= 8 with 16.
-template <int MP, int MT, int CW>
+template <int MP, int MT, int CW, int MC>
 __global__ void __maxnreg__(CW == 16 ? 96 : 168)
     stream_mma_kernel(GemvArgs a, MmaPlan p, const __grid_constant__ WeightMaps maps) {
   constexpr bool kNarrow = MP < 8;
+  const int m_rows = MC > 0 ? MC : a.m;  // rows of x: compile-time where the instance has one M
   constexpr int kCW = CW;
   constexpr int kConsumerThreads = kCW * kWarp;
   constexpr int kThreads = kConsumerThreads + kWarp;
@@ -615,7 +658,7 @@ __global__ void __maxnreg__(CW == 16 ? 96 : 168)
   const int r_lo = 16 * tile + mma_row(g);
   const int r_hi = r_lo + 8;
   NarrowThread<kNarrow ? MP : 2, kNR> nt;
-  if constexpr (kNarrow) nt.init(warp, lane, a.m, p.xs_stride, static_cast<int>(zero - xs));
+  if constexpr (kNarrow) nt.init(warp, lane, m_rows, p.xs_stride, static_cast<int>(zero - xs));
 
   StageRing in{full, p.stages, p.status, true, 0, 0u};
   for (int pi = 0, p0 = 0; p0 < p.steps; ++pi, p0 += p.panel_steps) {
@@ -635,16 +678,37 @@ __global__ void __maxnreg__(CW == 16 ? 96 : 168)
       const bool active = 16 * tile < rows_b;
       if constexpr (kNarrow) {
         float acc[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
-        for (int j = 0; j < psteps; ++j) {
-          const int slot = in.next();
-          if (!active) {
+        if (!active) {
+          for (int j = 0; j < psteps; ++j) {
+            const int slot = in.next();
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
-            continue;
           }
-          narrow_stage<MP, kNR>(nt, stages + slot * kStageBytes, xs + nt.b_base + j * nt.b_step,
-                                corr + j * kItemsPerStage * p.mc, p.mc, a.m, acc, &empty[slot],
-                                lane);
+        } else {
+          // Software pipeline, two stages per iteration with alternating register sets: the MMAs
+          // of stage j are issued, then stage j + 1 is waited for and loaded, then stage j's
+          // epilogue runs, so the MMA latency overlaps the wait and the loads.
+          using Regs = NarrowRegs<MP, kNR>;
+          using Acc = float[NarrowThread<MP, kNR>::kSets][narrow_acc<MP>()][4];
+          Regs ra, rb;
+          int slot = in.next();
+          narrow_load(nt, stages + slot * kStageBytes, ra, &empty[slot], lane);
+          for (int j = 0; j < psteps; j += 2) {
+            Acc d;
+            narrow_mma(ra, xs + nt.b_base + j * nt.b_step, d);
+            if (j + 1 < psteps) {
+              slot = in.next();
+              narrow_load(nt, stages + slot * kStageBytes, rb, &empty[slot], lane);
+            }
+            narrow_epilogue(nt, ra, d, corr + j * kItemsPerStage * p.mc, p.mc, m_rows, acc);
+            if (j + 1 >= psteps) break;
+            narrow_mma(rb, xs + nt.b_base + (j + 1) * nt.b_step, d);
+            if (j + 2 < psteps) {
+              slot = in.next();
+              narrow_load(nt, stages + slot * kStageBytes, ra, &empty[slot], lane);
+            }
+            narrow_epilogue(nt, rb, d, corr + (j + 1) * kItemsPerStage * p.mc, p.mc, m_rows, acc);
+          }
         }
         if (active) {
 #pragma unroll
@@ -771,13 +835,13 @@ bool make_plan(const GemvArgs& a, MmaPlan* p, const char** why) {
 // Kernel instances (MP, MT, CW) for M = 1, 2, 3..4, 5..8, 9..16, 17..24, 25..32.
 template <typename F>
 cudaError_t with_shape(int m, F&& f) {
-  if (m <= 1) return f.template operator()<2, 1, 8>();
-  if (m <= 2) return f.template operator()<2, 1, 16>();
-  if (m <= 4) return f.template operator()<4, 1, 16>();
-  if (m <= 8) return f.template operator()<8, 1, 16>();
-  if (m <= 16) return f.template operator()<8, 2, 8>();
-  if (m <= 24) return f.template operator()<8, 3, 8>();
-  return f.template operator()<8, 4, 8>();
+  if (m <= 1) return f.template operator()<2, 1, 8, 1>();
+  if (m <= 2) return f.template operator()<2, 1, 16, 2>();
+  if (m <= 4) return f.template operator()<4, 1, 16, 0>();
+  if (m <= 8) return f.template operator()<8, 1, 16, 0>();
+  if (m <= 16) return f.template operator()<8, 2, 8, 0>();
+  if (m <= 24) return f.template operator()<8, 3, 8, 0>();
+  return f.template operator()<8, 4, 8, 0>();
 }
 
 int shape_index(int m) {
@@ -805,10 +869,10 @@ cudaError_t launch_stream_mma(const GemvArgs& a, cudaStream_t stream, bool stric
   int dev = 0;
   const cudaError_t derr = cudaGetDevice(&dev);
   if (derr != cudaSuccess) return derr;
-  return with_shape(a.m, [&]<int MP, int MT, int CW>() {
+  return with_shape(a.m, [&]<int MP, int MT, int CW, int MC>() {
     cudaError_t result = cudaSuccess;
     std::call_once(g_attr_once[shape_index(a.m)][dev & 63], [&] {
-      result = cudaFuncSetAttribute(stream_mma_kernel<MP, MT, CW>,
+      result = cudaFuncSetAttribute(stream_mma_kernel<MP, MT, CW, MC>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
     });
     if (result != cudaSuccess) return result;
@@ -822,18 +886,18 @@ cudaError_t launch_stream_mma(const GemvArgs& a, cudaStream_t stream, bool stric
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, stream_mma_kernel<MP, MT, CW>, a, p, maps);
+    return cudaLaunchKernelEx(&cfg, stream_mma_kernel<MP, MT, CW, MC>, a, p, maps);
   });
 }
 
 // Occupancy is reported for the shared memory the kernel uses at N = K = 8192.
 cudaError_t stream_mma_attrs(int m, KernelAttrs* out) {
   const int mm = m < 1 ? 1 : m > kMaxM ? kMaxM : m;
-  return with_shape(mm, [&]<int MP, int MT, int CW>() {
+  return with_shape(mm, [&]<int MP, int MT, int CW, int MC>() {
     cudaFuncAttributes fa;
-    cudaError_t err = cudaFuncGetAttributes(&fa, stream_mma_kernel<MP, MT, CW>);
+    cudaError_t err = cudaFuncGetAttributes(&fa, stream_mma_kernel<MP, MT, CW, MC>);
     if (err != cudaSuccess) return err;
-    err = cudaFuncSetAttribute(stream_mma_kernel<MP, MT, CW>,
+    err = cudaFuncSetAttribute(stream_mma_kernel<MP, MT, CW, MC>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
     if (err != cudaSuccess) return err;
     GemvArgs a{};
@@ -844,7 +908,7 @@ cudaError_t stream_mma_attrs(int m, KernelAttrs* out) {
     int blocks = 0;
     if (make_plan(a, &p, nullptr)) {
       err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-          &blocks, stream_mma_kernel<MP, MT, CW>, (CW + 1) * kWarp, p.smem_bytes);
+          &blocks, stream_mma_kernel<MP, MT, CW, MC>, (CW + 1) * kWarp, p.smem_bytes);
       if (err != cudaSuccess) return err;
     }
     out->registers = fa.numRegs;
