@@ -105,6 +105,17 @@ int int4gemv_w4a16_kernel(const char* kernel, void* y, const void* x, const void
                           const void* scales, const void* zeros, int64_t m, int64_t n, int64_t k,
                           int64_t group_size, void* stream);
 
+/* Fused gate / up projection (new; no counterpart in the reference): qweight, scales and zeros hold
+ * 2 * n_out rows with the gate and up rows interleaved (row 2i = gate i, row 2i + 1 = up i, see
+ * int4gemv/quant.py interleave_rows), n = 2 * n_out, and y [m, n_out] fp16 =
+ * silu(x @ gate^T) * (x @ up^T), computed from the fp32 sums and rounded once. One weight stream
+ * and one read of x for both projections. Needs the fast path's shapes (group_size 128, K a
+ * multiple of 1024, M <= 32, 16-byte aligned x, qweight, scales, zeros); INT4GEMV_ERR_INVALID
+ * with the reason otherwise. */
+int int4gemv_w4a16_silu_mul(void* y, const void* x, const void* qweight, const void* scales,
+                            const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
+                            void* stream);
+
 /* ---- Packed-format helpers on the device (int4gemv/quant.py:40-53), bit-exact ---------------- */
 
 /* q [N, K] int32 = the 4-bit values of qweight [N, K/8]   (quant.py:40-44). */

@@ -137,6 +137,20 @@ std::string w4a16_kernel(const at::Tensor& x, const at::Tensor& qweight, const a
                                     group_size);
 }
 
+at::Tensor w4a16_silu_mul(const at::Tensor& x, const at::Tensor& qweight,
+                          const at::Tensor& scales, const at::Tensor& zeros, int64_t group_size) {
+  check_inputs("w4a16_silu_mul", x, qweight, scales, zeros, group_size, c10::DeviceType::CUDA);
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t m = x.size(0), n = qweight.size(0), k = x.size(1);
+  TORCH_CHECK(n % 2 == 0, "w4a16_silu_mul: qweight must hold gate and up rows in pairs, got ", n,
+              " rows");
+  at::Tensor y = x.new_empty({m, n / 2});
+  check_status(int4gemv_w4a16_silu_mul(y.data_ptr(), x.data_ptr(), qweight.data_ptr(),
+                                       scales.data_ptr(), zeros.data_ptr(), m, n, k, group_size,
+                                       stream_of(x)));
+  return y;
+}
+
 at::Tensor unpack(const at::Tensor& qweight) {
   TORCH_CHECK(qweight.scalar_type() == at::kInt && qweight.dim() == 2 && qweight.is_contiguous() &&
                   qweight.is_cuda(),
@@ -190,6 +204,8 @@ PYBIND11_MODULE(int4gemv_ops, m) {
   m.def("w4a16", &int4gemv::w4a16, py::arg("x"), py::arg("qweight"), py::arg("scales"),
         py::arg("zeros"), py::arg("group_size"));
   m.def("w4a16_info", &int4gemv::w4a16_info, py::arg("m"));
+  m.def("w4a16_silu_mul", &int4gemv::w4a16_silu_mul, py::arg("x"), py::arg("qweight"),
+        py::arg("scales"), py::arg("zeros"), py::arg("group_size"));
   m.def("w4a16_with", &int4gemv::w4a16_with, py::arg("x"), py::arg("qweight"), py::arg("scales"),
         py::arg("zeros"), py::arg("group_size"), py::arg("kernel"));
   m.def("w4a16_kernel", &int4gemv::w4a16_kernel, py::arg("x"), py::arg("qweight"),

@@ -371,6 +371,29 @@ int int4gemv_w4a16_kernel(const char* kernel, void* y, const void* x, const void
   return fail(INT4GEMV_ERR_INVALID, "w4a16: unknown kernel '%s'", kernel);
 }
 
+int int4gemv_w4a16_silu_mul(void* y, const void* x, const void* qweight, const void* scales,
+                            const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
+                            void* stream) {
+  const char* name = "w4a16_silu_mul";
+  if (int e = check_sizes(name, m, n, k, group_size)) return e;
+  if (n % 2 != 0) {
+    return fail(INT4GEMV_ERR_INVALID, "%s: N = %lld must be even (gate and up rows interleaved)",
+                name, static_cast<long long>(n));
+  }
+  if (int e = check_pointers(name, m, n, k, y, x, qweight, scales, zeros)) return e;
+  const auto st = static_cast<cudaStream_t>(stream);
+  if (m == 0 || n == 0) return ok();
+  if (k == 0) {  // silu(0) * 0
+    const cudaError_t err = cudaMemsetAsync(y, 0, static_cast<size_t>(m * (n / 2) * 2), st);
+    return err == cudaSuccess ? ok() : cuda_fail(name, err);
+  }
+  i4::GemvArgs a = make_args(y, x, qweight, scales, zeros, m, n, k, group_size);
+  a.epilogue = i4::kSiluMul;
+  const char* why = "unsupported shape";
+  if (!i4::stream_mma_supported(a, &why)) return fail(INT4GEMV_ERR_INVALID, "%s: %s", name, why);
+  return launched(name, i4::launch_stream_mma(a, st, false));
+}
+
 int int4gemv_unpack(void* q, const void* qweight, int64_t n, int64_t k, void* stream) {
   const char* name = "unpack";
   if (n < 0 || k < 0 || k % 8 != 0) {

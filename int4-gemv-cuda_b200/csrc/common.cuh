@@ -39,6 +39,16 @@ __device__ __forceinline__ void unpack_x16(uint32_t w, uint32_t (&h)[4]) {
   asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(h[3]) : "r"(hi), "r"(0x00F000F0u), "r"(0x64006400u));
 }
 
+// One register of unpack_x16: the nibbles in bits 0..3 and 16..19 of w (high = false) as
+// (1024 + q, 1024 + q), or those in bits 4..7 and 20..23 (high = true) as (1024 + 16 q, ...).
+__device__ __forceinline__ uint32_t magic_f16(uint32_t w, bool high) {
+  uint32_t h;
+  asm("lop3.b32 %0, %1, %2, %3, 0xea;"
+      : "=r"(h)
+      : "r"(w), "r"(high ? 0x00F000F0u : 0x000F000Fu), "r"(0x64006400u));
+  return h;
+}
+
 // Same trick without the factor 16: h[j] = (1024 + q_j, 1024 + q_{j+4}) for j = 0..3.
 __device__ __forceinline__ void unpack_pairs(uint32_t w, uint32_t (&h)[4]) {
 #pragma unroll

@@ -61,6 +61,11 @@ at::Tensor w4a16_with(const at::Tensor& x, const at::Tensor& qweight, const at::
 std::string w4a16_kernel(const at::Tensor& x, const at::Tensor& qweight, const at::Tensor& scales,
                          const at::Tensor& zeros, int64_t group_size);
 
+// Fused gate / up projection: the rows of qweight, scales and zeros are gate and up rows
+// interleaved (quant.interleave_rows); returns silu(x @ gate^T) * (x @ up^T), [M, N / 2] fp16.
+at::Tensor w4a16_silu_mul(const at::Tensor& x, const at::Tensor& qweight,
+                          const at::Tensor& scales, const at::Tensor& zeros, int64_t group_size);
+
 // Bit-exact device versions of int4gemv/quant.py:40-53.
 at::Tensor unpack(const at::Tensor& qweight);
 at::Tensor dequantize(const at::Tensor& qweight, const at::Tensor& scales, const at::Tensor& zeros,

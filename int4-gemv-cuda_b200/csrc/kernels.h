@@ -9,13 +9,18 @@
 
 namespace i4 {
 
+// What the GEMV writes. kStoreY: y [m, n]. kSiluMul: the rows of W are gate and up rows
+// interleaved (row 2i = gate i, row 2i + 1 = up i) and y [m, n / 2] = silu(gate) * up.
+enum Epilogue : int { kStoreY = 0, kSiluMul = 1 };
+
 struct GemvArgs {
-  half* y;             // [m, n]
+  half* y;             // [m, n] (kSiluMul: [m, n / 2])
   const half* x;       // [m, k]
   const uint32_t* q;   // [n, k / 8]
   const half* s;       // [n, k / group]
   const half* z;       // [n, k / group]
   int m, n, k, group;
+  int epilogue = kStoreY;  // only stream_mma implements kSiluMul
 };
 
 // Attributes of one compiled kernel, for the *_info entry points.

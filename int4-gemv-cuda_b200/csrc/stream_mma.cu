@@ -439,17 +439,18 @@ __device__ __forceinline__ void narrow_mma(const NarrowRegs<MP, NR>& r, const un
       w1r0 = r.wb[j][0].y;
       w1r1 = r.wb[j][1].y;
     }
-    uint32_t u00[4], u01[4], u10[4], u11[4];
-    unpack_x16(w0r0, u00);
-    unpack_x16(w0r1, u01);
-    unpack_x16(w1r0, u10);
-    unpack_x16(w1r1, u11);
+    // The nibble unpacking of unpack_x16, one MMA operand quad at a time: the four LOP3s that make
+    // an MMA's A registers come right before it, so each lands where the MMA reads it.
+    const uint32_t lo[4] = {w0r0, w0r1, w1r0, w1r1};
+    const uint32_t hi[4] = {w0r0 >> 8, w0r1 >> 8, w1r0 >> 8, w1r1 >> 8};
     const uint4 bx0 = *reinterpret_cast<const uint4*>(xb + NarrowThread<MP, NR>::b_off(j, 0));
     const uint4 bx1 = *reinterpret_cast<const uint4*>(xb + NarrowThread<MP, NR>::b_off(j, 1));
     const int set = MP == 2 ? (j >> 1) : j;
 #pragma unroll
     for (int hh = 0; hh < 4; ++hh) {
-      const uint32_t afr[4] = {u00[hh], u01[hh], u10[hh], u11[hh]};
+      uint32_t afr[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) afr[i] = magic_f16(hh < 2 ? lo[i] : hi[i], hh & 1);
       const uint4& bx = hh < 2 ? bx0 : bx1;
       const uint32_t b0 = (hh & 1) ? bx.z : bx.x;
       const uint32_t b1 = (hh & 1) ? bx.w : bx.y;
@@ -758,9 +759,7 @@ __global__ void __maxnreg__(CW == 16 ? 96 : 168)
 
   // ---- add the partials of every output in a fixed order; store fp16 -------------------------
   named_barrier(kConsumerBarrier, kConsumerThreads);
-  for (int o = tid; o < rows * a.m; o += kConsumerThreads) {
-    const int m = o / rows;
-    const int r = o - m * rows;
+  auto row_sum = [&](int r, int m) {
     float sum = 0.0f;
     if constexpr (kNarrow) {
 #pragma unroll
@@ -771,7 +770,28 @@ __global__ void __maxnreg__(CW == 16 ? 96 : 168)
 #pragma unroll
       for (int q = 0; q < 4 * kSplit; ++q) sum += red[(q * p.rows_cap + r) * a.m + m];
     }
-    if (in.ok) a.y[static_cast<int64_t>(m) * a.n + row_begin + r] = __float2half_rn(sum);
+    return sum;
+  };
+  if (a.epilogue == kSiluMul) {
+    // Row pairs (gate 2i, up 2i + 1) never straddle CTAs: shares are whole 4-row units.
+    const int pairs = rows / 2;
+    for (int o = tid; o < pairs * a.m; o += kConsumerThreads) {
+      const int m = o / pairs;
+      const int i = o - m * pairs;
+      const float gate = row_sum(2 * i, m);
+      const float up = row_sum(2 * i + 1, m);
+      const float silu = gate / (1.0f + __expf(-gate));
+      if (in.ok) {
+        a.y[static_cast<int64_t>(m) * (a.n / 2) + row_begin / 2 + i] = __float2half_rn(silu * up);
+      }
+    }
+  } else {
+    for (int o = tid; o < rows * a.m; o += kConsumerThreads) {
+      const int m = o / rows;
+      const int r = o - m * rows;
+      const float sum = row_sum(r, m);
+      if (in.ok) a.y[static_cast<int64_t>(m) * a.n + row_begin + r] = __float2half_rn(sum);
+    }
   }
 }
 
@@ -816,6 +836,7 @@ bool make_plan(const GemvArgs& a, MmaPlan* p, const char** why) {
   if (a.m < 1 || a.m > kMaxM) return fail("M must be in [1, 32]");
   if (!weight_stream_supported(a, why)) return false;
   if (reinterpret_cast<uintptr_t>(a.x) % 16) return fail("x must be 16-byte aligned");
+  if (a.epilogue == kSiluMul && a.n % 2) return fail("gate/up rows must come in pairs (N even)");
   p->units = (a.n + 3) / 4;
   p->ctas = std::min(sm_count(), p->units);
   p->rows_cap = 4 * ((p->units + p->ctas - 1) / p->ctas);

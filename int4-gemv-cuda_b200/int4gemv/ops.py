@@ -63,6 +63,7 @@ load_only = int4gemv_ops.load_only
 w4a16 = int4gemv_ops.w4a16
 w4a16_kernel = int4gemv_ops.w4a16_kernel
 w4a16_with = int4gemv_ops.w4a16_with
+w4a16_silu_mul = int4gemv_ops.w4a16_silu_mul
 unpack = int4gemv_ops.unpack
 dequantize = int4gemv_ops.dequantize
 check_inputs = int4gemv_ops.check_inputs

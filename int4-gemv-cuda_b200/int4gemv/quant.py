@@ -61,3 +61,11 @@ def dequantize(qweight, scales, zeros, group_size: int) -> torch.Tensor:
     q = q.reshape(n, k // group_size, group_size)
     w = (q - zeros.to(torch.float32).unsqueeze(-1)) * scales.to(torch.float32).unsqueeze(-1)
     return w.reshape(n, k)
+
+
+def interleave_rows(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """Row i of gate -> row 2i, row i of up -> row 2i + 1 (any of qweight, scales, zeros): the
+    layout ops.w4a16_silu_mul reads, so one weight stream feeds both projections."""
+    if gate.shape != up.shape:
+        raise ValueError(f"gate and up shapes differ: {tuple(gate.shape)} vs {tuple(up.shape)}")
+    return torch.stack((gate, up), dim=1).reshape(2 * gate.shape[0], *gate.shape[1:]).contiguous()

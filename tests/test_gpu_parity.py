@@ -308,3 +308,33 @@ def test_matches_reference_gpu_kernels():
 def test_device_status_clean():
     from int4gemv import capi
     assert capi.device_status() == 0
+
+
+# Fused gate / up projection: silu(x @ gate^T) * (x @ up^T) from one interleaved weight stream.
+SILU = [(1, 4096, 4096), (2, 512, 1024), (4, 1000, 2048), (8, 4102, 3072), (17, 300, 1024),
+        (32, 1024, 8192), (1, 14336, 4096)]
+
+
+@pytest.mark.parametrize("m,n,k", SILU, ids=[f"m{m}_n{n}_k{k}" for m, n, k in SILU])
+def test_silu_mul(m, n, k):
+    from int4gemv import quant
+
+    x, qg, sg, zg = oracle.synthetic(m, n, k, 128, seed=5 * n + k)
+    _, qu, su, zu = oracle.synthetic(m, n, k, 128, seed=5 * n + k + 1)
+    gate = oracle.reference(x, qg, sg, zg, 128).astype(np.float64)
+    up = oracle.reference(x, qu, su, zu, 128).astype(np.float64)
+    want = gate / (1.0 + np.exp(-gate)) * up
+    q, s, z = (quant.interleave_rows(*cuda(a, b)) for a, b in ((qg, qu), (sg, su), (zg, zu)))
+    y = ops.w4a16_silu_mul(cuda(x)[0], q, s, z, 128)
+    torch.cuda.synchronize()
+    assert tuple(y.shape) == (m, n)
+    assert_close(y, want.astype(np.float32), f"silu_mul {m}x{n}x{k}")
+
+
+def test_silu_mul_rejects():
+    x, q, s, z = cuda(*oracle.synthetic(1, 6, 1024, 128))
+    with pytest.raises(RuntimeError, match="pairs"):
+        ops.w4a16_silu_mul(x, q[:5], s[:5], z[:5], 128)
+    x, q, s, z = cuda(*oracle.synthetic(1, 8, 512, 128))
+    with pytest.raises(RuntimeError, match="K must be a multiple of 1024"):
+        ops.w4a16_silu_mul(x, q, s, z, 128)

@@ -59,3 +59,13 @@ def test_reference_api(golden):
     assert_matches_reference(torch.from_numpy(golden["y_seq"]), ref)
     with pytest.raises(AssertionError):
         assert_matches_reference(torch.from_numpy(golden["y_seq"]) * 1.1 + 0.1, ref)
+
+
+def test_interleave_rows():
+    g = torch.arange(12, dtype=torch.int32).reshape(3, 4)
+    u = -g
+    r = quant.interleave_rows(g, u)
+    assert r.shape == (6, 4)
+    assert torch.equal(r[0::2], g) and torch.equal(r[1::2], u)
+    with pytest.raises(ValueError):
+        quant.interleave_rows(g, u[:2])
