@@ -309,6 +309,30 @@ def cpu_sample(ref, x_cpu, q_cpu, s_cpu, z_cpu, budget_s: float, threads: int):
 
 
 # ---------------------------------------------------------------- arms
+def time_quantize(n: int = 28672, k: int = 8192, calls: int = 20) -> dict:
+    """Device quantize (ops.quantize) of an fp16 [n, k] matrix (the sharded up projection, 470 MB,
+    larger than L2): read 2 B and write 0.5 + 4 / GROUP B per weight."""
+    from int4gemv import ops
+
+    gen = torch.Generator(device="cuda").manual_seed(7)
+    w = torch.randn(n, k, generator=gen, device="cuda", dtype=torch.float16) * 0.02
+    for _ in range(3):
+        ops.quantize(w, GROUP)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(calls):
+        ops.quantize(w, GROUP)
+    end.record()
+    end.synchronize()
+    sec = start.elapsed_time(end) / 1e3 / calls
+    moved = n * k * 2 + n * k // 2 + 2 * n * (k // GROUP) * 2
+    peak = measured_peak()
+    del w
+    return {"shape": [n, k], "dtype_in": "fp16", "us": round(sec * 1e6, 2),
+            "gb_s": round(moved / sec / 1e9, 1), "frac_of_hbm": round(moved / sec / 1e9 / peak[0], 4)}
+
+
 def run_reference_arm(args, world, rank):
     if rank != 0:
         return
@@ -457,6 +481,7 @@ def run_ours(args, world, rank, local):
         # ---- our vectorized (the reference-shaped API kernel)
         vv = [(lambda i=i: ops.vectorized(x, *sets[i], GROUP)) for i in range(n_sets)]
         extra["vectorized_us"] = round(time_graph_calls(vv * max(1, 64 // n_sets), 5000, 100) * 1e6, 3)
+        extra["quantize"] = time_quantize()
 
     # ---- end to end through the public API with host buffers
     x_host = x.cpu().pin_memory()

@@ -126,6 +126,24 @@ int int4gemv_unpack(void* q, const void* qweight, int64_t n, int64_t k, void* st
 int int4gemv_dequantize(void* w, const void* qweight, const void* scales, const void* zeros,
                         int64_t n, int64_t k, int64_t group_size, void* stream);
 
+/* Group quantisation of w [N, K] on the device, bit-exact with quant.py:14-29 (quantize) for
+ * finite weights: per group of group_size weights along K, lo = min(w, 0), hi = max(w, 0),
+ * s = fp16((hi - lo) / 15 clamped to >= 1e-6), z = clamp(round(-lo / s), 0, 15),
+ * q = clamp(round(w / s + z), 0, 15) with round half to even, then packed as by int4gemv_pack.
+ * w holds fp32, fp16 or bf16 (dtype, INT4GEMV_DTYPE_*) and must be 16-byte aligned; the reference
+ * widens w to fp32 first, which is exact for fp16 and bf16. Writes qweight [N, K/8] int32,
+ * scales and zeros [N, K/group_size] fp16. New: the reference quantises with torch on the host. */
+#define INT4GEMV_DTYPE_F32 0
+#define INT4GEMV_DTYPE_F16 1
+#define INT4GEMV_DTYPE_BF16 2
+int int4gemv_quantize(void* qweight, void* scales, void* zeros, const void* w, int dtype,
+                      int64_t n, int64_t k, int64_t group_size, void* stream);
+
+/* qweight [N, K/8] int32 from q [N, K] int32 (16-byte aligned): word = sum over j of
+ * q[8w + j] << 4j, modulo 2^32, as quant.py:32-37 (pack) computes it in int64 and casts to int32
+ * (values outside 0..15 carry into the neighbouring nibbles the same way). */
+int int4gemv_pack(void* qweight, const void* q, int64_t n, int64_t k, void* stream);
+
 /* ---- Device-side status --------------------------------------------------------------------- */
 
 /* Reads and clears the current device's kernel status word: 0 if every pipelined kernel since the

@@ -176,6 +176,38 @@ at::Tensor dequantize(const at::Tensor& qweight, const at::Tensor& scales, const
   return w;
 }
 
+std::tuple<at::Tensor, at::Tensor, at::Tensor> quantize(const at::Tensor& w, int64_t group_size) {
+  TORCH_CHECK(w.dim() == 2 && w.is_cuda() && w.is_contiguous(),
+              "quantize: expected a contiguous 2-D CUDA tensor w");
+  int dtype;
+  switch (w.scalar_type()) {
+    case at::kFloat: dtype = INT4GEMV_DTYPE_F32; break;
+    case at::kHalf: dtype = INT4GEMV_DTYPE_F16; break;
+    case at::kBFloat16: dtype = INT4GEMV_DTYPE_BF16; break;
+    default: TORCH_CHECK(false, "quantize: w must be float32, float16 or bfloat16, got ", w.scalar_type());
+  }
+  const int64_t n = w.size(0), k = w.size(1);
+  TORCH_CHECK(group_size > 0 && group_size % 8 == 0 && k % group_size == 0, "quantize: group_size ",
+              group_size, " must be a positive multiple of 8 dividing K = ", k);
+  const c10::cuda::CUDAGuard guard(w.device());
+  at::Tensor qweight = at::empty({n, k / 8}, w.options().dtype(at::kInt));
+  at::Tensor scales = at::empty({n, k / group_size}, w.options().dtype(at::kHalf));
+  at::Tensor zeros = at::empty({n, k / group_size}, w.options().dtype(at::kHalf));
+  check_status(int4gemv_quantize(qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(),
+                                 w.data_ptr(), dtype, n, k, group_size, stream_of(w)));
+  return {qweight, scales, zeros};
+}
+
+at::Tensor pack(const at::Tensor& q) {
+  TORCH_CHECK(q.scalar_type() == at::kInt && q.dim() == 2 && q.is_contiguous() && q.is_cuda(),
+              "pack: expected a contiguous 2-D int32 CUDA q");
+  TORCH_CHECK(q.size(1) % 8 == 0, "pack: K = ", q.size(1), " must be a multiple of 8");
+  const c10::cuda::CUDAGuard guard(q.device());
+  at::Tensor qweight = q.new_empty({q.size(0), q.size(1) / 8});
+  check_status(int4gemv_pack(qweight.data_ptr(), q.data_ptr(), q.size(0), q.size(1), stream_of(q)));
+  return qweight;
+}
+
 }  // namespace int4gemv
 
 PYBIND11_MODULE(int4gemv_ops, m) {
@@ -213,6 +245,8 @@ PYBIND11_MODULE(int4gemv_ops, m) {
   m.def("unpack", &int4gemv::unpack, py::arg("qweight"));
   m.def("dequantize", &int4gemv::dequantize, py::arg("qweight"), py::arg("scales"),
         py::arg("zeros"), py::arg("group_size"));
+  m.def("quantize", &int4gemv::quantize, py::arg("w"), py::arg("group_size") = 128);
+  m.def("pack", &int4gemv::pack, py::arg("q"));
   m.def(
       "check_inputs",
       [](const char* name, const at::Tensor& x, const at::Tensor& qweight,

@@ -423,6 +423,38 @@ int int4gemv_dequantize(void* w, const void* qweight, const void* scales, const 
                                               n, k, group_size, static_cast<cudaStream_t>(stream)));
 }
 
+int int4gemv_quantize(void* qweight, void* scales, void* zeros, const void* w, int dtype,
+                      int64_t n, int64_t k, int64_t group_size, void* stream) {
+  const char* name = "quantize";
+  if (dtype != INT4GEMV_DTYPE_F32 && dtype != INT4GEMV_DTYPE_F16 && dtype != INT4GEMV_DTYPE_BF16) {
+    return fail(INT4GEMV_ERR_INVALID, "quantize: unknown weight dtype %d", dtype);
+  }
+  if (int e = check_sizes(name, 0, n, k, group_size)) return e;
+  if (n == 0 || k == 0) return ok();
+  if (!qweight || !scales || !zeros || !w) return fail(INT4GEMV_ERR_INVALID, "quantize: null pointer");
+  if (reinterpret_cast<uintptr_t>(w) % 16 != 0) {
+    return fail(INT4GEMV_ERR_INVALID, "quantize: w must be 16-byte aligned");
+  }
+  return launched(name, i4::launch_quantize(static_cast<uint32_t*>(qweight), static_cast<half*>(scales),
+                                            static_cast<half*>(zeros), w, dtype, n, k, group_size,
+                                            static_cast<cudaStream_t>(stream)));
+}
+
+int int4gemv_pack(void* qweight, const void* q, int64_t n, int64_t k, void* stream) {
+  const char* name = "pack";
+  if (n < 0 || k < 0 || k % 8 != 0) {
+    return fail(INT4GEMV_ERR_INVALID, "pack: N = %lld, K = %lld: K must be a non-negative multiple of 8",
+                static_cast<long long>(n), static_cast<long long>(k));
+  }
+  if (n == 0 || k == 0) return ok();
+  if (!q || !qweight) return fail(INT4GEMV_ERR_INVALID, "pack: null pointer");
+  if (reinterpret_cast<uintptr_t>(q) % 16 != 0) {
+    return fail(INT4GEMV_ERR_INVALID, "pack: q must be 16-byte aligned");
+  }
+  return launched(name, i4::launch_pack(static_cast<uint32_t*>(qweight), static_cast<const int32_t*>(q), n,
+                                        k, static_cast<cudaStream_t>(stream)));
+}
+
 int int4gemv_device_status(int* status) {
   if (!status) return fail(INT4GEMV_ERR_INVALID, "device_status: null argument");
   const cudaError_t err = i4::read_and_clear_status(status);

@@ -16,6 +16,7 @@
 #include <cstdint>
 #include <map>
 #include <string>
+#include <tuple>
 
 namespace int4gemv {
 
@@ -70,5 +71,10 @@ at::Tensor w4a16_silu_mul(const at::Tensor& x, const at::Tensor& qweight,
 at::Tensor unpack(const at::Tensor& qweight);
 at::Tensor dequantize(const at::Tensor& qweight, const at::Tensor& scales, const at::Tensor& zeros,
                       int64_t group_size);
+
+// Bit-exact device versions of int4gemv/quant.py:14-37 for finite weights: w [N, K] fp32, fp16
+// or bf16 (CUDA, contiguous) -> (qweight, scales, zeros); q [N, K] int32 -> qweight.
+std::tuple<at::Tensor, at::Tensor, at::Tensor> quantize(const at::Tensor& w, int64_t group_size);
+at::Tensor pack(const at::Tensor& q);
 
 }  // namespace int4gemv

@@ -72,6 +72,13 @@ cudaError_t launch_unpack(int32_t* q, const uint32_t* qweight, int64_t n, int64_
 cudaError_t launch_dequantize(float* w, const uint32_t* qweight, const half* s, const half* z,
                               int64_t n, int64_t k, int64_t group, cudaStream_t stream);
 
+// Group quantisation and packing (quantize.cu). The weight element types quantize reads.
+enum WeightType : int { kWeightF32 = 0, kWeightF16 = 1, kWeightBF16 = 2 };
+cudaError_t launch_quantize(uint32_t* qweight, half* scales, half* zeros, const void* w,
+                            int dtype, int64_t n, int64_t k, int64_t group, cudaStream_t stream);
+cudaError_t launch_pack(uint32_t* qweight, const int32_t* q, int64_t n, int64_t k,
+                        cudaStream_t stream);
+
 // SM count of the current device (cached per device).
 int sm_count();
 

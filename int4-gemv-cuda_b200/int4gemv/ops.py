@@ -2,8 +2,8 @@
 
 Drop-in for the reference's int4gemv.ops (int4gemv/ops.py:11-36 of Yu-TingLee/int4-GEMV-cuda):
 the same names (sequential, naive, coalesced, vectorized, load_only), the same KERNELS and
-KERNEL_INFO tables, plus the B200 fast path `w4a16` and the bit-exact device `unpack` /
-`dequantize`. As in the reference, INT4GEMV_BUILD_DIR may point at another build directory (its
+KERNEL_INFO tables, plus the B200 fast path `w4a16`, the fused `w4a16_silu_mul` and the bit-exact
+device `quantize` / `pack` / `unpack` / `dequantize`. As in the reference, INT4GEMV_BUILD_DIR may point at another build directory (its
 `python/` subdirectory or the directory itself is searched).
 
 There is no fallback: if the compiled module is missing this import fails and says how to build.
@@ -66,6 +66,8 @@ w4a16_with = int4gemv_ops.w4a16_with
 w4a16_silu_mul = int4gemv_ops.w4a16_silu_mul
 unpack = int4gemv_ops.unpack
 dequantize = int4gemv_ops.dequantize
+quantize = int4gemv_ops.quantize
+pack = int4gemv_ops.pack
 check_inputs = int4gemv_ops.check_inputs
 
 # The GEMV kernels, slowest first. All share the 5-argument signature of csrc/w4a16.h.

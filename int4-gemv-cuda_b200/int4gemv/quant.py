@@ -21,9 +21,19 @@ def bits_per_weight(group_size: int = GROUP_SIZE) -> float:
 
 
 def quantize(w: torch.Tensor, group_size: int = GROUP_SIZE):
-    """w [N, K] -> (qweight [N, K/8] int32, scales [N, K/g] fp16, zeros [N, K/g] fp16)."""
+    """w [N, K] -> (qweight [N, K/8] int32, scales [N, K/g] fp16, zeros [N, K/g] fp16).
+
+    A CUDA tensor is quantised on its device by the compiled kernel (ops.quantize), which reads
+    fp32, fp16 and bf16 as they are; other dtypes are widened to fp32 first, as the reference does.
+    """
     n, k = w.shape
     assert k % group_size == 0 and group_size % 8 == 0, (k, group_size)
+    if w.is_cuda:
+        from . import ops
+
+        if w.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+            w = w.float()
+        return ops.quantize(w.contiguous(), group_size)
     groups = w.float().reshape(n, k // group_size, group_size)
     lo, hi = torch.aminmax(groups, dim=-1, keepdim=True)
     lo = torch.clamp(lo, max=0.0)
@@ -36,13 +46,17 @@ def quantize(w: torch.Tensor, group_size: int = GROUP_SIZE):
 
 
 def pack(q: torch.Tensor) -> torch.Tensor:
-    """q [N, K] of values 0..15 -> [N, K/8] int32, lowest nibble = lowest k."""
+    """q [N, K] of values 0..15 -> [N, K/8] int32, lowest nibble = lowest k.
+
+    word = sum_j q[8w + j] << 4j modulo 2^32, like the reference's int64 sum and int32 cast: values
+    outside 0..15 are not masked and carry into the neighbouring nibbles."""
     n, k = q.shape
-    nib = (q.to(torch.int64) & 0xF).reshape(n, k // 8, 8)
+    parts = q.to(torch.int64).reshape(n, k // 8, 8)
     word = torch.zeros(n, k // 8, dtype=torch.int64, device=q.device)
     for j, shift in enumerate(_NIBBLE_SHIFTS):
-        word |= nib[..., j] << shift
-    # int32 has no unsigned form in torch: reinterpret the 32-bit pattern
+        word += parts[..., j] << shift
+    # keep the low 32 bits, then reinterpret them as int32 (torch has no uint32 arithmetic)
+    word = word & 0xFFFFFFFF
     word = torch.where(word >= 2**31, word - 2**32, word)
     return word.to(torch.int32)
 

@@ -60,13 +60,15 @@ void oracle_unpack(const int32_t* qweight, int32_t* q, int64_t n, int64_t k) {
   }
 }
 
-/* quant.py:32-37: the inverse of unpack; values are masked to 4 bits. */
+/* quant.py:32-37: word = sum over j of q[8w + j] << 4j, computed there in int64 and cast to int32,
+ * i.e. modulo 2^32. Values outside 0..15 are not masked: they carry into the neighbouring
+ * nibbles exactly as in the reference. For 0..15 this is the inverse of unpack. */
 void oracle_pack(const int32_t* q, int32_t* qweight, int64_t n, int64_t k) {
   const int64_t words = k / 8;
   for (int64_t r = 0; r < n; ++r) {
     for (int64_t w = 0; w < words; ++w) {
-      uint32_t word = 0;
-      for (int j = 0; j < 8; ++j) word |= ((uint32_t)q[r * k + 8 * w + j] & 0xFu) << (4 * j);
+      uint32_t word = 0; /* unsigned arithmetic wraps modulo 2^32 */
+      for (int j = 0; j < 8; ++j) word += (uint32_t)q[r * k + 8 * w + j] << (4 * j);
       qweight[r * words + w] = (int32_t)word;
     }
   }

@@ -21,7 +21,8 @@ def pytest_configure(config):
 
 
 def golden_names() -> list[str]:
-    return sorted(p.stem for p in GOLDEN.glob("*.npz"))
+    """The GEMV / quantize cases (pack_wrap.npz holds only pack vectors)."""
+    return sorted(p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith("pack_"))
 
 
 def load_golden(name: str) -> dict:
@@ -34,3 +35,9 @@ def golden(request):
     case = load_golden(request.param)
     case["name"] = request.param
     return case
+
+
+@pytest.fixture
+def pack_wrap():
+    """int32 q [6, 128] with values inside and outside 0..15, and the reference's pack of it."""
+    return load_golden("pack_wrap")

@@ -10,6 +10,7 @@ For every case it records what the reference produces:
   y_ref                    int4gemv/reference.py:8-10 (torch fp32 dequantise-then-matmul)
   y_seq                    csrc/sequential.cpp:11-54, the reference's compiled CPU path
                            (oracle/_ref, built by oracle/build_ref.py)
+  pack_wrap.npz            int4gemv/quant.py:32-37 (pack) on int32 values inside and outside 0..15
 The tests then pin the C oracle (oracle/w4a16_oracle.c) to these, and the CUDA kernels to both.
 Nothing on the GPU box reads the reference: only these .npz files travel.
 """
@@ -108,6 +109,14 @@ def main() -> None:
         record(name, w, m, g, keep_w, 2000 + i)
     record("quant_edges_g128", edge_weights(), 2, 128, True, 3000)
     record("quant_edges_g32", edge_weights(), 1, 32, True, 3001)
+
+    # pack on values outside 0..15 (quant.py:32-37 sums q << 4j in int64, then casts to int32)
+    gen = torch.Generator().manual_seed(4000)
+    q = torch.randint(-40, 60, (6, 128), generator=gen, dtype=torch.int32)
+    q[0, :8] = torch.tensor([2**31 - 1, -2**31, 15, 15, 15, 15, 15, 15], dtype=torch.int32)
+    q[1] = torch.randint(0, 16, (128,), generator=gen, dtype=torch.int32)
+    np.savez_compressed(HERE / "pack_wrap.npz", q=q.numpy(), qweight=ref_quant.pack(q).numpy())
+    print("pack_wrap", tuple(q.shape))
 
 
 if __name__ == "__main__":

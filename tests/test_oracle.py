@@ -33,6 +33,10 @@ def test_unpack_pack_round_trip(golden):
     np.testing.assert_array_equal(oracle.pack(q), golden["qweight"])
 
 
+def test_pack_wraps_like_reference(pack_wrap):
+    np.testing.assert_array_equal(oracle.pack(pack_wrap["q"]), pack_wrap["qweight"])
+
+
 def test_dequantize_bit_exact(golden):
     if "deq" not in golden:
         pytest.skip("case stores no dequantized weights")

@@ -39,6 +39,11 @@ def test_unpack_pack(golden):
     assert torch.equal(quant.pack(q), qw)
 
 
+def test_pack_wraps_like_reference(pack_wrap):
+    assert torch.equal(quant.pack(torch.from_numpy(pack_wrap["q"])),
+                       torch.from_numpy(pack_wrap["qweight"]))
+
+
 def test_pack_sign_bit_words():
     q = torch.full((2, 16), 15, dtype=torch.int32)
     packed = quant.pack(q)
