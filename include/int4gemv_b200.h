@@ -116,6 +116,16 @@ int int4gemv_w4a16_silu_mul(void* y, const void* x, const void* qweight, const v
                             const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
                             void* stream);
 
+/* y [M, N] = x @ W^T + bias + residual with both additions fused into the GEMV's store: the fp32
+ * row sum plus bias[n] plus residual[m, n], rounded to fp16 once. bias ([N] fp16) and residual
+ * ([M, N] fp16) may each be NULL; residual may be y itself (in-place residual add). Same kernel
+ * choice and checks as int4gemv_w4a16; with K = 0, y = bias + residual. New: the reference has no
+ * fused epilogue (a caller adds bias and residual with separate elementwise kernels). */
+int int4gemv_w4a16_bias_residual(void* y, const void* x, const void* qweight, const void* scales,
+                                 const void* zeros, const void* bias, const void* residual,
+                                 int64_t m, int64_t n, int64_t k, int64_t group_size,
+                                 void* stream);
+
 /* ---- Packed-format helpers on the device (int4gemv/quant.py:40-53), bit-exact ---------------- */
 
 /* q [N, K] int32 = the 4-bit values of qweight [N, K/8]   (quant.py:40-44). */

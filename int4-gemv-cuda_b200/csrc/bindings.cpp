@@ -151,6 +151,37 @@ at::Tensor w4a16_silu_mul(const at::Tensor& x, const at::Tensor& qweight,
   return y;
 }
 
+at::Tensor w4a16_bias_residual(const at::Tensor& x, const at::Tensor& qweight,
+                               const at::Tensor& scales, const at::Tensor& zeros,
+                               int64_t group_size, const c10::optional<at::Tensor>& bias,
+                               const c10::optional<at::Tensor>& residual) {
+  check_inputs("w4a16_bias_residual", x, qweight, scales, zeros, group_size, c10::DeviceType::CUDA);
+  const int64_t m = x.size(0), n = qweight.size(0), k = x.size(1);
+  const void* bias_ptr = nullptr;
+  const void* res_ptr = nullptr;
+  if (bias.has_value()) {
+    const at::Tensor& b = *bias;
+    TORCH_CHECK(b.scalar_type() == at::kHalf && b.dim() == 1 && b.size(0) == n && b.is_contiguous() &&
+                    b.device() == x.device(),
+                "w4a16_bias_residual: bias must be a contiguous float16 [", n, "] tensor on x's device");
+    bias_ptr = b.data_ptr();
+  }
+  if (residual.has_value()) {
+    const at::Tensor& r = *residual;
+    TORCH_CHECK(r.scalar_type() == at::kHalf && r.dim() == 2 && r.size(0) == m && r.size(1) == n &&
+                    r.is_contiguous() && r.device() == x.device(),
+                "w4a16_bias_residual: residual must be a contiguous float16 [", m, ", ", n,
+                "] tensor on x's device");
+    res_ptr = r.data_ptr();
+  }
+  const c10::cuda::CUDAGuard guard(x.device());
+  at::Tensor y = x.new_empty({m, n});
+  check_status(int4gemv_w4a16_bias_residual(y.data_ptr(), x.data_ptr(), qweight.data_ptr(),
+                                            scales.data_ptr(), zeros.data_ptr(), bias_ptr, res_ptr,
+                                            m, n, k, group_size, stream_of(x)));
+  return y;
+}
+
 at::Tensor unpack(const at::Tensor& qweight) {
   TORCH_CHECK(qweight.scalar_type() == at::kInt && qweight.dim() == 2 && qweight.is_contiguous() &&
                   qweight.is_cuda(),
@@ -242,6 +273,9 @@ PYBIND11_MODULE(int4gemv_ops, m) {
         py::arg("zeros"), py::arg("group_size"), py::arg("kernel"));
   m.def("w4a16_kernel", &int4gemv::w4a16_kernel, py::arg("x"), py::arg("qweight"),
         py::arg("scales"), py::arg("zeros"), py::arg("group_size"));
+  m.def("w4a16_bias_residual", &int4gemv::w4a16_bias_residual, py::arg("x"), py::arg("qweight"),
+        py::arg("scales"), py::arg("zeros"), py::arg("group_size"), py::arg("bias") = py::none(),
+        py::arg("residual") = py::none());
   m.def("unpack", &int4gemv::unpack, py::arg("qweight"));
   m.def("dequantize", &int4gemv::dequantize, py::arg("qweight"), py::arg("scales"),
         py::arg("zeros"), py::arg("group_size"));

@@ -156,6 +156,22 @@ Pick pick_kernel(const i4::GemvArgs& a) {
   return Pick::kCoalesced;
 }
 
+// Launches the kernel pick_kernel chooses for `a` (the dispatch of int4gemv_w4a16).
+int run_picked(const char* name, const i4::GemvArgs& a, cudaStream_t st) {
+  switch (pick_kernel(a)) {
+    case Pick::kStreamMma:
+      return launched(name, i4::launch_stream_mma(a, st, false));
+    case Pick::kTcgen05:
+      return launched(name, i4::launch_tc_gemv(a, st, false));
+    case Pick::kMmaPipeline:
+      return launched(name, i4::launch_mma_pipeline(a, st));
+    case Pick::kVectorized:
+      return launched(name, i4::launch_vectorized(a, 128, 2, st));
+    default:
+      return launched(name, i4::launch_coalesced(a, st));
+  }
+}
+
 }  // namespace
 
 extern "C" {
@@ -300,19 +316,23 @@ int int4gemv_w4a16(void* y, const void* x, const void* qweight, const void* scal
   const auto st = static_cast<cudaStream_t>(stream);
   int e = empty_cases(name, y, m, n, k, st, &done);
   if (done) return e;
-  const i4::GemvArgs a = make_args(y, x, qweight, scales, zeros, m, n, k, group_size);
-  switch (pick_kernel(a)) {
-    case Pick::kStreamMma:
-      return launched(name, i4::launch_stream_mma(a, st, false));
-    case Pick::kTcgen05:
-      return launched(name, i4::launch_tc_gemv(a, st, false));
-    case Pick::kMmaPipeline:
-      return launched(name, i4::launch_mma_pipeline(a, st));
-    case Pick::kVectorized:
-      return launched(name, i4::launch_vectorized(a, 128, 2, st));
-    default:
-      return launched(name, i4::launch_coalesced(a, st));
-  }
+  return run_picked(name, make_args(y, x, qweight, scales, zeros, m, n, k, group_size), st);
+}
+
+int int4gemv_w4a16_bias_residual(void* y, const void* x, const void* qweight, const void* scales,
+                                 const void* zeros, const void* bias, const void* residual,
+                                 int64_t m, int64_t n, int64_t k, int64_t group_size,
+                                 void* stream) {
+  const char* name = "w4a16_bias_residual";
+  if (int e = check_sizes(name, m, n, k, group_size)) return e;
+  if (int e = check_pointers(name, m, n, k, y, x, qweight, scales, zeros)) return e;
+  const auto st = static_cast<cudaStream_t>(stream);
+  if (m == 0 || n == 0) return ok();
+  i4::GemvArgs a = make_args(y, x, qweight, scales, zeros, m, n, k, group_size);
+  a.bias = static_cast<const half*>(bias);
+  a.residual = static_cast<const half*>(residual);
+  if (k == 0) return launched(name, i4::launch_bias_residual(a, st));  // y = bias + residual
+  return run_picked(name, a, st);
 }
 
 const char* int4gemv_w4a16_kernel_name(const void* x, const void* qweight, const void* scales,

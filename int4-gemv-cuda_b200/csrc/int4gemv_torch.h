@@ -12,6 +12,7 @@
 
 #include <ATen/core/Tensor.h>
 #include <c10/core/DeviceType.h>
+#include <c10/util/Optional.h>
 
 #include <cstdint>
 #include <map>
@@ -66,6 +67,13 @@ std::string w4a16_kernel(const at::Tensor& x, const at::Tensor& qweight, const a
 // interleaved (quant.interleave_rows); returns silu(x @ gate^T) * (x @ up^T), [M, N / 2] fp16.
 at::Tensor w4a16_silu_mul(const at::Tensor& x, const at::Tensor& qweight,
                           const at::Tensor& scales, const at::Tensor& zeros, int64_t group_size);
+
+// x @ W^T + bias + residual with both additions fused into the GEMV's store (each optional;
+// bias [N], residual [M, N], float16), rounded to fp16 once.
+at::Tensor w4a16_bias_residual(const at::Tensor& x, const at::Tensor& qweight,
+                               const at::Tensor& scales, const at::Tensor& zeros,
+                               int64_t group_size, const c10::optional<at::Tensor>& bias,
+                               const c10::optional<at::Tensor>& residual);
 
 // Bit-exact device versions of int4gemv/quant.py:40-53.
 at::Tensor unpack(const at::Tensor& qweight);

@@ -21,7 +21,20 @@ struct GemvArgs {
   const half* z;       // [n, k / group]
   int m, n, k, group;
   int epilogue = kStoreY;  // only stream_mma implements kSiluMul
+  // kStoreY only, each optional: y[m, r] = sum + bias[r] + residual[m, r], rounded to fp16 once.
+  // residual may be y itself (each output is read and written by the same thread).
+  const half* bias = nullptr;      // [n]
+  const half* residual = nullptr;  // [m, n]
 };
+
+#if defined(__CUDACC__)
+// The fp16 value a GEMV kernel stores for output (m, r) of row sum `sum` (kStoreY).
+__device__ __forceinline__ half store_value(const GemvArgs& a, int m, int r, float sum) {
+  if (a.bias) sum += __half2float(a.bias[r]);
+  if (a.residual) sum += __half2float(a.residual[static_cast<int64_t>(m) * a.n + r]);
+  return __float2half_rn(sum);
+}
+#endif
 
 // Attributes of one compiled kernel, for the *_info entry points.
 struct KernelAttrs {
@@ -71,6 +84,8 @@ cudaError_t launch_unpack(int32_t* q, const uint32_t* qweight, int64_t n, int64_
                           cudaStream_t stream);
 cudaError_t launch_dequantize(float* w, const uint32_t* qweight, const half* s, const half* z,
                               int64_t n, int64_t k, int64_t group, cudaStream_t stream);
+// y = bias + residual (the K = 0 case of a GEMV with a bias / residual epilogue).
+cudaError_t launch_bias_residual(const GemvArgs& a, cudaStream_t stream);
 
 // Group quantisation and packing (quantize.cu). The weight element types quantize reads.
 enum WeightType : int { kWeightF32 = 0, kWeightF16 = 1, kWeightBF16 = 2 };

@@ -319,7 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1) mma_pipeline_kernel(GemvArgs a, P
         for (int w = t; w < kConsumerWarps; w += T) {
           sum += red[((w * kWarp + src_lane) * NT + nt) * 4 + i];
         }
-        a.y[static_cast<int64_t>(mcol) * a.n + c0 + r] = __float2half_rn(sum);
+        a.y[static_cast<int64_t>(mcol) * a.n + c0 + r] = store_value(a, mcol, c0 + r, sum);
       }
     }
     named_barrier(kConsumerBarrier, kConsumerThreads);

@@ -2,6 +2,7 @@
 //   unpack      q[n, 8w + j] = (qweight[n, w] >> 4j) & 0xF              (quant.py:40-44)
 //   dequantize  w = (float(q) - float(z)) * float(s), one IEEE rounding
 //               per operation, no FMA contraction                        (quant.py:47-53)
+// Plus y = bias + residual, the K = 0 case of the fused bias / residual GEMV epilogue.
 // One thread per packed word; the word's eight outputs are written as two 16-byte (unpack) or
 // two 32-byte (dequantize) vectors. Grid-stride loops sized to a multiple of the SM count.
 #include "common.cuh"
@@ -43,6 +44,16 @@ __global__ void dequantize_kernel(float4* __restrict__ out, const uint32_t* __re
   }
 }
 
+__global__ void bias_residual_kernel(GemvArgs a) {
+  const int64_t total = static_cast<int64_t>(a.m) * a.n;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int m = static_cast<int>(i / a.n);
+    const int r = static_cast<int>(i - static_cast<int64_t>(m) * a.n);
+    a.y[i] = store_value(a, m, r, 0.0f);
+  }
+}
+
 int grid_for(int64_t items) {
   const int64_t blocks = (items + kThreads - 1) / kThreads;
   const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
@@ -67,6 +78,13 @@ cudaError_t launch_dequantize(float* w, const uint32_t* qweight, const half* s, 
   dequantize_kernel<<<grid_for(words), kThreads, 0, stream>>>(reinterpret_cast<float4*>(w),
                                                                qweight, s, z, words, k / 8,
                                                                k / group, group / 8);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bias_residual(const GemvArgs& a, cudaStream_t stream) {
+  const int64_t total = static_cast<int64_t>(a.m) * a.n;
+  if (total == 0) return cudaSuccess;
+  bias_residual_kernel<<<grid_for(total), kThreads, 0, stream>>>(a);
   return cudaGetLastError();
 }
 

@@ -31,11 +31,13 @@ __device__ __forceinline__ void tile_rows(const half* (&rows)[TM], const half* x
 }
 
 template <int TM>
-__device__ __forceinline__ void store_tile(half* y, const float (&acc)[TM], int m, int n, int m0,
+__device__ __forceinline__ void store_tile(const GemvArgs& a, const float (&acc)[TM], int m0,
                                            int row) {
 #pragma unroll
   for (int i = 0; i < TM; ++i) {
-    if (m0 + i < m) y[static_cast<int64_t>(m0 + i) * n + row] = __float2half_rn(acc[i]);
+    if (m0 + i < a.m) {
+      a.y[static_cast<int64_t>(m0 + i) * a.n + row] = store_value(a, m0 + i, row, acc[i]);
+    }
   }
 }
 
@@ -69,7 +71,7 @@ __global__ void __launch_bounds__(kNaiveThreads) naive_kernel(GemvArgs a) {
       }
     }
   }
-  store_tile(a.y, acc, a.m, a.n, m0, row);
+  store_tile(a, acc, m0, row);
 }
 
 // ---- coalesced: warp per row, lanes stride the row's words -------------------------------------
@@ -103,7 +105,7 @@ __global__ void __launch_bounds__(kCoalescedWarps * kWarp) coalesced_kernel(Gemv
   }
 #pragma unroll
   for (int i = 0; i < TM; ++i) acc[i] = warp_sum(acc[i]);
-  if (lane == 0) store_tile(a.y, acc, a.m, a.n, m0, row);
+  if (lane == 0) store_tile(a, acc, m0, row);
 }
 
 // ---- vectorized: RPW rows per warp, lane-strided 16-byte chunks of 32 weights ------------------
@@ -195,7 +197,7 @@ __global__ void vectorized_kernel(GemvArgs a) {
   if (lane == 0) {
 #pragma unroll
     for (int r = 0; r < RPW; ++r) {
-      if (row0 + r < a.n) store_tile(a.y, acc[r], a.m, a.n, m0, row0 + r);
+      if (row0 + r < a.n) store_tile(a, acc[r], m0, row0 + r);
     }
   }
 }

@@ -790,7 +790,9 @@ __global__ void __maxnreg__(CW == 16 ? 96 : 168)
       const int m = o / rows;
       const int r = o - m * rows;
       const float sum = row_sum(r, m);
-      if (in.ok) a.y[static_cast<int64_t>(m) * a.n + row_begin + r] = __float2half_rn(sum);
+      if (in.ok) {
+        a.y[static_cast<int64_t>(m) * a.n + row_begin + r] = store_value(a, m, row_begin + r, sum);
+      }
     }
   }
 }

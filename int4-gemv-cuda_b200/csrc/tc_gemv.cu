@@ -421,7 +421,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     float sum = 0.0f;
 #pragma unroll
     for (int q = 0; q < 4; ++q) sum += red[(q * p.rows_cap + r) * MT + m];
-    if (ok) a.y[static_cast<int64_t>(m) * a.n + row_begin + r] = __float2half_rn(sum);
+    if (ok) {
+      a.y[static_cast<int64_t>(m) * a.n + row_begin + r] = store_value(a, m, row_begin + r, sum);
+    }
   }
   if (warp == 0) {
     tc_fence_after();

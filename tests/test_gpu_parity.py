@@ -338,3 +338,64 @@ def test_silu_mul_rejects():
     x, q, s, z = cuda(*oracle.synthetic(1, 8, 512, 128))
     with pytest.raises(RuntimeError, match="K must be a multiple of 1024"):
         ops.w4a16_silu_mul(x, q, s, z, 128)
+
+
+# Fused bias / residual epilogue: y = x @ W^T + bias + residual, rounded to fp16 once, on every
+# kernel the dispatcher can pick (the shapes below reach stream_mma, mma_pipeline, vectorized and
+# coalesced).
+BIAS = [(1, 8192, 8192, 128, "stream_mma"), (5, 300, 1024, 128, "stream_mma"),
+        (3, 257, 768, 64, "mma_pipeline"), (2, 100, 640, 128, "vectorized"),
+        (4, 77, 96, 16, "coalesced")]
+
+
+@pytest.mark.parametrize("m,n,k,g,kernel", BIAS, ids=[f"{b[4]}_m{b[0]}_n{b[1]}" for b in BIAS])
+@pytest.mark.parametrize("with_bias,with_res", [(True, True), (True, False), (False, True)])
+def test_bias_residual(m, n, k, g, kernel, with_bias, with_res):
+    x, q, s, z = oracle.synthetic(m, n, k, g, seed=n + k + g)
+    rng = np.random.default_rng(m * n)
+    bias = rng.standard_normal(n).astype(np.float16)
+    res = rng.standard_normal((m, n)).astype(np.float16)
+    want = oracle.reference(x, q, s, z, g).astype(np.float64)
+    if with_bias:
+        want = want + bias.astype(np.float64)
+    if with_res:
+        want = want + res.astype(np.float64)
+    args = cuda(x, q, s, z)
+    assert ops.w4a16_kernel(*args, g) == kernel
+    tb, tr = cuda(bias, res)
+    y = ops.w4a16_bias_residual(*args, g, bias=tb if with_bias else None,
+                                residual=tr if with_res else None)
+    torch.cuda.synchronize()
+    assert_close(y, want.astype(np.float32), f"{kernel} bias={with_bias} residual={with_res}")
+
+
+def test_bias_residual_in_place_and_empty():
+    """residual may be y itself (through the C ABI); K = 0 gives bias + residual; M = 0 is empty."""
+    from int4gemv import capi
+
+    m, n, k = 2, 4096, 4096
+    x, q, s, z = oracle.synthetic(m, n, k, 128, seed=9)
+    rng = np.random.default_rng(9)
+    bias = rng.standard_normal(n).astype(np.float16)
+    res = rng.standard_normal((m, n)).astype(np.float16)
+    tx, tq, ts, tz, tb, ty = cuda(x, q, s, z, bias, res)
+    stream = torch.cuda.current_stream().cuda_stream
+    capi.call("int4gemv_w4a16_bias_residual", ty.data_ptr(), tx.data_ptr(), tq.data_ptr(),
+              ts.data_ptr(), tz.data_ptr(), tb.data_ptr(), ty.data_ptr(), m, n, k, 128, stream)
+    torch.cuda.synchronize()
+    want = oracle.reference(x, q, s, z, 128).astype(np.float64) + bias + res.astype(np.float64)
+    assert_close(ty, want.astype(np.float32), "in place")
+
+    x0 = torch.empty(m, 0, dtype=torch.float16, device="cuda")
+    q0 = torch.empty(n, 0, dtype=torch.int32, device="cuda")
+    s0 = torch.empty(n, 0, dtype=torch.float16, device="cuda")
+    tr = cuda(res)[0]
+    y = ops.w4a16_bias_residual(x0, q0, s0, s0, 128, bias=tb, residual=tr)
+    torch.cuda.synchronize()
+    want0 = (bias.astype(np.float32) + res.astype(np.float32)).astype(np.float16)
+    np.testing.assert_array_equal(y.cpu().numpy().view(np.uint16), want0.view(np.uint16))
+    assert ops.w4a16_bias_residual(tx[:0], tq, ts, tz, 128, bias=tb).shape == (0, n)
+    with pytest.raises(RuntimeError, match="bias must be"):
+        ops.w4a16_bias_residual(tx, tq, ts, tz, 128, bias=tb[:-1])
+    with pytest.raises(RuntimeError, match="residual must be"):
+        ops.w4a16_bias_residual(tx, tq, ts, tz, 128, residual=tr.t())
