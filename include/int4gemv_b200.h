@@ -154,6 +154,24 @@ int int4gemv_quantize(void* qweight, void* scales, void* zeros, const void* w, i
  * (values outside 0..15 carry into the neighbouring nibbles the same way). */
 int int4gemv_pack(void* qweight, const void* q, int64_t n, int64_t k, void* stream);
 
+/* ---- Checkpoint repacking (new: the reference reads only unquantised fp16 / bf16 weights) ---- */
+
+/* AWQ checkpoint tensors -> qweight [N, K/8] int32, scales and zeros [N, K/group_size] fp16.
+ * awq_qweight [K, N/8] int32 and awq_qzeros [K/group_size, N/8] int32 hold column 8c + j of word
+ * c in nibble (j % 2) * 4 + j / 2 (AutoAWQ's order 0 2 4 6 1 3 5 7); awq_scales [K/group_size, N]
+ * fp16. Exact bit movement; N must be a multiple of 8. All pointers are device addresses. */
+int int4gemv_repack_awq(void* qweight, void* scales, void* zeros, const void* awq_qweight,
+                        const void* awq_qzeros, const void* awq_scales, int64_t n, int64_t k,
+                        int64_t group_size, void* stream);
+
+/* GPTQ checkpoint tensors -> the same outputs. gptq_qweight [K/8, N] int32 holds weight 8r + i of
+ * column n in nibble i of word (r, n); gptq_qzeros [K/group_size, N/8] int32 holds column 8c + i in
+ * nibble i, stored as z - zero_offset (1 for the original "gptq" format, 0 for "gptq_v2");
+ * gptq_scales [K/group_size, N] fp16. Groups must be contiguous (no act-order g_idx). */
+int int4gemv_repack_gptq(void* qweight, void* scales, void* zeros, const void* gptq_qweight,
+                         const void* gptq_qzeros, const void* gptq_scales, int zero_offset,
+                         int64_t n, int64_t k, int64_t group_size, void* stream);
+
 /* ---- Device-side status --------------------------------------------------------------------- */
 
 /* Reads and clears the current device's kernel status word: 0 if every pipelined kernel since the

@@ -35,7 +35,7 @@ NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++20", "-Xcompiler", "-fPIC",
                      f"-I{INCLUDE}", f"-I{CSRC}"]
 CU_SOURCES = [
     "capi.cu", "simt.cu", "mma_pipeline.cu", "tc_gemv.cu", "stream_mma.cu", "weight_stream.cu",
-    "packed.cu", "quantize.cu",
+    "packed.cu", "quantize.cu", "repack.cu",
 ]
 # The CPU path must keep one IEEE rounding per operation: no contraction, no fast-math.
 CPU_SOURCES = {"sequential.cpp": ["-O3", "-ffp-contract=off", "-fno-fast-math"]}

@@ -239,6 +239,67 @@ at::Tensor pack(const at::Tensor& q) {
   return qweight;
 }
 
+namespace {
+void check_ck(const char* name, const at::Tensor& t, at::ScalarType dtype, int64_t rows,
+              int64_t cols, const char* what, const at::Tensor& like) {
+  TORCH_CHECK(t.scalar_type() == dtype && t.dim() == 2 && t.size(0) == rows && t.size(1) == cols &&
+                  t.is_contiguous() && t.device() == like.device(),
+              name, ": ", what, " must be a contiguous ", c10::toString(dtype), " [", rows, ", ", cols,
+              "] tensor on the device of qweight, got ", t.scalar_type(), " ", t.sizes());
+}
+
+std::tuple<at::Tensor, at::Tensor, at::Tensor> repack_outputs(const at::Tensor& like, int64_t n,
+                                                              int64_t k, int64_t group_size) {
+  return {at::empty({n, k / 8}, like.options().dtype(at::kInt)),
+          at::empty({n, k / group_size}, like.options().dtype(at::kHalf)),
+          at::empty({n, k / group_size}, like.options().dtype(at::kHalf))};
+}
+}  // namespace
+
+std::tuple<at::Tensor, at::Tensor, at::Tensor> repack_awq(const at::Tensor& qweight,
+                                                         const at::Tensor& qzeros,
+                                                         const at::Tensor& scales,
+                                                         int64_t group_size) {
+  const char* name = "repack_awq";
+  TORCH_CHECK(qweight.dim() == 2 && qweight.is_cuda(), name, ": qweight must be a 2-D CUDA tensor");
+  TORCH_CHECK(group_size > 0 && qweight.size(0) % group_size == 0, name, ": group_size ",
+              group_size, " must divide K = ", qweight.size(0));
+  const int64_t k = qweight.size(0), n = qweight.size(1) * 8;
+  check_ck(name, qweight, at::kInt, k, n / 8, "qweight", qweight);
+  check_ck(name, qzeros, at::kInt, k / group_size, n / 8, "qzeros", qweight);
+  check_ck(name, scales, at::kHalf, k / group_size, n, "scales", qweight);
+  const c10::cuda::CUDAGuard guard(qweight.device());
+  auto out = repack_outputs(qweight, n, k, group_size);
+  check_status(int4gemv_repack_awq(std::get<0>(out).data_ptr(), std::get<1>(out).data_ptr(),
+                                   std::get<2>(out).data_ptr(), qweight.data_ptr(),
+                                   qzeros.data_ptr(), scales.data_ptr(), n, k, group_size,
+                                   stream_of(qweight)));
+  return out;
+}
+
+std::tuple<at::Tensor, at::Tensor, at::Tensor> repack_gptq(const at::Tensor& qweight,
+                                                          const at::Tensor& qzeros,
+                                                          const at::Tensor& scales,
+                                                          int64_t group_size, int64_t zero_offset) {
+  const char* name = "repack_gptq";
+  TORCH_CHECK(qweight.dim() == 2 && qweight.is_cuda(), name, ": qweight must be a 2-D CUDA tensor");
+  const int64_t k = qweight.size(0) * 8, n = qweight.size(1);
+  TORCH_CHECK(group_size > 0 && k % group_size == 0, name, ": group_size ", group_size,
+              " must divide K = ", k);
+  TORCH_CHECK(n % 8 == 0, name, ": N = ", n, " must be a multiple of 8 (packed zero points)");
+  check_ck(name, qweight, at::kInt, k / 8, n, "qweight", qweight);
+  check_ck(name, qzeros, at::kInt, k / group_size, n / 8, "qzeros", qweight);
+  check_ck(name, scales, at::kHalf, k / group_size, n, "scales", qweight);
+  const c10::cuda::CUDAGuard guard(qweight.device());
+  auto out = repack_outputs(qweight, n, k, group_size);
+  check_status(int4gemv_repack_gptq(std::get<0>(out).data_ptr(), std::get<1>(out).data_ptr(),
+                                    std::get<2>(out).data_ptr(), qweight.data_ptr(),
+                                    qzeros.data_ptr(), scales.data_ptr(),
+                                    static_cast<int>(zero_offset), n, k, group_size,
+                                    stream_of(qweight)));
+  return out;
+}
+
 }  // namespace int4gemv
 
 PYBIND11_MODULE(int4gemv_ops, m) {
@@ -280,6 +341,10 @@ PYBIND11_MODULE(int4gemv_ops, m) {
   m.def("dequantize", &int4gemv::dequantize, py::arg("qweight"), py::arg("scales"),
         py::arg("zeros"), py::arg("group_size"));
   m.def("quantize", &int4gemv::quantize, py::arg("w"), py::arg("group_size") = 128);
+  m.def("repack_awq", &int4gemv::repack_awq, py::arg("qweight"), py::arg("qzeros"),
+        py::arg("scales"), py::arg("group_size"));
+  m.def("repack_gptq", &int4gemv::repack_gptq, py::arg("qweight"), py::arg("qzeros"),
+        py::arg("scales"), py::arg("group_size"), py::arg("zero_offset") = 1);
   m.def("pack", &int4gemv::pack, py::arg("q"));
   m.def(
       "check_inputs",

@@ -475,6 +475,44 @@ int int4gemv_pack(void* qweight, const void* q, int64_t n, int64_t k, void* stre
                                         k, static_cast<cudaStream_t>(stream)));
 }
 
+namespace {
+int repack(const char* name, bool awq, void* qweight, void* scales, void* zeros,
+           const void* ck_qweight, const void* ck_qzeros, const void* ck_scales, int zero_offset,
+           int64_t n, int64_t k, int64_t group_size, void* stream) {
+  if (int e = check_sizes(name, 0, n, k, group_size)) return e;
+  if (n % 8 != 0) {
+    return fail(INT4GEMV_ERR_INVALID, "%s: N = %lld must be a multiple of 8 (packed zero points)",
+                name, static_cast<long long>(n));
+  }
+  if (zero_offset < 0 || zero_offset > 1) {
+    return fail(INT4GEMV_ERR_INVALID, "%s: zero_offset %d must be 0 or 1", name, zero_offset);
+  }
+  if (n == 0 || k == 0) return ok();
+  if (!qweight || !scales || !zeros || !ck_qweight || !ck_qzeros || !ck_scales) {
+    return fail(INT4GEMV_ERR_INVALID, "%s: null pointer", name);
+  }
+  return launched(name, i4::launch_repack(awq, static_cast<uint32_t*>(qweight), static_cast<half*>(scales),
+                                          static_cast<half*>(zeros), static_cast<const uint32_t*>(ck_qweight),
+                                          static_cast<const uint32_t*>(ck_qzeros),
+                                          static_cast<const half*>(ck_scales), n, k, group_size,
+                                          zero_offset, static_cast<cudaStream_t>(stream)));
+}
+}  // namespace
+
+int int4gemv_repack_awq(void* qweight, void* scales, void* zeros, const void* awq_qweight,
+                        const void* awq_qzeros, const void* awq_scales, int64_t n, int64_t k,
+                        int64_t group_size, void* stream) {
+  return repack("repack_awq", true, qweight, scales, zeros, awq_qweight, awq_qzeros, awq_scales, 0,
+                n, k, group_size, stream);
+}
+
+int int4gemv_repack_gptq(void* qweight, void* scales, void* zeros, const void* gptq_qweight,
+                         const void* gptq_qzeros, const void* gptq_scales, int zero_offset,
+                         int64_t n, int64_t k, int64_t group_size, void* stream) {
+  return repack("repack_gptq", false, qweight, scales, zeros, gptq_qweight, gptq_qzeros,
+                gptq_scales, zero_offset, n, k, group_size, stream);
+}
+
 int int4gemv_device_status(int* status) {
   if (!status) return fail(INT4GEMV_ERR_INVALID, "device_status: null argument");
   const cudaError_t err = i4::read_and_clear_status(status);

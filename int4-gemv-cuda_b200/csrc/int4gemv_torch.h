@@ -85,4 +85,15 @@ at::Tensor dequantize(const at::Tensor& qweight, const at::Tensor& scales, const
 std::tuple<at::Tensor, at::Tensor, at::Tensor> quantize(const at::Tensor& w, int64_t group_size);
 at::Tensor pack(const at::Tensor& q);
 
+// AWQ / GPTQ checkpoint tensors (CUDA, contiguous) -> (qweight, scales, zeros) of this layout.
+// zero_offset: 1 for GPTQ's original format (stored z - 1), 0 for gptq_v2.
+std::tuple<at::Tensor, at::Tensor, at::Tensor> repack_awq(const at::Tensor& qweight,
+                                                         const at::Tensor& qzeros,
+                                                         const at::Tensor& scales,
+                                                         int64_t group_size);
+std::tuple<at::Tensor, at::Tensor, at::Tensor> repack_gptq(const at::Tensor& qweight,
+                                                          const at::Tensor& qzeros,
+                                                          const at::Tensor& scales,
+                                                          int64_t group_size, int64_t zero_offset);
+
 }  // namespace int4gemv

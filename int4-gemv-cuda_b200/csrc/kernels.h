@@ -94,6 +94,13 @@ cudaError_t launch_quantize(uint32_t* qweight, half* scales, half* zeros, const 
 cudaError_t launch_pack(uint32_t* qweight, const int32_t* q, int64_t n, int64_t k,
                         cudaStream_t stream);
 
+// AWQ / GPTQ checkpoint tensors -> this layout (repack.cu). awq selects the AWQ layout, else
+// GPTQ's; zero_offset is added to every stored zero point (1 for GPTQ's "gptq" format).
+cudaError_t launch_repack(bool awq, uint32_t* qweight, half* scales, half* zeros,
+                          const uint32_t* ck_qweight, const uint32_t* ck_qzeros,
+                          const half* ck_scales, int64_t n, int64_t k, int64_t group,
+                          int zero_offset, cudaStream_t stream);
+
 // SM count of the current device (cached per device).
 int sm_count();
 

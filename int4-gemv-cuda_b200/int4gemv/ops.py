@@ -70,6 +70,8 @@ unpack = int4gemv_ops.unpack
 dequantize = int4gemv_ops.dequantize
 quantize = int4gemv_ops.quantize
 pack = int4gemv_ops.pack
+repack_awq = int4gemv_ops.repack_awq
+repack_gptq = int4gemv_ops.repack_gptq
 check_inputs = int4gemv_ops.check_inputs
 
 # The GEMV kernels, slowest first. All share the 5-argument signature of csrc/w4a16.h.

@@ -9,6 +9,12 @@ Each function names the reference code it restates (paths inside Yu-TingLee/int4
   reference                               int4gemv/reference.py:8-10 (double accumulation)
   assert_matches_reference                int4gemv/reference.py:13-22 (the tolerance rule)
 
+Checkpoint formats (not in the reference, whose quant.py:5 only names them): AWQ and GPTQ 4-bit
+tensors and their conversion to the reference's layout, restated from the published packers
+(AutoAWQ's GEMM layout, order 0 2 4 6 1 3 5 7; AutoGPTQ's QuantLinear.pack, which stores zeros
+minus one; as implemented by vLLM 0.22 quantization/utils/quant_utils.py awq_pack / gptq_pack /
+pack_cols, which tests/golden/make_checkpoint_golden.py runs to pin these functions).
+
 Arrays are numpy: x float16 [M, K], qweight int32 [N, K/8], scales / zeros float16 [N, K/g].
 """
 
@@ -178,3 +184,74 @@ def synthetic(m: int, n: int, k: int, group_size: int = GROUP_SIZE, seed: int = 
     x = rng.standard_normal((m, k), dtype=np.float32).astype(np.float16)
     qweight, scales, zeros = quantize(w, group_size)
     return x, qweight, scales, zeros
+
+
+# ---------------------------------------------------------------- AWQ / GPTQ checkpoint formats
+AWQ_ORDER = np.array([0, 2, 4, 6, 1, 3, 5, 7])  # nibble i of an AWQ word holds column AWQ_ORDER[i]
+GPTQ_ZERO_OFFSET = {"gptq": 1, "gptq_v2": 0}
+
+
+def _nibbles(words: np.ndarray) -> np.ndarray:
+    """int32 [..., W] -> int32 [..., W, 8], element i = nibble i (bits 4i .. 4i + 3)."""
+    u = words.astype(np.uint32)[..., None] >> (np.arange(8, dtype=np.uint32) * 4)
+    return (u & 0xF).astype(np.int32)
+
+
+def _pack_nibbles(nib: np.ndarray) -> np.ndarray:
+    """int [..., W, 8] of 0..15 -> int32 [..., W], element i in nibble i."""
+    words = (nib.astype(np.uint32) << (np.arange(8, dtype=np.uint32) * 4)).sum(-1, dtype=np.uint64)
+    return (words & 0xFFFFFFFF).astype(np.uint32).view(np.int32)
+
+
+def awq_unpack(words: np.ndarray) -> np.ndarray:
+    """AWQ-packed [R, C/8] -> values [R, C] by column (column AWQ_ORDER[i] <- nibble i)."""
+    nib = _nibbles(words)
+    cols = np.empty_like(nib)
+    cols[..., AWQ_ORDER] = nib
+    return cols.reshape(words.shape[0], -1)
+
+
+def awq_pack(values: np.ndarray) -> np.ndarray:
+    """values [R, C] (0..15) -> AWQ-packed [R, C/8]."""
+    r, c = values.shape
+    return _pack_nibbles(values.reshape(r, c // 8, 8)[..., AWQ_ORDER])
+
+
+def awq_to_packed(qweight, qzeros, scales, group_size: int = GROUP_SIZE):
+    """AWQ (qweight [K, N/8], qzeros [K/g, N/8], scales [K/g, N]) -> (qweight [N, K/8] int32,
+    scales [N, K/g] float16, zeros [N, K/g] float16) of the reference's layout."""
+    q = awq_unpack(np.asarray(qweight))  # [K, N]
+    z = awq_unpack(np.asarray(qzeros))   # [K/g, N]
+    return (pack(np.ascontiguousarray(q.T)), np.ascontiguousarray(np.asarray(scales).T),
+            np.ascontiguousarray(z.T).astype(np.float16))
+
+
+def packed_to_awq(qweight, scales, zeros):
+    """The inverse of awq_to_packed for integer zeros 0..15."""
+    q = unpack(qweight)  # [N, K]
+    return (awq_pack(np.ascontiguousarray(q.T)),
+            awq_pack(np.ascontiguousarray(zeros.T).astype(np.int32)),
+            np.ascontiguousarray(np.asarray(scales).T))
+
+
+def gptq_to_packed(qweight, qzeros, scales, group_size: int = GROUP_SIZE,
+                   checkpoint_format: str = "gptq"):
+    """GPTQ (qweight [K/8, N] packed along K, qzeros [K/g, N/8] packed along N in order and stored
+    minus GPTQ_ZERO_OFFSET[format], scales [K/g, N]) -> the reference's layout."""
+    qweight = np.asarray(qweight)
+    nib = _nibbles(qweight)                                   # [K/8, N, 8]: q[8r + i, n]
+    q = nib.transpose(0, 2, 1).reshape(-1, qweight.shape[1])  # [K, N]
+    z = _nibbles(np.asarray(qzeros)).reshape(qzeros.shape[0], -1) + GPTQ_ZERO_OFFSET[
+        checkpoint_format]
+    return (pack(np.ascontiguousarray(q.T)), np.ascontiguousarray(np.asarray(scales).T),
+            np.ascontiguousarray(z.T).astype(np.float16))
+
+
+def packed_to_gptq(qweight, scales, zeros, checkpoint_format: str = "gptq"):
+    """The inverse of gptq_to_packed for integer zeros (0..15 for "gptq_v2", 1..16 for "gptq")."""
+    q = unpack(qweight).T                                      # [K, N]
+    k, n = q.shape
+    qw = _pack_nibbles(q.reshape(k // 8, 8, n).transpose(0, 2, 1))
+    zs = np.ascontiguousarray(zeros.T).astype(np.int32) - GPTQ_ZERO_OFFSET[checkpoint_format]
+    qz = _pack_nibbles((zs & 0xF).reshape(zs.shape[0], -1, 8))
+    return qw, qz, np.ascontiguousarray(np.asarray(scales).T)

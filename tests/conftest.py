@@ -20,9 +20,13 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200); run with -m gpu")
 
 
-def golden_names() -> list[str]:
-    """The GEMV / quantize cases (pack_wrap.npz holds only pack vectors)."""
-    return sorted(p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith("pack_"))
+def golden_names(prefix: str | None = None) -> list[str]:
+    """prefix None: the GEMV / quantize cases; else the files named prefix* (pack_wrap.npz holds
+    only pack vectors, checkpoint_*.npz AWQ / GPTQ tensors)."""
+    names = sorted(p.stem for p in GOLDEN.glob("*.npz"))
+    if prefix is None:
+        return [n for n in names if not n.startswith(("pack_", "checkpoint_"))]
+    return [n for n in names if n.startswith(prefix)]
 
 
 def load_golden(name: str) -> dict:
@@ -41,3 +45,11 @@ def golden(request):
 def pack_wrap():
     """int32 q [6, 128] with values inside and outside 0..15, and the reference's pack of it."""
     return load_golden("pack_wrap")
+
+
+@pytest.fixture(params=golden_names("checkpoint_"))
+def checkpoint(request):
+    """The reference's packed weights and the same weights as AWQ / GPTQ checkpoint tensors."""
+    case = load_golden(request.param)
+    case["name"] = request.param
+    return case
