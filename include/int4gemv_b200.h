@@ -21,6 +21,7 @@
 #ifndef INT4GEMV_B200_H_
 #define INT4GEMV_B200_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -171,6 +172,54 @@ int int4gemv_repack_awq(void* qweight, void* scales, void* zeros, const void* aw
 int int4gemv_repack_gptq(void* qweight, void* scales, void* zeros, const void* gptq_qweight,
                          const void* gptq_qzeros, const void* gptq_scales, int zero_offset,
                          int64_t n, int64_t k, int64_t group_size, void* stream);
+
+/* ---- Sharded layers with the exchange fused into the GEMV (new: the reference is single-GPU) -- */
+
+/* One process per GPU of a node. Each rank allocates its exchange buffers with
+ * int4gemv_peer_alloc (zeroed device memory plus a CUDA IPC handle of INT4GEMV_IPC_HANDLE_BYTES),
+ * sends the handle to the other ranks (any host channel) and maps theirs with int4gemv_peer_open.
+ * Release with int4gemv_peer_close (mapped peers' buffers) and int4gemv_peer_free (own). */
+#define INT4GEMV_IPC_HANDLE_BYTES 64
+int int4gemv_peer_alloc(int64_t bytes, void** ptr, void* ipc_handle);
+int int4gemv_peer_open(const void* ipc_handle, void** ptr);
+int int4gemv_peer_close(void* ptr);
+int int4gemv_peer_free(void* ptr);
+
+#define INT4GEMV_MAX_PEERS 8
+#define INT4GEMV_SHARD_ROWS 0          /* N split: every rank gets y [m, n_total] (all-gather) */
+#define INT4GEMV_SHARD_K 1             /* K split: every rank gets y [m, n] = sum of partials */
+#define INT4GEMV_PEER_FLAG_STRIDE 1024 /* flag words per source rank */
+
+typedef struct {
+  int32_t world, rank, mode;
+  uint32_t epoch;   /* 1, 2, 3, ...: one more on every call, the same on every rank */
+  int64_t n_total;  /* ROWS: columns of the gathered y */
+  int64_t col0;     /* ROWS: first column of this rank's shard in y */
+  /* out[r]: rank r's buffer, mapped here (out[rank] is this rank's own). ROWS: y [m, n_total]
+   * fp16. K: receive buffer [world, m, n] fp32. Buffers for consecutive calls must alternate
+   * (two per rank): a rank may run one call ahead of the others. */
+  void* out[INT4GEMV_MAX_PEERS];
+  /* flags[r]: rank r's flag words, world * INT4GEMV_PEER_FLAG_STRIDE uint32, zeroed once at
+   * allocation and never reset (each call's epoch is larger than the last). */
+  void* flags[INT4GEMV_MAX_PEERS];
+} int4gemv_peers_t;
+
+/* sizeof(int4gemv_peers_t), for bindings that build the struct themselves. */
+size_t int4gemv_peers_struct_bytes(void);
+
+/* The GEMV of this rank's shard with the exchange fused into its epilogue, on the fast path's
+ * shapes (group_size 128, K % 1024 == 0, M <= 32). ROWS: the shard's rows are columns
+ * [col0, col0 + n) of y; each CTA writes its outputs into every rank's y over NVLink (peer
+ * stores), publishes a flag on every rank and waits for its counterparts' flags, so when the
+ * kernel completes this rank's y [m, n_total] is whole. y is unused. K: each CTA writes its fp32
+ * partial sums into every rank's receive buffer, waits likewise, and writes y [m, n] fp16 = the
+ * ranks' partials added in rank order (bit-identical on every rank). Every rank must make the same
+ * sequence of calls with the same m, n, k (so each launches the same CTAs). A wait on a peer is
+ * bounded (2 s); when it runs out the kernel records INT4GEMV status 3 (int4gemv_device_status)
+ * and finishes with an undefined result. */
+int int4gemv_w4a16_exchange(void* y, const void* x, const void* qweight, const void* scales,
+                            const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
+                            const int4gemv_peers_t* peers, void* stream);
 
 /* ---- Device-side status --------------------------------------------------------------------- */
 

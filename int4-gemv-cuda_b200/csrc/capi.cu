@@ -513,6 +513,97 @@ int int4gemv_repack_gptq(void* qweight, void* scales, void* zeros, const void* g
                 gptq_scales, zero_offset, n, k, group_size, stream);
 }
 
+static_assert(INT4GEMV_MAX_PEERS == i4::kMaxPeers, "peer count");
+static_assert(INT4GEMV_PEER_FLAG_STRIDE == i4::kPeerFlagStride, "flag stride");
+
+size_t int4gemv_peers_struct_bytes(void) { return sizeof(int4gemv_peers_t); }
+
+int int4gemv_peer_alloc(int64_t bytes, void** ptr, void* ipc_handle) {
+  if (bytes <= 0 || !ptr || !ipc_handle) return fail(INT4GEMV_ERR_INVALID, "peer_alloc: bad argument");
+  void* p = nullptr;
+  cudaError_t err = cudaMalloc(&p, static_cast<size_t>(bytes));
+  if (err != cudaSuccess) return cuda_fail("peer_alloc", err);
+  err = cudaMemset(p, 0, static_cast<size_t>(bytes));
+  cudaIpcMemHandle_t h;
+  if (err == cudaSuccess) err = cudaIpcGetMemHandle(&h, p);
+  if (err != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail("peer_alloc", err);
+  }
+  static_assert(sizeof(h) == INT4GEMV_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  *ptr = p;
+  return ok();
+}
+
+int int4gemv_peer_open(const void* ipc_handle, void** ptr) {
+  if (!ipc_handle || !ptr) return fail(INT4GEMV_ERR_INVALID, "peer_open: null argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  const cudaError_t err = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  return err == cudaSuccess ? ok() : cuda_fail("peer_open", err);
+}
+
+int int4gemv_peer_close(void* ptr) {
+  const cudaError_t err = cudaIpcCloseMemHandle(ptr);
+  return err == cudaSuccess ? ok() : cuda_fail("peer_close", err);
+}
+
+int int4gemv_peer_free(void* ptr) {
+  const cudaError_t err = cudaFree(ptr);
+  return err == cudaSuccess ? ok() : cuda_fail("peer_free", err);
+}
+
+int int4gemv_w4a16_exchange(void* y, const void* x, const void* qweight, const void* scales,
+                            const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
+                            const int4gemv_peers_t* peers, void* stream) {
+  const char* name = "w4a16_exchange";
+  if (!peers) return fail(INT4GEMV_ERR_INVALID, "%s: null peers", name);
+  const int mode = peers->mode;
+  if (mode != INT4GEMV_SHARD_ROWS && mode != INT4GEMV_SHARD_K) {
+    return fail(INT4GEMV_ERR_INVALID, "%s: unknown mode %d", name, mode);
+  }
+  if (peers->world < 1 || peers->world > INT4GEMV_MAX_PEERS || peers->rank < 0 ||
+      peers->rank >= peers->world) {
+    return fail(INT4GEMV_ERR_INVALID, "%s: rank %d of world %d (at most %d ranks)", name,
+                peers->rank, peers->world, INT4GEMV_MAX_PEERS);
+  }
+  for (int r = 0; r < peers->world; ++r) {
+    if (!peers->out[r] || !peers->flags[r]) {
+      return fail(INT4GEMV_ERR_INVALID, "%s: null buffer of rank %d", name, r);
+    }
+  }
+  if (int e = check_sizes(name, m, n, k, group_size)) return e;
+  if (m == 0 || n == 0 || k == 0) {
+    return fail(INT4GEMV_ERR_INVALID, "%s: M, N and K must be positive", name);
+  }
+  if (int e = check_pointers(name, m, n, k, mode == INT4GEMV_SHARD_K ? y : x, x, qweight, scales,
+                             zeros)) {
+    return e;
+  }
+  if (mode == INT4GEMV_SHARD_ROWS &&
+      (peers->col0 < 0 || peers->n_total > INT_MAX || peers->col0 + n > peers->n_total)) {
+    return fail(INT4GEMV_ERR_INVALID, "%s: columns [%lld, %lld) outside y's %lld", name,
+                static_cast<long long>(peers->col0), static_cast<long long>(peers->col0 + n),
+                static_cast<long long>(peers->n_total));
+  }
+  i4::GemvArgs a = make_args(y, x, qweight, scales, zeros, m, n, k, group_size);
+  a.epilogue = mode == INT4GEMV_SHARD_ROWS ? i4::kGatherPeers : i4::kReducePeers;
+  const char* why = "unsupported shape";
+  if (!i4::stream_mma_supported(a, &why)) return fail(INT4GEMV_ERR_INVALID, "%s: %s", name, why);
+  i4::PeerSet ps{};
+  for (int r = 0; r < peers->world; ++r) {
+    ps.out[r] = peers->out[r];
+    ps.flags[r] = static_cast<unsigned*>(peers->flags[r]);
+  }
+  ps.world = peers->world;
+  ps.rank = peers->rank;
+  ps.epoch = peers->epoch;
+  ps.n_total = static_cast<int>(peers->n_total);
+  ps.col0 = static_cast<int>(peers->col0);
+  return launched(name, i4::launch_stream_mma(a, static_cast<cudaStream_t>(stream), false, &ps));
+}
+
 int int4gemv_device_status(int* status) {
   if (!status) return fail(INT4GEMV_ERR_INVALID, "device_status: null argument");
   const cudaError_t err = i4::read_and_clear_status(status);

@@ -14,6 +14,7 @@ constexpr int kWarp = 32;
 // Status codes a kernel writes to the device status word when a bounded wait gives up.
 constexpr int kStatusFullBarrierTimeout = 1;
 constexpr int kStatusEmptyBarrierTimeout = 2;
+constexpr int kStatusPeerTimeout = 3;  // a peer rank's flag did not arrive within the limit
 
 // About one second at B200 clocks. A correct pipeline never waits more than microseconds.
 constexpr long long kWaitLimitCycles = 2000000000LL;
@@ -127,6 +128,35 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   const long long start = clock64();
   while (!mbar_try_wait(bar, parity)) {
     if (clock64() - start > kWaitLimitCycles) return false;
+  }
+  return true;
+}
+
+// ---- flags between ranks (peer memory over NVLink) ----------------------------------------------
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Waits until *flag has reached `epoch` (modulo 2^32), at most `limit_ns` nanoseconds.
+__device__ __forceinline__ bool wait_flag_bounded(const unsigned* flag, unsigned epoch,
+                                                  unsigned long long limit_ns) {
+  if (static_cast<int>(ld_acquire_sys(flag) - epoch) >= 0) return true;
+  const unsigned long long start = global_ns();
+  while (static_cast<int>(ld_acquire_sys(flag) - epoch) < 0) {
+    if (global_ns() - start > limit_ns) return false;
+    __nanosleep(100);
   }
   return true;
 }

@@ -11,7 +11,29 @@ namespace i4 {
 
 // What the GEMV writes. kStoreY: y [m, n]. kSiluMul: the rows of W are gate and up rows
 // interleaved (row 2i = gate i, row 2i + 1 = up i) and y [m, n / 2] = silu(gate) * up.
-enum Epilogue : int { kStoreY = 0, kSiluMul = 1 };
+// kGatherPeers / kReducePeers: the fused exchange of a layer sharded over the ranks of one node
+// (PeerSet below): rows split (every rank's y gets this rank's columns) or K split (every rank
+// gets this rank's fp32 partial sums, then each adds all ranks' partials in rank order).
+enum Epilogue : int { kStoreY = 0, kSiluMul = 1, kGatherPeers = 2, kReducePeers = 3 };
+
+constexpr int kMaxPeers = 8;
+constexpr int kPeerFlagStride = 1024;  // flag words per source rank (>= CTAs of any launch)
+constexpr unsigned long long kPeerWaitNs = 2000000000ull;  // limit of one wait on a peer's flag
+
+// Peer pointers of one exchange call. out[r] and flags[r] are rank r's buffers, mapped into this
+// process (out[rank] and flags[rank] are this rank's own). kGatherPeers: out[r] = rank r's y
+// [m, n_total] fp16, this rank writes columns [col0, col0 + n). kReducePeers: out[r] = rank r's
+// receive buffer [world, m, n] fp32, this rank writes slot `rank`. flags[r] = world *
+// kPeerFlagStride words; this rank's CTA c sets word rank * kPeerFlagStride + c of every rank to
+// `epoch` after its stores, and waits for word r * kPeerFlagStride + c of its own flags, for
+// every r.
+struct PeerSet {
+  void* out[kMaxPeers];
+  unsigned* flags[kMaxPeers];
+  int world, rank;
+  unsigned epoch;
+  int n_total, col0;
+};
 
 struct GemvArgs {
   half* y;             // [m, n] (kSiluMul: [m, n / 2])
@@ -67,7 +89,8 @@ cudaError_t tc_gemv_attrs(int m, KernelAttrs* out);
 // TMA-tile-fed mma.sync GEMV for M <= 32, group 128 (stream_mma.cu): the fast path. Launched
 // with programmatic stream serialization like launch_tc_gemv.
 bool stream_mma_supported(const GemvArgs& a, const char** why);
-cudaError_t launch_stream_mma(const GemvArgs& a, cudaStream_t stream, bool strict);
+cudaError_t launch_stream_mma(const GemvArgs& a, cudaStream_t stream, bool strict,
+                              const PeerSet* peers = nullptr);
 cudaError_t stream_mma_attrs(int m, KernelAttrs* out);
 
 // TMA-bulk-fed mma.sync pipeline (mma_pipeline.cu). `why` gets a reason when unsupported.

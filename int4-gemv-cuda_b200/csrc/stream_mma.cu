@@ -593,13 +593,36 @@ __device__ __forceinline__ void wide_stage(const unsigned char* st, const unsign
   }
 }
 
+// The consumers' half of a peer exchange, after each has issued its stores into the ranks'
+// buffers: every thread fences its own stores at system scope, the CTA synchronises, one thread
+// publishes this CTA's flag (`epoch`, release) on every rank, and threads 0 .. world - 1 each wait
+// (acquire, bounded) for the flag of this CTA's counterpart on one rank. Then the CTA
+// synchronises again, so its threads may read what the other ranks wrote. A wait that runs out
+// records kStatusPeerTimeout and stops waiting.
+template <int kConsumerThreads>
+__device__ __forceinline__ void exchange_flags(const PeerSet& peers, int* status, int tid) {
+  __threadfence_system();
+  named_barrier(kConsumerBarrier, kConsumerThreads);
+  if (tid == 0) {
+    for (int q = 0; q < peers.world; ++q) {
+      st_release_sys(peers.flags[q] + peers.rank * kPeerFlagStride + blockIdx.x, peers.epoch);
+    }
+  }
+  if (tid < peers.world) {
+    const unsigned* f = peers.flags[peers.rank] + tid * kPeerFlagStride + blockIdx.x;
+    if (!wait_flag_bounded(f, peers.epoch, kPeerWaitNs)) atomicExch(status, kStatusPeerTimeout);
+  }
+  named_barrier(kConsumerBarrier, kConsumerThreads);
+}
+
 // MP: M rounded up to 2 or 4 (narrow path) or 8 (wide path, MT tiles of 8 rows of x). MC: M when
 // the instance serves a single M (else 0: read at run time). CW: consumer warps, 8 or 16. With 16 (17 warps, at most 5 per SM sub-partition) a thread may use
 // 96 registers, so the sub-partition's 16384 registers hold them; with 8 (3 per sub-partition),
 // 168. Measured on B200: M = 1 is fastest with 8 consumer warps, 2 <= M <= 8 with 16.
 template <int MP, int MT, int CW, int MC>
 __global__ void __maxnreg__(CW == 16 ? 96 : 168)
-    stream_mma_kernel(GemvArgs a, MmaPlan p, const __grid_constant__ WeightMaps maps) {
+    stream_mma_kernel(GemvArgs a, MmaPlan p, const __grid_constant__ WeightMaps maps,
+                      const __grid_constant__ PeerSet peers) {
   constexpr bool kNarrow = MP < 8;
   const int m_rows = MC > 0 ? MC : a.m;  // rows of x: compile-time where the instance has one M
   constexpr int kCW = CW;
@@ -785,6 +808,42 @@ __global__ void __maxnreg__(CW == 16 ? 96 : 168)
         a.y[static_cast<int64_t>(m) * (a.n / 2) + row_begin / 2 + i] = __float2half_rn(silu * up);
       }
     }
+  } else if (a.epilogue == kGatherPeers) {
+    // This rank's columns of y, written into every rank's y (this one's included).
+    for (int o = tid; o < rows * a.m; o += kConsumerThreads) {
+      const int m = o / rows;
+      const int r = o - m * rows;
+      const half h = __float2half_rn(row_sum(r, m));
+      const int64_t at = static_cast<int64_t>(m) * peers.n_total + peers.col0 + row_begin + r;
+      if (in.ok) {
+        for (int q = 0; q < peers.world; ++q) static_cast<half*>(peers.out[q])[at] = h;
+      }
+    }
+    exchange_flags<kConsumerThreads>(peers, p.status, tid);
+  } else if (a.epilogue == kReducePeers) {
+    // This rank's fp32 partial sums into slot `rank` of every rank's receive buffer; then, once
+    // every rank's partials for these rows are in, their sum in rank order (the same on every
+    // rank, so all ranks hold bit-identical y).
+    const int64_t slot = static_cast<int64_t>(a.m) * a.n;
+    for (int o = tid; o < rows * a.m; o += kConsumerThreads) {
+      const int m = o / rows;
+      const int r = o - m * rows;
+      const float sum = row_sum(r, m);
+      const int64_t at = peers.rank * slot + static_cast<int64_t>(m) * a.n + row_begin + r;
+      if (in.ok) {
+        for (int q = 0; q < peers.world; ++q) static_cast<float*>(peers.out[q])[at] = sum;
+      }
+    }
+    exchange_flags<kConsumerThreads>(peers, p.status, tid);
+    const float* mine = static_cast<const float*>(peers.out[peers.rank]);
+    for (int o = tid; o < rows * a.m; o += kConsumerThreads) {
+      const int m = o / rows;
+      const int r = o - m * rows;
+      const int64_t at = static_cast<int64_t>(m) * a.n + row_begin + r;
+      float total = 0.0f;
+      for (int q = 0; q < peers.world; ++q) total += __ldcg(mine + q * slot + at);
+      if (in.ok) a.y[at] = store_value(a, m, row_begin + r, total);
+    }
   } else {
     for (int o = tid; o < rows * a.m; o += kConsumerThreads) {
       const int m = o / rows;
@@ -880,9 +939,15 @@ bool stream_mma_supported(const GemvArgs& a, const char** why) {
   return make_plan(a, &p, why);
 }
 
-cudaError_t launch_stream_mma(const GemvArgs& a, cudaStream_t stream, bool strict) {
+cudaError_t launch_stream_mma(const GemvArgs& a, cudaStream_t stream, bool strict,
+                              const PeerSet* peers) {
   MmaPlan p;
   if (!make_plan(a, &p, nullptr)) return cudaErrorInvalidValue;
+  const bool exchange = a.epilogue == kGatherPeers || a.epilogue == kReducePeers;
+  if (exchange != (peers != nullptr) || (exchange && p.ctas > kPeerFlagStride)) {
+    return cudaErrorInvalidValue;
+  }
+  const PeerSet ps = peers ? *peers : PeerSet{};
   p.strict = strict ? 1 : 0;
   p.status = device_status_word();
   if (!p.status) return cudaErrorInvalidSymbol;
@@ -909,7 +974,7 @@ cudaError_t launch_stream_mma(const GemvArgs& a, cudaStream_t stream, bool stric
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, stream_mma_kernel<MP, MT, CW, MC>, a, p, maps);
+    return cudaLaunchKernelEx(&cfg, stream_mma_kernel<MP, MT, CW, MC>, a, p, maps, ps);
   });
 }
 

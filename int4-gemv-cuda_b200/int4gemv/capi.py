@@ -42,7 +42,26 @@ _PROTOTYPES = {
     "int4gemv_quantize": (ctypes.c_int, [_p] * 4 + [ctypes.c_int] + [_i64] * 3 + [_p]),
     "int4gemv_pack": (ctypes.c_int, [_p, _p, _i64, _i64, _p]),
     "int4gemv_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
+    "int4gemv_peers_struct_bytes": (ctypes.c_size_t, []),
+    "int4gemv_peer_alloc": (ctypes.c_int, [_i64, ctypes.POINTER(_p), _p]),
+    "int4gemv_peer_open": (ctypes.c_int, [_p, ctypes.POINTER(_p)]),
+    "int4gemv_peer_close": (ctypes.c_int, [_p]),
+    "int4gemv_peer_free": (ctypes.c_int, [_p]),
+    "int4gemv_w4a16_exchange": (ctypes.c_int, [_p] * 5 + [_i64] * 4 + [_p, _p]),
 }
+
+MAX_PEERS = 8
+SHARD_ROWS, SHARD_K = 0, 1
+PEER_FLAG_STRIDE = 1024
+IPC_HANDLE_BYTES = 64
+
+
+class Peers(ctypes.Structure):
+    """int4gemv_peers_t."""
+
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("mode", ctypes.c_int32),
+                ("epoch", ctypes.c_uint32), ("n_total", ctypes.c_int64), ("col0", ctypes.c_int64),
+                ("out", _p * MAX_PEERS), ("flags", _p * MAX_PEERS)]
 
 
 class CapiError(RuntimeError):

@@ -1,0 +1,155 @@
+"""A W4A16 layer sharded over the GPUs of one node with the exchange fused into the GEMV kernel.
+
+Same two layouts as int4gemv.sharded (rows split with an all-gather of y; K split with a sum of
+the partial y), but instead of a NCCL collective after the GEMV, the GEMV's own epilogue writes
+its outputs straight into the other ranks' buffers over NVLink (peer stores into CUDA-IPC-mapped
+memory) and each CTA then waits, bounded, for the flags of its counterparts on the other ranks
+(int4gemv_w4a16_exchange in the C ABI). One kernel per call, no collective launch, and the exchange
+of a CTA's rows overlaps the other CTAs' weight streaming.
+
+Buffers: each rank allocates two y (rows split) or receive (K split) buffers, used alternately
+(a rank can run at most one call ahead of the slowest one), plus flag words that carry the call
+number. The handles travel over the process group once, at construction. The y a rows-split call
+returns is a view of one of the two buffers: it stays valid until the call after the next one.
+
+Constraints: the fast path's shapes (group 128, the rank's K a multiple of 1024, M <= 32); rows
+split needs N % world == 0 (equal shards, so every rank launches the same CTAs); K split cuts K in
+whole 1024-weight stages; at most 8 ranks; every rank makes the same calls in the same order.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+from . import capi
+from .sharded import split_range
+
+_STAGE_K = 1024
+
+
+class PeerBuffer:
+    """`nbytes` of zeroed device memory on every rank of `group`, mapped into every rank."""
+
+    def __init__(self, nbytes: int, group=None):
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        lib = capi.lib()
+        local = ctypes.c_void_p()
+        handle = (ctypes.c_char * capi.IPC_HANDLE_BYTES)()
+        capi.check(lib.int4gemv_peer_alloc(nbytes, ctypes.byref(local), ctypes.addressof(handle)))
+        self.local = local.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.ptrs = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                self.ptrs.append(self.local)
+                continue
+            mapped = ctypes.c_void_p()
+            buf = (ctypes.c_char * capi.IPC_HANDLE_BYTES).from_buffer_copy(h)
+            capi.check(lib.int4gemv_peer_open(ctypes.addressof(buf), ctypes.byref(mapped)))
+            self.ptrs.append(mapped.value)
+
+    def close(self) -> None:
+        if not self.ptrs:
+            return
+        lib = capi.lib()
+        for r, p in enumerate(self.ptrs):
+            if r != self.rank:
+                capi.check(lib.int4gemv_peer_close(p))
+        capi.check(lib.int4gemv_peer_free(self.local))
+        self.ptrs = []
+
+
+class _DeviceArray:
+    """A device pointer seen as a tensor (__cuda_array_interface__, no copy, no ownership)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (ptr, False), "version": 3, "strides": None}
+
+
+class FusedShardedW4A16:
+    """One weight matrix sharded over a process group; calling it with the full x returns the full
+    y on every rank, the exchange done inside the GEMV kernel.
+
+    mode "n": rows split (up projections, N % world == 0). mode "k": K split (down projections).
+    The constructor takes the full packed tensors (as every rank would load them), keeps this
+    rank's shard and sets up the peer buffers for inputs of up to `max_m` rows. Call close()
+    (on every rank) to release them.
+    """
+
+    def __init__(self, qweight: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor,
+                 group_size: int, mode: str, process_group=None, max_m: int = 32):
+        if mode not in ("n", "k"):
+            raise ValueError(f"mode must be 'n' or 'k', got {mode!r}")
+        self.mode, self.group_size, self.pg, self.max_m = mode, int(group_size), process_group, max_m
+        self.world = dist.get_world_size(process_group)
+        self.rank = dist.get_rank(process_group)
+        if self.world > capi.MAX_PEERS:
+            raise ValueError(f"at most {capi.MAX_PEERS} ranks, got {self.world}")
+        self.n = qweight.shape[0]
+        self.k = qweight.shape[1] * 8
+        if mode == "n":
+            if self.n % self.world:
+                raise ValueError(f"N = {self.n} must be a multiple of the world size {self.world}")
+            n0, n1 = split_range(self.n, self.world, self.rank)
+            self.q, self.s, self.z = (t[n0:n1].contiguous() for t in (qweight, scales, zeros))
+            self.span = (n0, n1)
+            half_bytes = max_m * self.n * 2
+        else:
+            if self.k % (_STAGE_K * self.world):
+                raise ValueError(f"K = {self.k} must be a multiple of {_STAGE_K} x world")
+            k0, k1 = split_range(self.k, self.world, self.rank, _STAGE_K)
+            g = self.group_size
+            self.q = qweight[:, k0 // 8:k1 // 8].contiguous()
+            self.s = scales[:, k0 // g:k1 // g].contiguous()
+            self.z = zeros[:, k0 // g:k1 // g].contiguous()
+            self.span = (k0, k1)
+            half_bytes = self.world * max_m * self.n * 4
+        self.half_bytes = half_bytes
+        self.out = PeerBuffer(2 * half_bytes, process_group)
+        self.flags = PeerBuffer(self.world * capi.PEER_FLAG_STRIDE * 4, process_group)
+        self.epoch = 0
+
+    def close(self) -> None:
+        torch.cuda.synchronize()
+        dist.barrier(group=self.pg)  # no rank still writes into another's buffers
+        self.out.close()
+        self.flags.close()
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        if x.dim() != 2 or x.shape[1] != self.k or x.dtype != torch.float16 or not x.is_cuda:
+            raise ValueError(f"x must be a float16 CUDA tensor [M, {self.k}], got "
+                             f"{x.dtype} {tuple(x.shape)}")
+        m = x.shape[0]
+        if not 1 <= m <= self.max_m:
+            raise ValueError(f"M = {m} must be in [1, {self.max_m}]")
+        self.epoch += 1
+        off = (self.epoch & 1) * self.half_bytes
+        peers = capi.Peers()
+        peers.world, peers.rank, peers.epoch = self.world, self.rank, self.epoch & 0xFFFFFFFF
+        for r in range(self.world):
+            peers.out[r] = self.out.ptrs[r] + off
+            peers.flags[r] = self.flags.ptrs[r]
+        stream = torch.cuda.current_stream().cuda_stream
+        g = self.group_size
+        if self.mode == "n":
+            peers.mode, peers.n_total, peers.col0 = capi.SHARD_ROWS, self.n, self.span[0]
+            xc = x.contiguous()
+            capi.call("int4gemv_w4a16_exchange", None, xc.data_ptr(), self.q.data_ptr(),
+                      self.s.data_ptr(), self.z.data_ptr(), m, self.q.shape[0], self.k, g,
+                      ctypes.addressof(peers), stream)
+            return torch.as_tensor(_DeviceArray(self.out.local + off, (m, self.n), "<f2"),
+                                   device=x.device)
+        peers.mode = capi.SHARD_K
+        k0, k1 = self.span
+        xs = x[:, k0:k1].contiguous()
+        y = torch.empty(m, self.n, dtype=torch.float16, device=x.device)
+        capi.call("int4gemv_w4a16_exchange", y.data_ptr(), xs.data_ptr(), self.q.data_ptr(),
+                  self.s.data_ptr(), self.z.data_ptr(), m, self.n, k1 - k0, g,
+                  ctypes.addressof(peers), stream)
+        return y

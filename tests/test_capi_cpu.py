@@ -90,3 +90,29 @@ def test_null_pointer_rejected():
 
 def test_workspace_size_is_nonnegative():
     assert capi.lib().int4gemv_w4a16_workspace_size(1, 8192, 8192, 128) >= 0
+
+
+def test_peers_struct_layout():
+    """The ctypes mirror of int4gemv_peers_t has the C struct's size."""
+    import ctypes
+
+    assert ctypes.sizeof(capi.Peers) == capi.lib().int4gemv_peers_struct_bytes()
+
+
+def test_exchange_rejects_bad_peers():
+    """Argument checks of int4gemv_w4a16_exchange run before any CUDA call."""
+    import ctypes
+
+    peers = capi.Peers()
+    peers.world, peers.rank, peers.mode = 9, 0, capi.SHARD_ROWS
+    with pytest.raises(capi.CapiError, match="at most 8 ranks"):
+        capi.call("int4gemv_w4a16_exchange", None, 16, 16, 16, 16, 1, 64, 1024, 128,
+                  ctypes.addressof(peers), None)
+    peers.world, peers.mode = 1, 7
+    with pytest.raises(capi.CapiError, match="unknown mode"):
+        capi.call("int4gemv_w4a16_exchange", None, 16, 16, 16, 16, 1, 64, 1024, 128,
+                  ctypes.addressof(peers), None)
+    peers.mode = capi.SHARD_ROWS
+    with pytest.raises(capi.CapiError, match="null buffer"):
+        capi.call("int4gemv_w4a16_exchange", None, 16, 16, 16, 16, 1, 64, 1024, 128,
+                  ctypes.addressof(peers), None)

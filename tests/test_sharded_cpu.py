@@ -81,3 +81,44 @@ def test_split_range():
     assert split_range(256, 4, 3, 128) == (256, 256)  # more ranks than groups: empty shard
     with pytest.raises(ValueError):
         split_range(100, 2, 0, 64)
+
+
+def _fused_worker(rank, world, port, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from int4gemv.exchange import FusedShardedW4A16
+
+        q = torch.zeros(6, 384, dtype=torch.int32)
+        s = torch.zeros(6, 24, dtype=torch.float16)
+        msgs = []
+        for mode in ("n", "k", "x"):
+            try:
+                FusedShardedW4A16(q, s, s, 128, mode)
+            except ValueError as e:
+                msgs.append(str(e))
+        results[rank] = msgs
+    finally:
+        dist.destroy_process_group()
+
+
+def test_fused_layer_shape_checks():
+    """int4gemv.exchange checks the sharding constraints on every rank before allocating: rows
+    split needs N % world == 0, K split whole 1024-weight stages per rank."""
+    world = 4
+    ctx = mp.get_context("spawn")
+    results = ctx.Manager().dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_fused_worker, args=(r, world, port, results))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for r in range(world):
+        n_msg, k_msg, mode_msg = results[r]
+        assert "multiple of the world size" in n_msg
+        assert "multiple of 1024 x world" in k_msg
+        assert "mode must be" in mode_msg
