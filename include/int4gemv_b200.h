@@ -189,18 +189,22 @@ int int4gemv_peer_free(void* ptr);
 #define INT4GEMV_SHARD_ROWS 0          /* N split: every rank gets y [m, n_total] (all-gather) */
 #define INT4GEMV_SHARD_K 1             /* K split: every rank gets y [m, n] = sum of partials */
 #define INT4GEMV_PEER_FLAG_STRIDE 1024 /* flag words per source rank */
+/* Bytes of one rank's flag buffer: the flag words, then two control words (call counter). */
+#define INT4GEMV_PEER_FLAG_BYTES(world) (((int64_t)(world) * INT4GEMV_PEER_FLAG_STRIDE + 16) * 4)
 
 typedef struct {
-  int32_t world, rank, mode;
-  uint32_t epoch;   /* 1, 2, 3, ...: one more on every call, the same on every rank */
-  int64_t n_total;  /* ROWS: columns of the gathered y */
-  int64_t col0;     /* ROWS: first column of this rank's shard in y */
-  /* out[r]: rank r's buffer, mapped here (out[rank] is this rank's own). ROWS: y [m, n_total]
-   * fp16. K: receive buffer [world, m, n] fp32. Buffers for consecutive calls must alternate
-   * (two per rank): a rank may run one call ahead of the others. */
+  int32_t world, rank, mode, reserved;
+  int64_t n_total;    /* ROWS: columns of the gathered y; must be n x world (equal shards) */
+  int64_t col0;       /* ROWS: first column of this rank's shard in y; must be n x rank */
+  int64_t out_bytes;  /* size of every rank's out buffer, the same on every rank */
+  /* out[r]: rank r's exchange buffer, mapped here (out[rank] is this rank's own), two halves used
+   * by alternate calls. ROWS: a half holds [m, n_total] fp16 (out_bytes >= 4 m n_total). K: a
+   * half holds [world, m, n] fp32 (out_bytes >= 8 world m n). */
   void* out[INT4GEMV_MAX_PEERS];
-  /* flags[r]: rank r's flag words, world * INT4GEMV_PEER_FLAG_STRIDE uint32, zeroed once at
-   * allocation and never reset (each call's epoch is larger than the last). */
+  /* flags[r]: rank r's flag buffer of INT4GEMV_PEER_FLAG_BYTES(world), zeroed once at
+   * allocation (int4gemv_peer_alloc does) and then owned by the kernel: it holds the number of
+   * the rank's last completed call, so calls need no host-side state and replay from a captured
+   * CUDA graph. Use one out / flag buffer set per sharded matrix. */
   void* flags[INT4GEMV_MAX_PEERS];
 } int4gemv_peers_t;
 
@@ -208,15 +212,15 @@ typedef struct {
 size_t int4gemv_peers_struct_bytes(void);
 
 /* The GEMV of this rank's shard with the exchange fused into its epilogue, on the fast path's
- * shapes (group_size 128, K % 1024 == 0, M <= 32). ROWS: the shard's rows are columns
- * [col0, col0 + n) of y; each CTA writes its outputs into every rank's y over NVLink (peer
- * stores), publishes a flag on every rank and waits for its counterparts' flags, so when the
- * kernel completes this rank's y [m, n_total] is whole. y is unused. K: each CTA writes its fp32
- * partial sums into every rank's receive buffer, waits likewise, and writes y [m, n] fp16 = the
- * ranks' partials added in rank order (bit-identical on every rank). Every rank must make the same
- * sequence of calls with the same m, n, k (so each launches the same CTAs). A wait on a peer is
- * bounded (2 s); when it runs out the kernel records INT4GEMV status 3 (int4gemv_device_status)
- * and finishes with an undefined result. */
+ * shapes (group_size 128, K % 1024 == 0, M <= 32), y [m, n_total] (ROWS) or [m, n] (K) fp16.
+ * ROWS: the shard's rows are columns [col0, col0 + n) of y; each CTA writes its outputs into
+ * every rank's exchange buffer over NVLink (peer stores), publishes a flag on every rank, waits
+ * for its counterparts' flags and copies the rows they wrote into y, so when the kernel completes
+ * y is whole. K: each CTA writes its fp32 partial sums into every rank's exchange buffer, waits
+ * likewise, and writes y = the ranks' partials added in rank order (bit-identical on every rank).
+ * Every rank must make the same sequence of calls with the same m, n, k (so each launches the
+ * same CTAs). A wait on a peer is bounded (2 s); when it runs out the kernel records status 3
+ * (int4gemv_device_status) and finishes with an undefined y. */
 int int4gemv_w4a16_exchange(void* y, const void* x, const void* qweight, const void* scales,
                             const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
                             const int4gemv_peers_t* peers, void* stream);

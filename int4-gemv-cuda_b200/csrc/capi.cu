@@ -577,16 +577,23 @@ int int4gemv_w4a16_exchange(void* y, const void* x, const void* qweight, const v
   if (m == 0 || n == 0 || k == 0) {
     return fail(INT4GEMV_ERR_INVALID, "%s: M, N and K must be positive", name);
   }
-  if (int e = check_pointers(name, m, n, k, mode == INT4GEMV_SHARD_K ? y : x, x, qweight, scales,
-                             zeros)) {
-    return e;
-  }
+  if (int e = check_pointers(name, m, n, k, y, x, qweight, scales, zeros)) return e;
+  const int64_t n_out = mode == INT4GEMV_SHARD_ROWS ? peers->n_total : n;
   if (mode == INT4GEMV_SHARD_ROWS &&
-      (peers->col0 < 0 || peers->n_total > INT_MAX || peers->col0 + n > peers->n_total)) {
-    return fail(INT4GEMV_ERR_INVALID, "%s: columns [%lld, %lld) outside y's %lld", name,
-                static_cast<long long>(peers->col0), static_cast<long long>(peers->col0 + n),
-                static_cast<long long>(peers->n_total));
+      (peers->n_total != n * peers->world || peers->col0 != n * peers->rank)) {
+    return fail(INT4GEMV_ERR_INVALID,
+                "%s: rows split needs equal shards: n_total = %lld must be %lld x %d and col0 = "
+                "%lld must be %lld x %d",
+                name, static_cast<long long>(peers->n_total), static_cast<long long>(n),
+                peers->world, static_cast<long long>(peers->col0), static_cast<long long>(n),
+                peers->rank);
   }
+  const int64_t need = mode == INT4GEMV_SHARD_ROWS ? m * n_out * 2 : peers->world * m * n * 4;
+  if (peers->out_bytes < 2 * need) {
+    return fail(INT4GEMV_ERR_INVALID, "%s: out buffers of %lld bytes, %lld needed (two halves)",
+                name, static_cast<long long>(peers->out_bytes), static_cast<long long>(2 * need));
+  }
+  if (n_out > INT_MAX) return fail(INT4GEMV_ERR_INVALID, "%s: y too wide", name);
   i4::GemvArgs a = make_args(y, x, qweight, scales, zeros, m, n, k, group_size);
   a.epilogue = mode == INT4GEMV_SHARD_ROWS ? i4::kGatherPeers : i4::kReducePeers;
   const char* why = "unsupported shape";
@@ -596,11 +603,11 @@ int int4gemv_w4a16_exchange(void* y, const void* x, const void* qweight, const v
     ps.out[r] = peers->out[r];
     ps.flags[r] = static_cast<unsigned*>(peers->flags[r]);
   }
+  ps.out_half = (peers->out_bytes / 2) / 16 * 16;
   ps.world = peers->world;
   ps.rank = peers->rank;
-  ps.epoch = peers->epoch;
-  ps.n_total = static_cast<int>(peers->n_total);
-  ps.col0 = static_cast<int>(peers->col0);
+  ps.n_total = static_cast<int>(n_out);
+  ps.col0 = static_cast<int>(mode == INT4GEMV_SHARD_ROWS ? peers->col0 : 0);
   return launched(name, i4::launch_stream_mma(a, static_cast<cudaStream_t>(stream), false, &ps));
 }
 

@@ -20,18 +20,22 @@ constexpr int kMaxPeers = 8;
 constexpr int kPeerFlagStride = 1024;  // flag words per source rank (>= CTAs of any launch)
 constexpr unsigned long long kPeerWaitNs = 2000000000ull;  // limit of one wait on a peer's flag
 
-// Peer pointers of one exchange call. out[r] and flags[r] are rank r's buffers, mapped into this
-// process (out[rank] and flags[rank] are this rank's own). kGatherPeers: out[r] = rank r's y
-// [m, n_total] fp16, this rank writes columns [col0, col0 + n). kReducePeers: out[r] = rank r's
-// receive buffer [world, m, n] fp32, this rank writes slot `rank`. flags[r] = world *
-// kPeerFlagStride words; this rank's CTA c sets word rank * kPeerFlagStride + c of every rank to
-// `epoch` after its stores, and waits for word r * kPeerFlagStride + c of its own flags, for
-// every r.
+// Peer buffers of a sharded layer. out[r] and flags[r] are rank r's buffers, mapped into this
+// process (out[rank] and flags[rank] are this rank's own). Each out buffer has two halves of
+// out_half bytes, used by alternate calls (a rank can run at most one call ahead of another).
+// kGatherPeers: a half is y [m, n_total] fp16; this rank writes columns [col0, col0 + n) of
+// every rank's half, then each CTA copies the rows it waited for into this rank's y.
+// kReducePeers: a half is [world, m, n] fp32; this rank writes slot `rank` of every rank's half.
+// flags[r] holds world * kPeerFlagStride flag words, then (rank r's own) two control words: the
+// number of the last completed call and a count of finished CTAs. A call's number is control[0]
+// + 1, read on the device, so a captured graph replays correctly. CTA c sets word
+// rank * kPeerFlagStride + c of every rank to the call number after its stores and waits for word
+// r * kPeerFlagStride + c of its own flags, for every r.
 struct PeerSet {
   void* out[kMaxPeers];
   unsigned* flags[kMaxPeers];
+  long long out_half;
   int world, rank;
-  unsigned epoch;
   int n_total, col0;
 };
 

@@ -593,6 +593,13 @@ __device__ __forceinline__ void wide_stage(const unsigned char* st, const unsign
   }
 }
 
+// Call number of this exchange: one more than the last completed call of this rank's layer
+// (control word 0 of its own flags). Read after the dependency wait, so the previous call's update
+// is visible.
+__device__ __forceinline__ unsigned exchange_epoch(const PeerSet& peers) {
+  return __ldcg(peers.flags[peers.rank] + peers.world * kPeerFlagStride) + 1u;
+}
+
 // The consumers' half of a peer exchange, after each has issued its stores into the ranks'
 // buffers: every thread fences its own stores at system scope, the CTA synchronises, one thread
 // publishes this CTA's flag (`epoch`, release) on every rank, and threads 0 .. world - 1 each wait
@@ -600,19 +607,35 @@ __device__ __forceinline__ void wide_stage(const unsigned char* st, const unsign
 // synchronises again, so its threads may read what the other ranks wrote. A wait that runs out
 // records kStatusPeerTimeout and stops waiting.
 template <int kConsumerThreads>
-__device__ __forceinline__ void exchange_flags(const PeerSet& peers, int* status, int tid) {
+__device__ __forceinline__ void exchange_flags(const PeerSet& peers, unsigned epoch, int* status,
+                                               int tid) {
   __threadfence_system();
   named_barrier(kConsumerBarrier, kConsumerThreads);
   if (tid == 0) {
     for (int q = 0; q < peers.world; ++q) {
-      st_release_sys(peers.flags[q] + peers.rank * kPeerFlagStride + blockIdx.x, peers.epoch);
+      st_release_sys(peers.flags[q] + peers.rank * kPeerFlagStride + blockIdx.x, epoch);
     }
   }
   if (tid < peers.world) {
     const unsigned* f = peers.flags[peers.rank] + tid * kPeerFlagStride + blockIdx.x;
-    if (!wait_flag_bounded(f, peers.epoch, kPeerWaitNs)) atomicExch(status, kStatusPeerTimeout);
+    if (!wait_flag_bounded(f, epoch, kPeerWaitNs)) atomicExch(status, kStatusPeerTimeout);
   }
   named_barrier(kConsumerBarrier, kConsumerThreads);
+}
+
+// The last CTA of the call to finish records `epoch` as this rank's last completed call.
+template <int kConsumerThreads>
+__device__ __forceinline__ void exchange_done(const PeerSet& peers, unsigned epoch, int tid) {
+  named_barrier(kConsumerBarrier, kConsumerThreads);  // this CTA's reads of the buffers are done
+  if (tid == 0) {
+    unsigned* control = peers.flags[peers.rank] + peers.world * kPeerFlagStride;
+    __threadfence();
+    if (atomicAdd(control + 1, 1u) == gridDim.x - 1) {
+      control[1] = 0;
+      control[0] = epoch;
+      __threadfence();
+    }
+  }
 }
 
 // MP: M rounded up to 2 or 4 (narrow path) or 8 (wide path, MT tiles of 8 rows of x). MC: M when
@@ -809,21 +832,40 @@ __global__ void __maxnreg__(CW == 16 ? 96 : 168)
       }
     }
   } else if (a.epilogue == kGatherPeers) {
-    // This rank's columns of y, written into every rank's y (this one's included).
+    // This rank's columns of y into the current half of every rank's gather buffer; once this
+    // CTA's counterparts on every rank have done the same, the rows they wrote (the same row
+    // range of every rank's shard) are copied into this rank's y.
+    const unsigned epoch = exchange_epoch(peers);
+    const long long off = (epoch & 1u) * peers.out_half;  // this call's half
     for (int o = tid; o < rows * a.m; o += kConsumerThreads) {
       const int m = o / rows;
       const int r = o - m * rows;
       const half h = __float2half_rn(row_sum(r, m));
       const int64_t at = static_cast<int64_t>(m) * peers.n_total + peers.col0 + row_begin + r;
       if (in.ok) {
-        for (int q = 0; q < peers.world; ++q) static_cast<half*>(peers.out[q])[at] = h;
+        for (int q = 0; q < peers.world; ++q) {
+          reinterpret_cast<half*>(static_cast<char*>(peers.out[q]) + off)[at] = h;
+        }
       }
     }
-    exchange_flags<kConsumerThreads>(peers, p.status, tid);
+    exchange_flags<kConsumerThreads>(peers, epoch, p.status, tid);
+    const half* buf =
+        reinterpret_cast<const half*>(static_cast<const char*>(peers.out[peers.rank]) + off);
+    for (int o = tid; o < peers.world * rows * a.m; o += kConsumerThreads) {
+      const int q = o / (rows * a.m);
+      const int rem = o - q * rows * a.m;
+      const int m = rem / rows;
+      const int r = rem - m * rows;
+      const int64_t at = static_cast<int64_t>(m) * peers.n_total + q * a.n + row_begin + r;
+      if (in.ok) a.y[at] = __ldcg(buf + at);
+    }
+    exchange_done<kConsumerThreads>(peers, epoch, tid);
   } else if (a.epilogue == kReducePeers) {
-    // This rank's fp32 partial sums into slot `rank` of every rank's receive buffer; then, once
-    // every rank's partials for these rows are in, their sum in rank order (the same on every
-    // rank, so all ranks hold bit-identical y).
+    // This rank's fp32 partial sums into slot `rank` of the current half of every rank's receive
+    // buffer; then, once every rank's partials for these rows are in, their sum in rank order
+    // (the same on every rank, so all ranks hold bit-identical y).
+    const unsigned epoch = exchange_epoch(peers);
+    const long long off = (epoch & 1u) * peers.out_half;  // this call's half
     const int64_t slot = static_cast<int64_t>(a.m) * a.n;
     for (int o = tid; o < rows * a.m; o += kConsumerThreads) {
       const int m = o / rows;
@@ -831,11 +873,14 @@ __global__ void __maxnreg__(CW == 16 ? 96 : 168)
       const float sum = row_sum(r, m);
       const int64_t at = peers.rank * slot + static_cast<int64_t>(m) * a.n + row_begin + r;
       if (in.ok) {
-        for (int q = 0; q < peers.world; ++q) static_cast<float*>(peers.out[q])[at] = sum;
+        for (int q = 0; q < peers.world; ++q) {
+          reinterpret_cast<float*>(static_cast<char*>(peers.out[q]) + off)[at] = sum;
+        }
       }
     }
-    exchange_flags<kConsumerThreads>(peers, p.status, tid);
-    const float* mine = static_cast<const float*>(peers.out[peers.rank]);
+    exchange_flags<kConsumerThreads>(peers, epoch, p.status, tid);
+    const float* mine =
+        reinterpret_cast<const float*>(static_cast<const char*>(peers.out[peers.rank]) + off);
     for (int o = tid; o < rows * a.m; o += kConsumerThreads) {
       const int m = o / rows;
       const int r = o - m * rows;
@@ -844,6 +889,7 @@ __global__ void __maxnreg__(CW == 16 ? 96 : 168)
       for (int q = 0; q < peers.world; ++q) total += __ldcg(mine + q * slot + at);
       if (in.ok) a.y[at] = store_value(a, m, row_begin + r, total);
     }
+    exchange_done<kConsumerThreads>(peers, epoch, tid);
   } else {
     for (int o = tid; o < rows * a.m; o += kConsumerThreads) {
       const int m = o / rows;

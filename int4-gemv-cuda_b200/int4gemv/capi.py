@@ -60,8 +60,14 @@ class Peers(ctypes.Structure):
     """int4gemv_peers_t."""
 
     _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("mode", ctypes.c_int32),
-                ("epoch", ctypes.c_uint32), ("n_total", ctypes.c_int64), ("col0", ctypes.c_int64),
+                ("reserved", ctypes.c_int32), ("n_total", ctypes.c_int64),
+                ("col0", ctypes.c_int64), ("out_bytes", ctypes.c_int64),
                 ("out", _p * MAX_PEERS), ("flags", _p * MAX_PEERS)]
+
+
+def peer_flag_bytes(world: int) -> int:
+    """INT4GEMV_PEER_FLAG_BYTES(world)."""
+    return (world * PEER_FLAG_STRIDE + 16) * 4
 
 
 class CapiError(RuntimeError):

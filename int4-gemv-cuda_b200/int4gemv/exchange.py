@@ -7,10 +7,11 @@ memory) and each CTA then waits, bounded, for the flags of its counterparts on t
 (int4gemv_w4a16_exchange in the C ABI). One kernel per call, no collective launch, and the exchange
 of a CTA's rows overlaps the other CTAs' weight streaming.
 
-Buffers: each rank allocates two y (rows split) or receive (K split) buffers, used alternately
-(a rank can run at most one call ahead of the slowest one), plus flag words that carry the call
-number. The handles travel over the process group once, at construction. The y a rows-split call
-returns is a view of one of the two buffers: it stays valid until the call after the next one.
+Buffers: each rank allocates one exchange buffer with two halves, used by alternate calls (a rank
+can run at most one call ahead of the slowest one), and a flag buffer whose words carry call
+numbers; the call counter itself lives in device memory, so a call needs no host-side state and
+can be captured in a CUDA graph and replayed. The handles travel over the process group once, at
+construction. Each call returns a new y tensor.
 
 Constraints: the fast path's shapes (group 128, the rank's K a multiple of 1024, M <= 32); rows
 split needs N % world == 0 (equal shards, so every rank launches the same CTAs); K split cuts K in
@@ -64,14 +65,6 @@ class PeerBuffer:
         self.ptrs = []
 
 
-class _DeviceArray:
-    """A device pointer seen as a tensor (__cuda_array_interface__, no copy, no ownership)."""
-
-    def __init__(self, ptr: int, shape, typestr: str):
-        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
-                                         "data": (ptr, False), "version": 3, "strides": None}
-
-
 class FusedShardedW4A16:
     """One weight matrix sharded over a process group; calling it with the full x returns the full
     y on every rank, the exchange done inside the GEMV kernel.
@@ -110,10 +103,20 @@ class FusedShardedW4A16:
             self.z = zeros[:, k0 // g:k1 // g].contiguous()
             self.span = (k0, k1)
             half_bytes = self.world * max_m * self.n * 4
-        self.half_bytes = half_bytes
-        self.out = PeerBuffer(2 * half_bytes, process_group)
-        self.flags = PeerBuffer(self.world * capi.PEER_FLAG_STRIDE * 4, process_group)
-        self.epoch = 0
+        self.out_bytes = 2 * half_bytes
+        self.out = PeerBuffer(self.out_bytes, process_group)
+        self.flags = PeerBuffer(capi.peer_flag_bytes(self.world), process_group)
+        self.peers = capi.Peers()
+        self.peers.world, self.peers.rank = self.world, self.rank
+        self.peers.out_bytes = self.out_bytes
+        for r in range(self.world):
+            self.peers.out[r] = self.out.ptrs[r]
+            self.peers.flags[r] = self.flags.ptrs[r]
+        if mode == "n":
+            self.peers.mode, self.peers.n_total = capi.SHARD_ROWS, self.n
+            self.peers.col0 = self.span[0]
+        else:
+            self.peers.mode = capi.SHARD_K
 
     def close(self) -> None:
         torch.cuda.synchronize()
@@ -128,28 +131,14 @@ class FusedShardedW4A16:
         m = x.shape[0]
         if not 1 <= m <= self.max_m:
             raise ValueError(f"M = {m} must be in [1, {self.max_m}]")
-        self.epoch += 1
-        off = (self.epoch & 1) * self.half_bytes
-        peers = capi.Peers()
-        peers.world, peers.rank, peers.epoch = self.world, self.rank, self.epoch & 0xFFFFFFFF
-        for r in range(self.world):
-            peers.out[r] = self.out.ptrs[r] + off
-            peers.flags[r] = self.flags.ptrs[r]
         stream = torch.cuda.current_stream().cuda_stream
-        g = self.group_size
         if self.mode == "n":
-            peers.mode, peers.n_total, peers.col0 = capi.SHARD_ROWS, self.n, self.span[0]
-            xc = x.contiguous()
-            capi.call("int4gemv_w4a16_exchange", None, xc.data_ptr(), self.q.data_ptr(),
-                      self.s.data_ptr(), self.z.data_ptr(), m, self.q.shape[0], self.k, g,
-                      ctypes.addressof(peers), stream)
-            return torch.as_tensor(_DeviceArray(self.out.local + off, (m, self.n), "<f2"),
-                                   device=x.device)
-        peers.mode = capi.SHARD_K
-        k0, k1 = self.span
-        xs = x[:, k0:k1].contiguous()
+            xs, n_local, k_local = x.contiguous(), self.q.shape[0], self.k
+        else:
+            k0, k1 = self.span
+            xs, n_local, k_local = x[:, k0:k1].contiguous(), self.n, k1 - k0
         y = torch.empty(m, self.n, dtype=torch.float16, device=x.device)
         capi.call("int4gemv_w4a16_exchange", y.data_ptr(), xs.data_ptr(), self.q.data_ptr(),
-                  self.s.data_ptr(), self.z.data_ptr(), m, self.n, k1 - k0, g,
-                  ctypes.addressof(peers), stream)
+                  self.s.data_ptr(), self.z.data_ptr(), m, n_local, k_local, self.group_size,
+                  ctypes.addressof(self.peers), stream)
         return y

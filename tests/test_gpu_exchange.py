@@ -1,8 +1,9 @@
 """The sharded layer with the exchange fused into the GEMV (int4gemv.exchange, the C ABI's
 int4gemv_w4a16_exchange): rows split (peer stores of y into every rank) and K split (peer stores of
 fp32 partials, summed in rank order), checked against the oracle on the full matrix over several
-consecutive calls (alternating buffers, increasing call numbers). World size 1 runs on one GPU;
-the 2-GPU test is skipped when fewer GPUs are visible."""
+consecutive calls (alternating buffers, increasing call numbers), eager and replayed from a
+captured CUDA graph. World size 1 runs on one GPU; the 2-GPU test is skipped when fewer GPUs are
+visible."""
 
 import datetime
 import os
@@ -47,8 +48,18 @@ def _run_cases(rank, world):
         ys = []
         for x in xs:
             y = layer(torch.from_numpy(x).cuda())
-            ys.append(y.float().cpu().numpy())  # copy before the buffer is reused
+            ys.append(y.float().cpu().numpy())
+        # the same calls replayed from a captured CUDA graph (call numbers kept on the device)
+        static_x = torch.zeros(m, k, dtype=torch.float16, device="cuda")
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            static_y = layer(static_x)
+        for x in xs:
+            static_x.copy_(torch.from_numpy(x).cuda())
+            graph.replay()
+            ys.append(static_y.float().cpu().numpy())
         torch.cuda.synchronize()
+        del graph
         layer.close()
         out.append(ys)
     assert capi.device_status() == 0
@@ -58,7 +69,7 @@ def _run_cases(rank, world):
 def _check(results_per_rank):
     for i, (mode, m, n, k) in enumerate(CASES):
         xs, q, s, z = _inputs(i, mode, m, n, k)
-        for c, x in enumerate(xs):
+        for c, x in enumerate(xs + xs):  # eager calls, then graph replays
             ref = oracle.reference(x, q, s, z, 128)
             for r, res in enumerate(results_per_rank):
                 ok, msg = oracle.check_close(res[i][c], ref, 1e-2, 1e-2)
