@@ -22,7 +22,10 @@ Measurement:
 sample of the same workload, in the same unit.
 Multi-GPU (torchrun): every rank runs the same workload on its own weights (independent weight
 matrices, e.g. different layers); no collective in the data path; value = sum over ranks of bytes
-/ the slowest rank's time ("scaling": "weak").
+/ the slowest rank's time ("scaling": "weak"). With more than one rank the line also carries
+"sharded": the multi-GPU configs (up 28672 x 8192 rows split, down 8192 x 28672 K split, M = 1
+and 8) timed with the exchange fused into the GEMV (int4gemv.exchange) and with the NCCL stack
+(int4gemv.sharded), device time max over ranks (--no-sharded skips it).
 """
 
 from __future__ import annotations
@@ -333,6 +336,66 @@ def time_quantize(n: int = 28672, k: int = 8192, calls: int = 20) -> dict:
             "gb_s": round(moved / sec / 1e9, 1), "frac_of_hbm": round(moved / sec / 1e9 / peak[0], 4)}
 
 
+def time_sharded(world: int, rank: int, reps: int = 5) -> dict:
+    """The sharded configs of the multi-GPU rows (up 28672 x 8192 rows split, down 8192 x 28672 K
+    split, M = 1 and 8) on this job's ranks: the fused exchange (int4gemv.exchange) against the
+    NCCL stack (int4gemv.sharded), both replayed from CUDA graphs, device time max over ranks.
+    Enough layers with distinct weights rotate through each graph that every call streams its
+    shard from HBM (more than 2x L2 per rank)."""
+    from int4gemv import ops
+    from int4gemv.exchange import FusedShardedW4A16
+    from int4gemv.sharded import ShardedW4A16
+
+    out = {}
+    for name, (n, k, mode) in (("up_28672x8192_rows_split", (28672, 8192, "n")),
+                               ("down_8192x28672_k_split", (8192, 28672, "k"))):
+        shard_bytes = n * k // 2 // world
+        layers = max(2, math.ceil(2 * L2_BYTES / shard_bytes) + 1)
+        gen = torch.Generator(device="cuda").manual_seed(11)
+        fused, nccl = [], []
+        for _ in range(layers):
+            w = torch.randn(n, k, generator=gen, device="cuda", dtype=torch.float16) * 0.02
+            q, s, z = ops.quantize(w, GROUP)
+            del w
+            fused.append(FusedShardedW4A16(q, s, z, GROUP, mode))
+            nccl.append(ShardedW4A16(q, s, z, GROUP, mode))
+            del q, s, z
+        res = {"layers_rotated": layers}
+        for m in (1, 8):
+            x = torch.randn(m, k, generator=gen, device="cuda", dtype=torch.float16)
+            row = {}
+            for label, stack in (("fused_us", fused), ("nccl_us", nccl)):
+                for layer in stack:
+                    layer(x)
+                torch.cuda.synchronize()
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    for layer in stack:
+                        layer(x)
+                graph.replay()
+                torch.cuda.synchronize()
+                barrier(world)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(reps):
+                    graph.replay()
+                e1.record()
+                e1.synchronize()
+                sec = max_over_ranks(e0.elapsed_time(e1) / 1e3, world) / (reps * layers)
+                row[label] = round(sec * 1e6, 2)
+                del graph
+            row["speedup_fused_vs_nccl"] = round(row["nccl_us"] / row["fused_us"], 3)
+            row["fused_gb_s_total"] = round(int4_bytes(m, n, k, GROUP) / (row["fused_us"] / 1e6)
+                                            / 1e9, 1)
+            res[f"m{m}"] = row
+        torch.cuda.synchronize()
+        barrier(world)
+        for layer in fused:
+            layer.close()
+        out[name] = res
+    return out
+
+
 def run_reference_arm(args, world, rank):
     if rank != 0:
         return
@@ -507,6 +570,8 @@ def run_ours(args, world, rank, local):
            "us_per_call": round(e2e_s * 1e6, 3),
            "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2}
 
+    sharded = time_sharded(world, rank) if world > 1 and not args.no_sharded else None
+
     peak, peak_kind = measured_peak()
     achieved = bytes_call / launch_s / 1e9
     traffic = ncu_traffic()
@@ -542,6 +607,8 @@ def run_ours(args, world, rank, local):
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    if sharded is not None:
+        line["sharded"] = sharded
     print(json.dumps(line), flush=True)
 
 
@@ -587,6 +654,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="with more than one GPU, skip the sharded-layer timing")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.profile:

@@ -189,8 +189,8 @@ int int4gemv_peer_free(void* ptr);
 #define INT4GEMV_SHARD_ROWS 0          /* N split: every rank gets y [m, n_total] (all-gather) */
 #define INT4GEMV_SHARD_K 1             /* K split: every rank gets y [m, n] = sum of partials */
 #define INT4GEMV_PEER_FLAG_STRIDE 1024 /* flag words per source rank */
-/* Bytes of one rank's flag buffer: the flag words, then two control words (call counter). */
-#define INT4GEMV_PEER_FLAG_BYTES(world) (((int64_t)(world) * INT4GEMV_PEER_FLAG_STRIDE + 16) * 4)
+/* Bytes of one rank's flag buffer: the flag words, then one call counter per CTA. */
+#define INT4GEMV_PEER_FLAG_BYTES(world) (((int64_t)(world) + 1) * INT4GEMV_PEER_FLAG_STRIDE * 4)
 
 typedef struct {
   int32_t world, rank, mode, reserved;

@@ -26,9 +26,9 @@ constexpr unsigned long long kPeerWaitNs = 2000000000ull;  // limit of one wait 
 // kGatherPeers: a half is y [m, n_total] fp16; this rank writes columns [col0, col0 + n) of
 // every rank's half, then each CTA copies the rows it waited for into this rank's y.
 // kReducePeers: a half is [world, m, n] fp32; this rank writes slot `rank` of every rank's half.
-// flags[r] holds world * kPeerFlagStride flag words, then (rank r's own) two control words: the
-// number of the last completed call and a count of finished CTAs. A call's number is control[0]
-// + 1, read on the device, so a captured graph replays correctly. CTA c sets word
+// flags[r] holds world * kPeerFlagStride flag words, then kPeerFlagStride control words (rank r's
+// own): CTA c's number of its last completed call. A call's number is that + 1, read on the
+// device, so a captured graph replays correctly. CTA c sets word
 // rank * kPeerFlagStride + c of every rank to the call number after its stores and waits for word
 // r * kPeerFlagStride + c of its own flags, for every r.
 struct PeerSet {

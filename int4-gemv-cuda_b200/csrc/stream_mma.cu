@@ -593,27 +593,33 @@ __device__ __forceinline__ void wide_stage(const unsigned char* st, const unsign
   }
 }
 
-// Call number of this exchange: one more than the last completed call of this rank's layer
-// (control word 0 of its own flags). Read after the dependency wait, so the previous call's update
-// is visible.
+// Call number of this exchange for this CTA: one more than the CTA's last completed call (its
+// control word in this rank's flags). Every call runs the same CTAs, so the per-CTA counters
+// advance together and need no cross-CTA coordination. Read after the dependency wait, so the
+// previous call's update is visible.
+__device__ __forceinline__ unsigned* exchange_counter(const PeerSet& peers) {
+  return peers.flags[peers.rank] + peers.world * kPeerFlagStride + blockIdx.x;
+}
+
 __device__ __forceinline__ unsigned exchange_epoch(const PeerSet& peers) {
-  return __ldcg(peers.flags[peers.rank] + peers.world * kPeerFlagStride) + 1u;
+  return __ldcg(exchange_counter(peers)) + 1u;
 }
 
 // The consumers' half of a peer exchange, after each has issued its stores into the ranks'
-// buffers: every thread fences its own stores at system scope, the CTA synchronises, one thread
-// publishes this CTA's flag (`epoch`, release) on every rank, and threads 0 .. world - 1 each wait
-// (acquire, bounded) for the flag of this CTA's counterpart on one rank. Then the CTA
-// synchronises again, so its threads may read what the other ranks wrote. A wait that runs out
-// records kStatusPeerTimeout and stops waiting.
+// buffers: the CTA synchronises (which orders every thread's stores before thread 0's next
+// operations), thread 0 publishes this CTA's flag on every rank with one system-scope release
+// fence and relaxed stores (the release is cumulative: it makes the whole CTA's stores visible
+// first; one fence per CTA, not one per thread or per rank), and threads 0 .. world - 1 each wait (acquire, bounded) for the flag of this CTA's
+// counterpart on one rank. Then the CTA synchronises again, so its threads may read what the
+// other ranks wrote. A wait that runs out records kStatusPeerTimeout and stops waiting.
 template <int kConsumerThreads>
 __device__ __forceinline__ void exchange_flags(const PeerSet& peers, unsigned epoch, int* status,
                                                int tid) {
-  __threadfence_system();
   named_barrier(kConsumerBarrier, kConsumerThreads);
   if (tid == 0) {
+    fence_release_sys();
     for (int q = 0; q < peers.world; ++q) {
-      st_release_sys(peers.flags[q] + peers.rank * kPeerFlagStride + blockIdx.x, epoch);
+      st_relaxed_sys(peers.flags[q] + peers.rank * kPeerFlagStride + blockIdx.x, epoch);
     }
   }
   if (tid < peers.world) {
@@ -623,19 +629,10 @@ __device__ __forceinline__ void exchange_flags(const PeerSet& peers, unsigned ep
   named_barrier(kConsumerBarrier, kConsumerThreads);
 }
 
-// The last CTA of the call to finish records `epoch` as this rank's last completed call.
-template <int kConsumerThreads>
+// Records `epoch` as this CTA's last completed call (read by the next call, after its
+// dependency wait on this kernel).
 __device__ __forceinline__ void exchange_done(const PeerSet& peers, unsigned epoch, int tid) {
-  named_barrier(kConsumerBarrier, kConsumerThreads);  // this CTA's reads of the buffers are done
-  if (tid == 0) {
-    unsigned* control = peers.flags[peers.rank] + peers.world * kPeerFlagStride;
-    __threadfence();
-    if (atomicAdd(control + 1, 1u) == gridDim.x - 1) {
-      control[1] = 0;
-      control[0] = epoch;
-      __threadfence();
-    }
-  }
+  if (tid == 0) *exchange_counter(peers) = epoch;
 }
 
 // MP: M rounded up to 2 or 4 (narrow path) or 8 (wide path, MT tiles of 8 rows of x). MC: M when
@@ -859,7 +856,7 @@ __global__ void __maxnreg__(CW == 16 ? 96 : 168)
       const int64_t at = static_cast<int64_t>(m) * peers.n_total + q * a.n + row_begin + r;
       if (in.ok) a.y[at] = __ldcg(buf + at);
     }
-    exchange_done<kConsumerThreads>(peers, epoch, tid);
+    exchange_done(peers, epoch, tid);
   } else if (a.epilogue == kReducePeers) {
     // This rank's fp32 partial sums into slot `rank` of the current half of every rank's receive
     // buffer; then, once every rank's partials for these rows are in, their sum in rank order
@@ -889,7 +886,7 @@ __global__ void __maxnreg__(CW == 16 ? 96 : 168)
       for (int q = 0; q < peers.world; ++q) total += __ldcg(mine + q * slot + at);
       if (in.ok) a.y[at] = store_value(a, m, row_begin + r, total);
     }
-    exchange_done<kConsumerThreads>(peers, epoch, tid);
+    exchange_done(peers, epoch, tid);
   } else {
     for (int o = tid; o < rows * a.m; o += kConsumerThreads) {
       const int m = o / rows;

@@ -67,7 +67,7 @@ class Peers(ctypes.Structure):
 
 def peer_flag_bytes(world: int) -> int:
     """INT4GEMV_PEER_FLAG_BYTES(world)."""
-    return (world * PEER_FLAG_STRIDE + 16) * 4
+    return (world + 1) * PEER_FLAG_STRIDE * 4
 
 
 class CapiError(RuntimeError):
