@@ -15,7 +15,8 @@ construction. Each call returns a new y tensor.
 
 Constraints: the fast path's shapes (group 128, the rank's K a multiple of 1024, M <= 32); rows
 split needs N % world == 0 (equal shards, so every rank launches the same CTAs); K split cuts K in
-whole 1024-weight stages; at most 8 ranks; every rank makes the same calls in the same order.
+whole 1024-weight stages, as evenly as they go (28672 over 8 ranks: 4 ranks of 4096, 4 of 3072);
+at most 8 ranks; every rank makes the same calls in the same order.
 """
 
 from __future__ import annotations
@@ -94,8 +95,9 @@ class FusedShardedW4A16:
             self.span = (n0, n1)
             half_bytes = max_m * self.n * 2
         else:
-            if self.k % (_STAGE_K * self.world):
-                raise ValueError(f"K = {self.k} must be a multiple of {_STAGE_K} x world")
+            if self.k % _STAGE_K or self.k < _STAGE_K * self.world:
+                raise ValueError(f"K = {self.k} must be a multiple of {_STAGE_K} and at least "
+                                 f"{_STAGE_K} x world ({self.world})")
             k0, k1 = split_range(self.k, self.world, self.rank, _STAGE_K)
             g = self.group_size
             self.q = qweight[:, k0 // 8:k1 // 8].contiguous()

@@ -17,9 +17,10 @@ import oracle
 
 pytestmark = pytest.mark.gpu
 
-# (mode, M, N, K): rows split needs N % world == 0, K split K % (1024 x world) == 0
+# (mode, M, N, K): rows split needs N % world == 0, K split K % 1024 == 0 and K >= 1024 x world
+# (uneven stage counts per rank allowed: 3072 over 2 ranks is 2 + 1 stages)
 CASES = [("n", 1, 28672, 8192), ("n", 8, 4096, 2048), ("k", 1, 8192, 28672), ("k", 5, 1024, 8192),
-         ("n", 32, 2048, 1024), ("k", 2, 4100, 4096)]
+         ("n", 32, 2048, 1024), ("k", 2, 4100, 4096), ("k", 3, 512, 3072)]
 CALLS = 3  # consecutive calls per case, each with its own x
 
 

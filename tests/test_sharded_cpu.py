@@ -105,7 +105,7 @@ def _fused_worker(rank, world, port, results):
 
 def test_fused_layer_shape_checks():
     """int4gemv.exchange checks the sharding constraints on every rank before allocating: rows
-    split needs N % world == 0, K split whole 1024-weight stages per rank."""
+    split needs N % world == 0, K split at least one whole 1024-weight stage per rank."""
     world = 4
     ctx = mp.get_context("spawn")
     results = ctx.Manager().dict()
@@ -120,5 +120,5 @@ def test_fused_layer_shape_checks():
     for r in range(world):
         n_msg, k_msg, mode_msg = results[r]
         assert "multiple of the world size" in n_msg
-        assert "multiple of 1024 x world" in k_msg
+        assert "multiple of 1024 and at least 1024 x world" in k_msg
         assert "mode must be" in mode_msg
