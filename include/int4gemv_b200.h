@@ -127,6 +127,17 @@ int int4gemv_w4a16_bias_residual(void* y, const void* x, const void* qweight, co
                                  int64_t m, int64_t n, int64_t k, int64_t group_size,
                                  void* stream);
 
+/* One launch for several matrices that share x (q / k / v, or gate / up kept apart): their
+ * packed weights stacked by rows into one qweight [sum ns, K/8], scales and zeros
+ * [sum ns, K/group_size] (stack them once at load time), and each matrix i's output written to
+ * its own ys[i] [m, ns[i]] fp16. count <= INT4GEMV_MAX_GROUP. On the fast path's shapes this is a
+ * single stream_mma launch over all the rows (one x load, one tail); otherwise one launch per
+ * matrix. New: the reference launches one GEMV per matrix. */
+#define INT4GEMV_MAX_GROUP 8
+int int4gemv_w4a16_grouped(int count, void* const* ys, const int64_t* ns, const void* x,
+                           const void* qweight, const void* scales, const void* zeros, int64_t m,
+                           int64_t k, int64_t group_size, void* stream);
+
 /* ---- Packed-format helpers on the device (int4gemv/quant.py:40-53), bit-exact ---------------- */
 
 /* q [N, K] int32 = the 4-bit values of qweight [N, K/8]   (quant.py:40-44). */

@@ -8,6 +8,8 @@
 #include <c10/cuda/CUDAStream.h>
 #include <torch/extension.h>
 
+#include <vector>
+
 #include "int4gemv_b200.h"
 #include "int4gemv_torch.h"
 
@@ -149,6 +151,33 @@ at::Tensor w4a16_silu_mul(const at::Tensor& x, const at::Tensor& qweight,
                                        scales.data_ptr(), zeros.data_ptr(), m, n, k, group_size,
                                        stream_of(x)));
   return y;
+}
+
+std::vector<at::Tensor> w4a16_grouped(const at::Tensor& x, const at::Tensor& qweight,
+                                      const at::Tensor& scales, const at::Tensor& zeros,
+                                      int64_t group_size, const std::vector<int64_t>& sizes) {
+  check_inputs("w4a16_grouped", x, qweight, scales, zeros, group_size, c10::DeviceType::CUDA);
+  TORCH_CHECK(!sizes.empty() && sizes.size() <= INT4GEMV_MAX_GROUP, "w4a16_grouped: between 1 and ",
+              INT4GEMV_MAX_GROUP, " matrices, got ", sizes.size());
+  int64_t total = 0;
+  for (int64_t n : sizes) {
+    TORCH_CHECK(n >= 0, "w4a16_grouped: negative matrix size ", n);
+    total += n;
+  }
+  TORCH_CHECK(total == qweight.size(0), "w4a16_grouped: sizes add up to ", total,
+              " rows, the stacked qweight has ", qweight.size(0));
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t m = x.size(0);
+  std::vector<at::Tensor> ys;
+  std::vector<void*> ptrs;
+  for (int64_t n : sizes) {
+    ys.push_back(x.new_empty({m, n}));
+    ptrs.push_back(ys.back().data_ptr());
+  }
+  check_status(int4gemv_w4a16_grouped(static_cast<int>(sizes.size()), ptrs.data(), sizes.data(),
+                                      x.data_ptr(), qweight.data_ptr(), scales.data_ptr(),
+                                      zeros.data_ptr(), m, x.size(1), group_size, stream_of(x)));
+  return ys;
 }
 
 at::Tensor w4a16_bias_residual(const at::Tensor& x, const at::Tensor& qweight,
@@ -334,6 +363,8 @@ PYBIND11_MODULE(int4gemv_ops, m) {
         py::arg("zeros"), py::arg("group_size"), py::arg("kernel"));
   m.def("w4a16_kernel", &int4gemv::w4a16_kernel, py::arg("x"), py::arg("qweight"),
         py::arg("scales"), py::arg("zeros"), py::arg("group_size"));
+  m.def("w4a16_grouped", &int4gemv::w4a16_grouped, py::arg("x"), py::arg("qweight"),
+        py::arg("scales"), py::arg("zeros"), py::arg("group_size"), py::arg("sizes"));
   m.def("w4a16_bias_residual", &int4gemv::w4a16_bias_residual, py::arg("x"), py::arg("qweight"),
         py::arg("scales"), py::arg("zeros"), py::arg("group_size"), py::arg("bias") = py::none(),
         py::arg("residual") = py::none());

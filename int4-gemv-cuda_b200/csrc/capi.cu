@@ -1,5 +1,6 @@
 // The C ABI (include/int4gemv_b200.h): argument checks with the reference's messages, dispatch to
 // the launchers, and error reporting through int4gemv_last_error(). No torch, no allocation.
+#include <algorithm>
 #include <climits>
 #include <cstdarg>
 #include <cstdio>
@@ -319,6 +320,52 @@ int int4gemv_w4a16(void* y, const void* x, const void* qweight, const void* scal
   return run_picked(name, make_args(y, x, qweight, scales, zeros, m, n, k, group_size), st);
 }
 
+int int4gemv_w4a16_grouped(int count, void* const* ys, const int64_t* ns, const void* x,
+                           const void* qweight, const void* scales, const void* zeros, int64_t m,
+                           int64_t k, int64_t group_size, void* stream) {
+  const char* name = "w4a16_grouped";
+  if (count < 1 || count > INT4GEMV_MAX_GROUP || !ys || !ns) {
+    return fail(INT4GEMV_ERR_INVALID, "%s: count %d must be in [1, %d] with ys and ns given", name,
+                count, INT4GEMV_MAX_GROUP);
+  }
+  int64_t total = 0;
+  i4::GroupOut go{};
+  go.count = count;
+  for (int i = 0; i < count; ++i) {
+    if (ns[i] < 0) return fail(INT4GEMV_ERR_INVALID, "%s: ns[%d] = %lld < 0", name, i,
+                               static_cast<long long>(ns[i]));
+    if (ns[i] > 0 && m > 0 && !ys[i]) return fail(INT4GEMV_ERR_INVALID, "%s: null ys[%d]", name, i);
+    total += ns[i];
+    go.y[i] = static_cast<half*>(ys[i]);
+    go.row_end[i] = static_cast<int>(std::min<int64_t>(total, INT_MAX));
+  }
+  if (int e = check_sizes(name, m, total, k, group_size)) return e;
+  if (int e = check_pointers(name, m, total, k, ys[0] ? ys[0] : x, x, qweight, scales, zeros)) {
+    return e;
+  }
+  const auto st = static_cast<cudaStream_t>(stream);
+  if (m == 0 || total == 0) return ok();
+  i4::GemvArgs a = make_args(ys[0], x, qweight, scales, zeros, m, total, k, group_size);
+  if (k > 0 && i4::stream_mma_supported(a, nullptr)) {
+    a.epilogue = i4::kGroupedY;
+    return launched(name, i4::launch_stream_mma(a, st, false, nullptr, &go));
+  }
+  // Other shapes: one launch per matrix on its rows of the stacked weights.
+  int64_t row0 = 0;
+  for (int i = 0; i < count; ++i) {
+    const int64_t groups = k / group_size;
+    const auto* q = static_cast<const uint32_t*>(qweight) + row0 * (k / 8);
+    const auto* sc = static_cast<const half*>(scales) + row0 * groups;
+    const auto* zc = static_cast<const half*>(zeros) + row0 * groups;
+    bool done;
+    int e = empty_cases(name, ys[i], m, ns[i], k, st, &done);
+    if (!done) e = run_picked(name, make_args(ys[i], x, q, sc, zc, m, ns[i], k, group_size), st);
+    if (e != INT4GEMV_OK) return e;
+    row0 += ns[i];
+  }
+  return ok();
+}
+
 int int4gemv_w4a16_bias_residual(void* y, const void* x, const void* qweight, const void* scales,
                                  const void* zeros, const void* bias, const void* residual,
                                  int64_t m, int64_t n, int64_t k, int64_t group_size,
@@ -514,6 +561,7 @@ int int4gemv_repack_gptq(void* qweight, void* scales, void* zeros, const void* g
 }
 
 static_assert(INT4GEMV_MAX_PEERS == i4::kMaxPeers, "peer count");
+static_assert(INT4GEMV_MAX_GROUP == i4::kMaxGroup, "group count");
 static_assert(INT4GEMV_PEER_FLAG_STRIDE == i4::kPeerFlagStride, "flag stride");
 
 size_t int4gemv_peers_struct_bytes(void) { return sizeof(int4gemv_peers_t); }

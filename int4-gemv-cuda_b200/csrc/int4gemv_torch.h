@@ -18,6 +18,7 @@
 #include <map>
 #include <string>
 #include <tuple>
+#include <vector>
 
 namespace int4gemv {
 
@@ -67,6 +68,12 @@ std::string w4a16_kernel(const at::Tensor& x, const at::Tensor& qweight, const a
 // interleaved (quant.interleave_rows); returns silu(x @ gate^T) * (x @ up^T), [M, N / 2] fp16.
 at::Tensor w4a16_silu_mul(const at::Tensor& x, const at::Tensor& qweight,
                           const at::Tensor& scales, const at::Tensor& zeros, int64_t group_size);
+
+// Several matrices sharing x, their packed weights stacked by rows (sizes[i] rows each): one
+// launch, one output [M, sizes[i]] per matrix.
+std::vector<at::Tensor> w4a16_grouped(const at::Tensor& x, const at::Tensor& qweight,
+                                      const at::Tensor& scales, const at::Tensor& zeros,
+                                      int64_t group_size, const std::vector<int64_t>& sizes);
 
 // x @ W^T + bias + residual with both additions fused into the GEMV's store (each optional;
 // bias [N], residual [M, N], float16), rounded to fp16 once.

@@ -14,7 +14,9 @@ namespace i4 {
 // kGatherPeers / kReducePeers: the fused exchange of a layer sharded over the ranks of one node
 // (PeerSet below): rows split (every rank's y gets this rank's columns) or K split (every rank
 // gets this rank's fp32 partial sums, then each adds all ranks' partials in rank order).
-enum Epilogue : int { kStoreY = 0, kSiluMul = 1, kGatherPeers = 2, kReducePeers = 3 };
+// kGroupedY: the rows of W are several matrices stacked (GroupOut below) and each matrix's
+// outputs go to its own y.
+enum Epilogue : int { kStoreY = 0, kSiluMul = 1, kGatherPeers = 2, kReducePeers = 3, kGroupedY = 4 };
 
 constexpr int kMaxPeers = 8;
 constexpr int kPeerFlagStride = 1024;  // flag words per source rank (>= CTAs of any launch)
@@ -37,6 +39,21 @@ struct PeerSet {
   long long out_half;
   int world, rank;
   int n_total, col0;
+};
+
+// Outputs of a grouped launch: matrix i is rows [row_end[i - 1], row_end[i]) of the stacked
+// weights (row_end[-1] = 0) and writes y[i] [m, row_end[i] - row_end[i - 1]].
+constexpr int kMaxGroup = 8;
+struct GroupOut {
+  half* y[kMaxGroup];
+  int row_end[kMaxGroup];
+  int count;
+};
+
+// Epilogue inputs beyond GemvArgs, one kernel parameter.
+struct EpilogueExtra {
+  PeerSet peers;
+  GroupOut groups;
 };
 
 struct GemvArgs {
@@ -94,7 +111,7 @@ cudaError_t tc_gemv_attrs(int m, KernelAttrs* out);
 // with programmatic stream serialization like launch_tc_gemv.
 bool stream_mma_supported(const GemvArgs& a, const char** why);
 cudaError_t launch_stream_mma(const GemvArgs& a, cudaStream_t stream, bool strict,
-                              const PeerSet* peers = nullptr);
+                              const PeerSet* peers = nullptr, const GroupOut* groups = nullptr);
 cudaError_t stream_mma_attrs(int m, KernelAttrs* out);
 
 // TMA-bulk-fed mma.sync pipeline (mma_pipeline.cu). `why` gets a reason when unsupported.

@@ -642,7 +642,8 @@ __device__ __forceinline__ void exchange_done(const PeerSet& peers, unsigned epo
 template <int MP, int MT, int CW, int MC>
 __global__ void __maxnreg__(CW == 16 ? 96 : 168)
     stream_mma_kernel(GemvArgs a, MmaPlan p, const __grid_constant__ WeightMaps maps,
-                      const __grid_constant__ PeerSet peers) {
+                      const __grid_constant__ EpilogueExtra ex) {
+  const PeerSet& peers = ex.peers;
   constexpr bool kNarrow = MP < 8;
   const int m_rows = MC > 0 ? MC : a.m;  // rows of x: compile-time where the instance has one M
   constexpr int kCW = CW;
@@ -828,6 +829,19 @@ __global__ void __maxnreg__(CW == 16 ? 96 : 168)
         a.y[static_cast<int64_t>(m) * (a.n / 2) + row_begin / 2 + i] = __float2half_rn(silu * up);
       }
     }
+  } else if (a.epilogue == kGroupedY) {
+    // Stacked matrices: row r of this CTA belongs to the matrix whose row range holds it.
+    const GroupOut& go = ex.groups;
+    for (int o = tid; o < rows * a.m; o += kConsumerThreads) {
+      const int m = o / rows;
+      const int row = row_begin + o - m * rows;
+      int gi = 0;
+      while (gi + 1 < go.count && row >= go.row_end[gi]) ++gi;
+      const int base = gi ? go.row_end[gi - 1] : 0;
+      const int ng = go.row_end[gi] - base;
+      const float sum = row_sum(row - row_begin, m);
+      if (in.ok) go.y[gi][static_cast<int64_t>(m) * ng + row - base] = __float2half_rn(sum);
+    }
   } else if (a.epilogue == kGatherPeers) {
     // This rank's columns of y into the current half of every rank's gather buffer; once this
     // CTA's counterparts on every rank have done the same, the rows they wrote (the same row
@@ -983,14 +997,17 @@ bool stream_mma_supported(const GemvArgs& a, const char** why) {
 }
 
 cudaError_t launch_stream_mma(const GemvArgs& a, cudaStream_t stream, bool strict,
-                              const PeerSet* peers) {
+                              const PeerSet* peers, const GroupOut* groups) {
   MmaPlan p;
   if (!make_plan(a, &p, nullptr)) return cudaErrorInvalidValue;
   const bool exchange = a.epilogue == kGatherPeers || a.epilogue == kReducePeers;
   if (exchange != (peers != nullptr) || (exchange && p.ctas > kPeerFlagStride)) {
     return cudaErrorInvalidValue;
   }
-  const PeerSet ps = peers ? *peers : PeerSet{};
+  if ((a.epilogue == kGroupedY) != (groups != nullptr)) return cudaErrorInvalidValue;
+  EpilogueExtra ex{};
+  if (peers) ex.peers = *peers;
+  if (groups) ex.groups = *groups;
   p.strict = strict ? 1 : 0;
   p.status = device_status_word();
   if (!p.status) return cudaErrorInvalidSymbol;
@@ -1017,7 +1034,7 @@ cudaError_t launch_stream_mma(const GemvArgs& a, cudaStream_t stream, bool stric
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, stream_mma_kernel<MP, MT, CW, MC>, a, p, maps, ps);
+    return cudaLaunchKernelEx(&cfg, stream_mma_kernel<MP, MT, CW, MC>, a, p, maps, ex);
   });
 }
 

@@ -36,6 +36,8 @@ _PROTOTYPES = {
     "int4gemv_w4a16_silu_mul": (ctypes.c_int, [_p] * 5 + [_i64] * 4 + [_p]),
     "int4gemv_unpack": (ctypes.c_int, [_p, _p, _i64, _i64, _p]),
     "int4gemv_dequantize": (ctypes.c_int, [_p] * 4 + [_i64] * 3 + [_p]),
+    "int4gemv_w4a16_grouped": (ctypes.c_int, [ctypes.c_int, _p, _p] + [_p] * 4 + [_i64] * 3
+                               + [_p]),
     "int4gemv_w4a16_bias_residual": (ctypes.c_int, [_p] * 7 + [_i64] * 4 + [_p]),
     "int4gemv_repack_awq": (ctypes.c_int, [_p] * 6 + [_i64] * 3 + [_p]),
     "int4gemv_repack_gptq": (ctypes.c_int, [_p] * 6 + [ctypes.c_int] + [_i64] * 3 + [_p]),

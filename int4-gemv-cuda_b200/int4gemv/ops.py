@@ -66,6 +66,7 @@ w4a16_kernel = int4gemv_ops.w4a16_kernel
 w4a16_with = int4gemv_ops.w4a16_with
 w4a16_silu_mul = int4gemv_ops.w4a16_silu_mul
 w4a16_bias_residual = int4gemv_ops.w4a16_bias_residual
+w4a16_grouped = int4gemv_ops.w4a16_grouped
 unpack = int4gemv_ops.unpack
 dequantize = int4gemv_ops.dequantize
 quantize = int4gemv_ops.quantize

@@ -83,3 +83,9 @@ def interleave_rows(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     if gate.shape != up.shape:
         raise ValueError(f"gate and up shapes differ: {tuple(gate.shape)} vs {tuple(up.shape)}")
     return torch.stack((gate, up), dim=1).reshape(2 * gate.shape[0], *gate.shape[1:]).contiguous()
+
+
+def stack_rows(*tensors: torch.Tensor) -> torch.Tensor:
+    """The matrices' rows one after another (any of qweight, scales, zeros): the stacked layout
+    ops.w4a16_grouped reads, built once at load time."""
+    return torch.cat(tensors, dim=0).contiguous()

@@ -399,3 +399,35 @@ def test_bias_residual_in_place_and_empty():
         ops.w4a16_bias_residual(tx, tq, ts, tz, 128, bias=tb[:-1])
     with pytest.raises(RuntimeError, match="residual must be"):
         ops.w4a16_bias_residual(tx, tq, ts, tz, 128, residual=tr.t())
+
+
+# Grouped launch: matrices sharing x, weights stacked by rows, one output per matrix.
+GROUPED = [(1, [4096, 1024, 1024], 4096, 128), (4, [4096, 1024, 1024], 4096, 128),
+           (17, [300, 5, 0, 77], 2048, 128), (2, [14336, 14336], 4096, 128),
+           (3, [200, 96], 768, 64)]
+
+
+@pytest.mark.parametrize("m,sizes,k,g", GROUPED,
+                         ids=[f"m{m}_{'-'.join(map(str, s))}_k{k}_g{g}" for m, s, k, g in GROUPED])
+def test_grouped(m, sizes, k, g):
+    from int4gemv import quant
+
+    x = oracle.synthetic(m, 8, k, g, seed=m)[0]
+    mats = [oracle.synthetic(1, max(n, 1), k, g, seed=100 * i + n)[1:] for i, n in enumerate(sizes)]
+    mats = [tuple(t[:n] for t in mat) for mat, n in zip(mats, sizes)]
+    stacked = [quant.stack_rows(*cuda(*(mat[j] for mat in mats))) for j in range(3)]
+    ys = ops.w4a16_grouped(cuda(x)[0], *stacked, g, sizes)
+    torch.cuda.synchronize()
+    assert len(ys) == len(sizes)
+    for (q, s, z), n, y in zip(mats, sizes, ys):
+        assert tuple(y.shape) == (m, n)
+        if n:
+            assert_close(y, oracle.reference(x, q, s, z, g), f"grouped matrix of {n} rows")
+
+
+def test_grouped_rejects():
+    x, q, s, z = cuda(*oracle.synthetic(1, 64, 1024, 128))
+    with pytest.raises(RuntimeError, match="add up to"):
+        ops.w4a16_grouped(x, q, s, z, 128, [32, 16])
+    with pytest.raises(RuntimeError, match="between 1 and 8"):
+        ops.w4a16_grouped(x, q, s, z, 128, [8] * 8 + [0])
