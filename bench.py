@@ -336,6 +336,33 @@ def time_quantize(n: int = 28672, k: int = 8192, calls: int = 20) -> dict:
             "gb_s": round(moved / sec / 1e9, 1), "frac_of_hbm": round(moved / sec / 1e9 / peak[0], 4)}
 
 
+def time_grouped(k: int = 4096, sizes=(4096, 1024, 1024)) -> dict:
+    """q / k / v of a Llama-3-8B attention block at M = 1 (shared x, K = 4096): one grouped launch
+    (ops.w4a16_grouped on stacked weights) against three ops.w4a16 launches, CUDA-graph replays
+    over enough weight sets that every call streams from HBM."""
+    from int4gemv import ops, quant
+
+    n_total = sum(sizes)
+    set_bytes = n_total * k // 2 + 2 * n_total * (k // GROUP) * 2
+    n_sets = math.ceil(2 * L2_BYTES / set_bytes) + 1
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn(1, k, generator=gen, device="cuda", dtype=torch.float16)
+    sets = []
+    for _ in range(n_sets):
+        mats = [ops.quantize(torch.randn(n, k, generator=gen, device="cuda",
+                                         dtype=torch.float16) * 0.02, GROUP) for n in sizes]
+        sets.append((mats, [quant.stack_rows(*(mt[j] for mt in mats)) for j in range(3)]))
+    separate = [lambda mats=mats, i=i: ops.w4a16(x, *mats[i], GROUP)
+                for mats, _ in sets for i in range(len(sizes))]
+    grouped = [lambda st=st: ops.w4a16_grouped(x, *st, GROUP, list(sizes)) for _, st in sets]
+    sep_s = time_graph_calls(separate, 300 * len(separate), 3 * len(separate)) * len(sizes)
+    grp_s = time_graph_calls(grouped, 300 * len(grouped), 3 * len(grouped))
+    del sets
+    return {"shape": {"k": k, "n": list(sizes), "m": 1},
+            "separate_launches_us": round(sep_s * 1e6, 2), "grouped_us": round(grp_s * 1e6, 2),
+            "speedup": round(sep_s / grp_s, 3)}
+
+
 def time_sharded(world: int, rank: int, reps: int = 5) -> dict:
     """The sharded configs of the multi-GPU rows (up 28672 x 8192 rows split, down 8192 x 28672 K
     split, M = 1 and 8) on this job's ranks: the fused exchange (int4gemv.exchange) against the
@@ -545,6 +572,7 @@ def run_ours(args, world, rank, local):
         vv = [(lambda i=i: ops.vectorized(x, *sets[i], GROUP)) for i in range(n_sets)]
         extra["vectorized_us"] = round(time_graph_calls(vv * max(1, 64 // n_sets), 5000, 100) * 1e6, 3)
         extra["quantize"] = time_quantize()
+        extra["grouped_qkv"] = time_grouped()
 
     # ---- end to end through the public API with host buffers
     x_host = x.cpu().pin_memory()
