@@ -236,6 +236,20 @@ int int4gemv_w4a16_exchange(void* y, const void* x, const void* qweight, const v
                             const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
                             const int4gemv_peers_t* peers, void* stream);
 
+/* int4gemv_w4a16_exchange for a single rank (world 1, rank 0) with no allocation at all: its
+ * exchange buffer and flag / call-counter words are a static device array in the library
+ * (4 MiB + 8 KiB per device), so no int4gemv_peer_alloc and no caller buffers. mode
+ * INT4GEMV_SHARD_ROWS or INT4GEMV_SHARD_K; y [m, n] fp16 as int4gemv_w4a16 computes it, through
+ * the exchange epilogue. Sizes needing more than the static buffer (ROWS: m x n > 1 Mi; K:
+ * m x n > 512 Ki) are rejected with INT4GEMV_ERR_INVALID and a message giving the limit.
+ * The first call on a device does the setup (looks up the array with cudaGetSymbolAddress and
+ * clears the flag words, synchronously), so it must come before any stream capture. All calls on
+ * a device share the one buffer: calls that overlap in time (different streams, or other host
+ * threads) race. No counterpart in the reference. */
+int int4gemv_w4a16_exchange_static(void* y, const void* x, const void* qweight,
+                                   const void* scales, const void* zeros, int64_t m, int64_t n,
+                                   int64_t k, int64_t group_size, int mode, void* stream);
+
 /* ---- Device-side status --------------------------------------------------------------------- */
 
 /* Reads and clears the current device's kernel status word: 0 if every pipelined kernel since the

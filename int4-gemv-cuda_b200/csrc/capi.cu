@@ -1,10 +1,12 @@
 // The C ABI (include/int4gemv_b200.h): argument checks with the reference's messages, dispatch to
-// the launchers, and error reporting through int4gemv_last_error(). No torch, no allocation.
+// the launchers, and error reporting through int4gemv_last_error(). No torch; the only device
+// allocation is int4gemv_peer_alloc's, which the caller asks for.
 #include <algorithm>
 #include <climits>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "int4gemv_b200.h"
@@ -173,6 +175,47 @@ int run_picked(const char* name, const i4::GemvArgs& a, cudaStream_t st) {
   }
 }
 
+}  // namespace
+
+// ---- Scratch of int4gemv_w4a16_exchange_static: static device memory, no allocation ---------
+// A single rank's exchange buffer (two halves) and its flag and call-counter words
+// (INT4GEMV_PEER_FLAG_BYTES(1)), in module memory of every device the library is loaded on.
+constexpr int64_t kStaticExchangeBytes = 4 << 20;
+constexpr int kStaticFlagWords = 2 * INT4GEMV_PEER_FLAG_STRIDE;
+static __device__ __align__(256) unsigned char g_static_exchange[kStaticExchangeBytes];
+static __device__ __align__(256) unsigned g_static_flags[kStaticFlagWords];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mu;
+void* g_static_out[kMaxDevices];
+void* g_static_flag_ptr[kMaxDevices];
+
+// The current device's static scratch. The first call on a device looks the symbols up and
+// clears the flag words (synchronously: it must not happen inside a stream capture).
+int static_scratch(const char* name, void** out, void** flags) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return cuda_fail(name, err);
+  if (dev < 0 || dev >= kMaxDevices) {
+    return fail(INT4GEMV_ERR_INVALID, "%s: device %d out of range", name, dev);
+  }
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (!g_static_out[dev]) {
+    void* o = nullptr;
+    void* f = nullptr;
+    err = cudaGetSymbolAddress(&o, g_static_exchange);
+    if (err == cudaSuccess) err = cudaGetSymbolAddress(&f, g_static_flags);
+    if (err == cudaSuccess) err = cudaMemset(f, 0, sizeof(unsigned) * kStaticFlagWords);
+    if (err == cudaSuccess) err = cudaDeviceSynchronize();
+    if (err != cudaSuccess) return cuda_fail(name, err);
+    g_static_flag_ptr[dev] = f;
+    g_static_out[dev] = o;
+  }
+  *out = g_static_out[dev];
+  *flags = g_static_flag_ptr[dev];
+  return INT4GEMV_OK;
+}
 }  // namespace
 
 extern "C" {
@@ -657,6 +700,40 @@ int int4gemv_w4a16_exchange(void* y, const void* x, const void* qweight, const v
   ps.n_total = static_cast<int>(n_out);
   ps.col0 = static_cast<int>(mode == INT4GEMV_SHARD_ROWS ? peers->col0 : 0);
   return launched(name, i4::launch_stream_mma(a, static_cast<cudaStream_t>(stream), false, &ps));
+}
+
+int int4gemv_w4a16_exchange_static(void* y, const void* x, const void* qweight,
+                                   const void* scales, const void* zeros, int64_t m, int64_t n,
+                                   int64_t k, int64_t group_size, int mode, void* stream) {
+  const char* name = "w4a16_exchange_static";
+  if (mode != INT4GEMV_SHARD_ROWS && mode != INT4GEMV_SHARD_K) {
+    return fail(INT4GEMV_ERR_INVALID, "%s: unknown mode %d", name, mode);
+  }
+  if (m < 0 || n < 0) return fail(INT4GEMV_ERR_INVALID, "%s: negative size", name);
+  const int64_t half = m * n * (mode == INT4GEMV_SHARD_ROWS ? 2 : 4);
+  if (2 * half > kStaticExchangeBytes) {
+    return fail(INT4GEMV_ERR_INVALID,
+                "%s: M = %lld, N = %lld needs %lld bytes of exchange buffer; the static buffer "
+                "holds %lld (M x N <= %lld in this mode)",
+                name, static_cast<long long>(m), static_cast<long long>(n),
+                static_cast<long long>(2 * half), static_cast<long long>(kStaticExchangeBytes),
+                static_cast<long long>(kStaticExchangeBytes / 2 /
+                                       (mode == INT4GEMV_SHARD_ROWS ? 2 : 4)));
+  }
+  void* out = nullptr;
+  void* flags = nullptr;
+  if (int e = static_scratch(name, &out, &flags)) return e;
+  int4gemv_peers_t peers{};
+  peers.world = 1;
+  peers.rank = 0;
+  peers.mode = mode;
+  peers.n_total = n;
+  peers.col0 = 0;
+  peers.out_bytes = kStaticExchangeBytes;
+  peers.out[0] = out;
+  peers.flags[0] = flags;
+  return int4gemv_w4a16_exchange(y, x, qweight, scales, zeros, m, n, k, group_size, &peers,
+                                 stream);
 }
 
 int int4gemv_device_status(int* status) {

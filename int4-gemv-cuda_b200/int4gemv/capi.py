@@ -50,6 +50,7 @@ _PROTOTYPES = {
     "int4gemv_peer_close": (ctypes.c_int, [_p]),
     "int4gemv_peer_free": (ctypes.c_int, [_p]),
     "int4gemv_w4a16_exchange": (ctypes.c_int, [_p] * 5 + [_i64] * 4 + [_p, _p]),
+    "int4gemv_w4a16_exchange_static": (ctypes.c_int, [_p] * 5 + [_i64] * 4 + [ctypes.c_int, _p]),
 }
 
 MAX_PEERS = 8
