@@ -369,7 +369,7 @@ def time_sharded(world: int, rank: int, reps: int = 5) -> dict:
     NCCL stack (int4gemv.sharded), both replayed from CUDA graphs, device time max over ranks.
     Enough layers with distinct weights rotate through each graph that every call streams its
     shard from HBM (more than 2x L2 per rank)."""
-    from int4gemv import ops
+    from int4gemv import capi, ops
     from int4gemv.exchange import FusedShardedW4A16
     from int4gemv.sharded import ShardedW4A16
 
@@ -395,6 +395,13 @@ def time_sharded(world: int, rank: int, reps: int = 5) -> dict:
                 for layer in stack:
                     layer(x)
                 torch.cuda.synchronize()
+                if label == "fused_us":
+                    # every rank learns whether any rank's bounded peer wait ran out
+                    bad = max_over_ranks(float(capi.device_status()), world)
+                    if bad:
+                        row[label] = None
+                        row["fused_error"] = f"device status {int(bad)} (peer wait ran out)"
+                        continue
                 graph = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(graph):
                     for layer in stack:
@@ -411,9 +418,10 @@ def time_sharded(world: int, rank: int, reps: int = 5) -> dict:
                 sec = max_over_ranks(e0.elapsed_time(e1) / 1e3, world) / (reps * layers)
                 row[label] = round(sec * 1e6, 2)
                 del graph
-            row["speedup_fused_vs_nccl"] = round(row["nccl_us"] / row["fused_us"], 3)
-            row["fused_gb_s_total"] = round(int4_bytes(m, n, k, GROUP) / (row["fused_us"] / 1e6)
-                                            / 1e9, 1)
+            if row["fused_us"]:
+                row["speedup_fused_vs_nccl"] = round(row["nccl_us"] / row["fused_us"], 3)
+                row["fused_gb_s_total"] = round(int4_bytes(m, n, k, GROUP)
+                                                / (row["fused_us"] / 1e6) / 1e9, 1)
             res[f"m{m}"] = row
         torch.cuda.synchronize()
         barrier(world)
