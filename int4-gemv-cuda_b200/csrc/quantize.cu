@@ -9,22 +9,27 @@
 //   pack (quant.py:32-37): word = sum_j q[8w + j] << 4j, modulo 2^32 (so out-of-range q wrap the
 //   same way the reference's int64 sum does after its cast to int32).
 //
-// Every fp32 operation is one IEEE operation rounded to nearest even (__fsub_rn, __fdiv_rn,
-// __fadd_rn: no contraction, no approximate division), which is what torch's CPU and CUDA
-// elementwise kernels compute. The sign of a zero zero-point follows the first minimal element of
-// the group in k order (lo = -0.0 gives z = +0.0, lo = +0.0 gives z = -0.0), as a sequential scan
-// does; ties of min are therefore broken by position in the reductions below.
+// The reference computes each of these as one IEEE fp32 operation rounded to nearest even; the
+// group parameters here do the same (__fsub_rn, __fdiv_rn: no contraction, no approximate
+// division). For q, w / s is first estimated as w * (1 / s) (one correctly rounded reciprocal per
+// group, then a fused multiply-add with z), which can only round differently from the reference
+// when the value lies within 1e-5 of a half-integer; any word with a weight within 1e-4 of one is
+// recomputed with IEEE division (quantize_word). The sign of a zero zero-point follows the first
+// minimal element of the group in k order (lo = -0.0 gives z = +0.0, lo = +0.0 gives z = -0.0),
+// as a sequential scan does (first_zero_key).
 //
-// Mapping. Each thread owns one packed word: it loads the word's 8 weights (32 B of fp32 or 16 B
-// of fp16 / bf16, one or two vector loads), so a warp reads 1 KB (512 B) of contiguous weights and
-// writes 128 B of contiguous words. When a group spans a power-of-two number of words <= 32, the
-// group's threads are an aligned segment of one warp and reduce min / max with xor shuffles inside
-// the segment; other group sizes take one warp per group with a loop over the group's words.
-// The path is HBM-bound: per weight it reads 4 (or 2) bytes and writes 0.5 + 4 / group bytes.
+// Mapping. Each thread owns two consecutive packed words (16 weights: 64 B of fp32 or 32 B of
+// fp16 / bf16), so a warp reads 2 KB (1 KB) of contiguous weights and writes 256 B of words. When
+// a group spans a power-of-two number of words <= 64, its threads are an aligned segment of one
+// warp and reduce min / max with xor shuffles inside the segment; other group sizes take one warp
+// per group with a loop over the group's words. The path is HBM-bound: per weight it reads 4 (or
+// 2) bytes and writes 0.5 + 4 / group bytes.
 #include "common.cuh"
 #include "kernels.h"
 
 #include <cuda_bf16.h>
+
+#include <climits>
 
 namespace i4 {
 namespace {
@@ -56,41 +61,49 @@ __device__ __forceinline__ void load8(const void* w, int64_t word, float (&v)[8]
   }
 }
 
-// Running minimum with its position: a later element replaces the minimum only when strictly
-// smaller, or equal (+0 / -0) and earlier in k.
-struct MinPos {
-  float v;
-  int pos;
-};
-
-__device__ __forceinline__ void take_min(MinPos& a, float v, int pos) {
-  if (v < a.v || (v == a.v && pos < a.pos)) {
-    a.v = v;
-    a.pos = pos;
-  }
-}
-
-// Min (with position) and max over the 8 weights of one word; `pos0` = position of v[0].
-__device__ __forceinline__ void scan8(const float (&v)[8], int pos0, MinPos& lo, float& hi) {
+// Min and max over a thread's weights; the position of the first zero matters only when the
+// group's minimum is a zero (see first_zero_key).
+template <int N>
+__device__ __forceinline__ void min_max(const float (&v)[N][8], float& lo, float& hi) {
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    take_min(lo, v[j], pos0 + j);
-    hi = fmaxf(hi, v[j]);
-  }
+  for (int t = 0; t < N; ++t)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      lo = fminf(lo, v[t][j]);
+      hi = fmaxf(hi, v[t][j]);
+    }
 }
 
-// Reduction over the lanes of an aligned segment of `width` lanes (a power of two <= 32).
-__device__ __forceinline__ void segment_reduce(MinPos& lo, float& hi, int width) {
+// 2 * (position in the group of the thread's first zero weight) + its sign bit, or INT_MAX.
+// `pos0` = position of v[0][0]. The smallest key over the group gives the sign that a sequential
+// scan (which keeps the first of equal minima) leaves in lo.
+template <int N>
+__device__ __forceinline__ int first_zero_key(const float (&v)[N][8], int pos0) {
+#pragma unroll
+  for (int t = 0; t < N; ++t)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (v[t][j] == 0.0f) return 2 * (pos0 + 8 * t + j) + (__float_as_uint(v[t][j]) >> 31);
+    }
+  return INT_MAX;
+}
+
+// Reduction over an aligned segment of `width` lanes (a power of two <= 32).
+__device__ __forceinline__ void segment_min_max(float& lo, float& hi, int width) {
   for (int off = width >> 1; off > 0; off >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, lo.v, off);
-    const int op = __shfl_xor_sync(0xffffffffu, lo.pos, off);
-    take_min(lo, ov, op);
+    lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, off));
     hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, off));
   }
 }
 
+__device__ __forceinline__ int segment_min(int key, int width) {
+  for (int off = width >> 1; off > 0; off >>= 1) key = min(key, __shfl_xor_sync(0xffffffffu, key, off));
+  return key;
+}
+
 struct GroupParams {
   float s;  // fp16-rounded scale, as fp32
+  float r;  // 1 / s, correctly rounded: the estimate of w / s is w * r
   float z;  // zero point 0..15 (possibly -0.0)
   half s_h, z_h;
 };
@@ -103,6 +116,7 @@ __device__ __forceinline__ GroupParams group_params(float lo, float hi) {
   GroupParams g;
   g.s_h = __float2half_rn(s);
   g.s = __half2float(g.s_h);
+  g.r = __frcp_rn(g.s);
   float z = rintf(__fdiv_rn(-lo, g.s));
   if (z < 0.0f) z = 0.0f;
   if (z > 15.0f) z = 15.0f;
@@ -111,22 +125,54 @@ __device__ __forceinline__ GroupParams group_params(float lo, float hi) {
   return g;
 }
 
-__device__ __forceinline__ uint32_t quantize_word(const float (&v)[8], const GroupParams& g) {
+// q = clamp(rint(fl(fl(w / s) + z)), 0, 15) with IEEE division: the reference's arithmetic.
+__device__ __forceinline__ uint32_t quantize_word_exact(const float (&v)[8], const GroupParams& g) {
   uint32_t word = 0;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     float q = rintf(__fadd_rn(__fdiv_rn(v[j], g.s), g.z));
-    if (q < 0.0f) q = 0.0f;
-    if (q > 15.0f) q = 15.0f;
+    q = fminf(fmaxf(q, 0.0f), 15.0f);
     word |= static_cast<uint32_t>(q) << (4 * j);
   }
   return word;
 }
 
-// Groups of `width` words, width a power of two <= 32: segments of one warp. Warp-uniform loop
-// over chunks of 32 words; lanes past the end compute on clamped data and store nothing (segments
-// never straddle the end because the word count is a multiple of width).
-template <int DT>
+// Adding 1.5 * 2^23 to c in [0, 15] rounds it to an integer, half to even, held in the low
+// mantissa bits: bits = 0x4B400000 + rint(c).
+constexpr float kRoundMagic = 12582912.0f;
+__host__ __device__ constexpr uint32_t magic_sum() {
+  uint32_t s = 0;
+  for (int j = 0; j < 8; ++j) s += 0x4B400000u << (4 * j);
+  return s;
+}
+
+// The same word from the estimate t = w * (1 / s) + z: w * r and the fma are within 2e-7
+// relative of w / s + z, so for every in-range weight (|w / s| <= 15.01, z <= 15) the estimate and
+// the reference's value differ by less than 1e-5. Clamping before rounding gives the same q as
+// rounding before clamping (0 and 15 are integers). They can round differently only when the
+// clamped estimate lies within 1e-5 of a half-integer, so a word with any weight within 1e-4 of
+// one is recomputed exactly. Packing: sum_j bits_j << 4j minus the magic's share, one multiply-add
+// per weight.
+__device__ __forceinline__ uint32_t quantize_word(const float (&v)[8], const GroupParams& g) {
+  uint32_t acc = 0;
+  float dmax = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float c = fminf(fmaxf(fmaf(v[j], g.r, g.z), 0.0f), 15.0f);
+    const float m = __fadd_rn(c, kRoundMagic);
+    dmax = fmaxf(dmax, fabsf(__fsub_rn(c, __fsub_rn(m, kRoundMagic))));
+    acc += __float_as_uint(m) << (4 * j);
+  }
+  if (dmax > 0.4999f) return quantize_word_exact(v, g);
+  constexpr uint32_t kMagicSum = magic_sum();
+  return acc - kMagicSum;
+}
+
+// Groups of `width` lanes x WPT words (width a power of two <= 32): aligned segments of one warp.
+// Warp-uniform loop over chunks of 32 WPT words; lanes past the end compute on clamped data and
+// store nothing (segments never straddle the end because the word count is a multiple of a
+// group's words).
+template <int DT, int WPT>
 __global__ void __launch_bounds__(kThreads) quantize_segment_kernel(
     uint32_t* __restrict__ qw, half* __restrict__ s, half* __restrict__ z,
     const void* __restrict__ w, int64_t words, int width) {
@@ -134,20 +180,29 @@ __global__ void __launch_bounds__(kThreads) quantize_segment_kernel(
   const int64_t warp = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
   const int64_t warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
   const int seg_lane = lane & (width - 1);
-  for (int64_t base = warp * 32; base < words; base += warps * 32) {
-    const int64_t i = base + lane;
-    const bool live = i < words;
-    float v[8];
-    load8<DT>(w, live ? i : words - 1, v);
-    MinPos lo{v[0], 8 * seg_lane};
-    float hi = v[0];
-    scan8(v, 8 * seg_lane, lo, hi);
-    segment_reduce(lo, hi, width);
-    const GroupParams g = group_params(lo.v, hi);
+  for (int64_t base = warp * 32 * WPT; base < words; base += warps * 32 * WPT) {
+    const int64_t i0 = base + lane * WPT;
+    const bool live = i0 < words;
+    float v[WPT][8];
+#pragma unroll
+    for (int t = 0; t < WPT; ++t) load8<DT>(w, live ? i0 + t : words - WPT + t, v[t]);
+    float lo = v[0][0], hi = v[0][0];
+    min_max(v, lo, hi);
+    segment_min_max(lo, hi, width);
+    if (lo == 0.0f) {  // uniform over the segment
+      const int key = segment_min(first_zero_key(v, 8 * WPT * seg_lane), width);
+      lo = (key & 1) ? -0.0f : 0.0f;
+    }
+    const GroupParams g = group_params(lo, hi);
     if (!live) continue;
-    qw[i] = quantize_word(v, g);
+    if constexpr (WPT == 2) {
+      *reinterpret_cast<uint2*>(qw + i0) = make_uint2(quantize_word(v[0], g),
+                                                      quantize_word(v[1], g));
+    } else {
+      qw[i0] = quantize_word(v[0], g);
+    }
     if (seg_lane == 0) {
-      const int64_t grp = i / width;
+      const int64_t grp = i0 / (static_cast<int64_t>(width) * WPT);
       s[grp] = g.s_h;
       z[grp] = g.z_h;
     }
@@ -164,15 +219,23 @@ __global__ void __launch_bounds__(kThreads) quantize_group_kernel(
   const int64_t warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
   for (int64_t grp = warp; grp < groups; grp += warps) {
     const int64_t first = grp * width;
-    MinPos lo{INFINITY, 0x7fffffff};
-    float hi = -INFINITY;
+    float lo = INFINITY, hi = -INFINITY;
     for (int j = lane; j < width; j += 32) {
-      float v[8];
-      load8<DT>(w, first + j, v);
-      scan8(v, 8 * j, lo, hi);
+      float v[1][8];
+      load8<DT>(w, first + j, v[0]);
+      min_max(v, lo, hi);
     }
-    segment_reduce(lo, hi, 32);
-    const GroupParams g = group_params(lo.v, hi);
+    segment_min_max(lo, hi, 32);
+    if (lo == 0.0f) {
+      int key = INT_MAX;
+      for (int j = lane; j < width; j += 32) {
+        float v[1][8];
+        load8<DT>(w, first + j, v[0]);
+        key = min(key, first_zero_key(v, 8 * j));
+      }
+      lo = (segment_min(key, 32) & 1) ? -0.0f : 0.0f;
+    }
+    const GroupParams g = group_params(lo, hi);
     for (int j = lane; j < width; j += 32) {
       float v[8];
       load8<DT>(w, first + j, v);
@@ -213,14 +276,18 @@ template <int DT>
 cudaError_t launch_quantize_t(uint32_t* qweight, half* s, half* z, const void* w, int64_t n,
                               int64_t k, int64_t group, cudaStream_t stream) {
   const int64_t words = n * (k / 8);
-  const int width = static_cast<int>(group / 8);
-  if ((width & (width - 1)) == 0 && width <= 32) {
-    quantize_segment_kernel<DT><<<grid_for(words), kThreads, 0, stream>>>(qweight, s, z, w,
-                                                                           words, width);
+  const int gw = static_cast<int>(group / 8);  // words per group
+  const bool pow2 = (gw & (gw - 1)) == 0;
+  if (pow2 && gw >= 2 && gw <= 64) {  // two words per thread, gw / 2 lanes per group
+    quantize_segment_kernel<DT, 2><<<grid_for(words / 2), kThreads, 0, stream>>>(
+        qweight, s, z, w, words, gw / 2);
+  } else if (gw == 1) {
+    quantize_segment_kernel<DT, 1><<<grid_for(words), kThreads, 0, stream>>>(qweight, s, z, w,
+                                                                              words, 1);
   } else {
     const int64_t groups = n * (k / group);
     quantize_group_kernel<DT><<<grid_for(groups * 32), kThreads, 0, stream>>>(qweight, s, z, w,
-                                                                               groups, width);
+                                                                               groups, gw);
   }
   return cudaGetLastError();
 }
