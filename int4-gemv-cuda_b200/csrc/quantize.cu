@@ -147,7 +147,7 @@ __host__ __device__ constexpr uint32_t magic_sum() {
 }
 
 // The same word from the estimate t = w * (1 / s) + z: w * r and the fma are within 2e-7
-// relative of w / s + z, so for every in-range weight (|w / s| <= 15.01, z <= 15) the estimate and
+// relative of w / s + z, so for every in-range weight (|w / s| < 16, also when s is an fp16 subnormal, and z <= 15) the estimate and
 // the reference's value differ by less than 1e-5. Clamping before rounding gives the same q as
 // rounding before clamping (0 and 15 are integers). They can round differently only when the
 // clamped estimate lies within 1e-5 of a half-integer, so a word with any weight within 1e-4 of
