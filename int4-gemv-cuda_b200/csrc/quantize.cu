@@ -146,13 +146,13 @@ __host__ __device__ constexpr uint32_t magic_sum() {
   return s;
 }
 
-// The same word from the estimate t = w * (1 / s) + z: w * r and the fma are within 2e-7
-// relative of w / s + z, so for every in-range weight (|w / s| < 16, also when s is an fp16 subnormal, and z <= 15) the estimate and
-// the reference's value differ by less than 1e-5. Clamping before rounding gives the same q as
-// rounding before clamping (0 and 15 are integers). They can round differently only when the
-// clamped estimate lies within 1e-5 of a half-integer, so a word with any weight within 1e-4 of
-// one is recomputed exactly. Packing: sum_j bits_j << 4j minus the magic's share, one multiply-add
-// per weight.
+// The same word from the estimate t = fma(w, 1 / s, z). For every weight of the group |w / s| < 16
+// (also when s rounds to an fp16 subnormal) and z <= 15, so the estimate and the reference's
+// fl(fl(w / s) + z) are both within 3e-6 of the exact value. Clamping before rounding gives the
+// same q as rounding before clamping (0 and 15 are integers), so they can round differently only
+// when the clamped estimate lies within 1e-5 of a half-integer; a word with any weight within 1e-4
+// of one is recomputed exactly. Packing: sum_j bits_j << 4j minus the magic's share, one integer
+// multiply-add per weight.
 __device__ __forceinline__ uint32_t quantize_word(const float (&v)[8], const GroupParams& g) {
   uint32_t acc = 0;
   float dmax = 0.0f;
