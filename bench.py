@@ -606,7 +606,12 @@ def run_ours(args, world, rank, local):
            "us_per_call": round(e2e_s * 1e6, 3),
            "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2}
 
-    sharded = time_sharded(world, rank) if world > 1 and not args.no_sharded else None
+    sharded = None
+    if world > 1 and not args.no_sharded:
+        try:
+            sharded = time_sharded(world, rank)
+        except Exception as e:  # the headline line is printed either way
+            sharded = {"error": f"{type(e).__name__}: {e}"[:300]}
 
     peak, peak_kind = measured_peak()
     achieved = bytes_call / launch_s / 1e9
