@@ -197,11 +197,9 @@ int int4gemv_peer_close(void* ptr);
 int int4gemv_peer_free(void* ptr);
 
 #define INT4GEMV_MAX_PEERS 8
-#define INT4GEMV_SHARD_ROWS 0          /* N split: every rank gets y [m, n_total] (all-gather) */
-#define INT4GEMV_SHARD_K 1             /* K split: every rank gets y [m, n] = sum of partials */
-#define INT4GEMV_PEER_FLAG_STRIDE 1024 /* flag words per source rank */
-/* Bytes of one rank's flag buffer: the flag words, then one call counter per CTA. */
-#define INT4GEMV_PEER_FLAG_BYTES(world) (((int64_t)(world) + 1) * INT4GEMV_PEER_FLAG_STRIDE * 4)
+#define INT4GEMV_SHARD_ROWS 0  /* N split: every rank gets y [m, n_total] (all-gather) */
+#define INT4GEMV_SHARD_K 1     /* K split: every rank gets y [m, n] = sum of partials */
+#define INT4GEMV_PEER_COUNTER_BYTES 4096  /* a rank's call counter words */
 
 typedef struct {
   int32_t world, rank, mode, reserved;
@@ -209,14 +207,15 @@ typedef struct {
   int64_t col0;       /* ROWS: first column of this rank's shard in y; must be n x rank */
   int64_t out_bytes;  /* size of every rank's out buffer, the same on every rank */
   /* out[r]: rank r's exchange buffer, mapped here (out[rank] is this rank's own), two halves used
-   * by alternate calls. ROWS: a half holds [m, n_total] fp16 (out_bytes >= 4 m n_total). K: a
-   * half holds [world, m, n] fp32 (out_bytes >= 8 world m n). */
+   * by alternate calls, each an array of 8-byte words (data and call number in one store).
+   * ROWS: a half holds m x n_total words (out_bytes >= 16 m n_total). K: a half holds
+   * world x m x n words (out_bytes >= 16 world m n). */
   void* out[INT4GEMV_MAX_PEERS];
-  /* flags[r]: rank r's flag buffer of INT4GEMV_PEER_FLAG_BYTES(world), zeroed once at
-   * allocation (int4gemv_peer_alloc does) and then owned by the kernel: it holds the number of
-   * the rank's last completed call, so calls need no host-side state and replay from a captured
-   * CUDA graph. Use one out / flag buffer set per sharded matrix. */
-  void* flags[INT4GEMV_MAX_PEERS];
+  /* this rank's call counters, INT4GEMV_PEER_COUNTER_BYTES, zeroed once at allocation
+   * (int4gemv_peer_alloc does) and then owned by the kernel: they hold the number of the last
+   * completed call, so calls need no host-side state and replay from a captured CUDA graph.
+   * Use one out buffer set and one counter buffer per sharded matrix. */
+  void* counters;
 } int4gemv_peers_t;
 
 /* sizeof(int4gemv_peers_t), for bindings that build the struct themselves. */
@@ -224,26 +223,27 @@ size_t int4gemv_peers_struct_bytes(void);
 
 /* The GEMV of this rank's shard with the exchange fused into its epilogue, on the fast path's
  * shapes (group_size 128, K % 1024 == 0, M <= 32), y [m, n_total] (ROWS) or [m, n] (K) fp16.
- * ROWS: the shard's rows are columns [col0, col0 + n) of y; each CTA writes its outputs into
- * every rank's exchange buffer over NVLink (peer stores), publishes a flag on every rank, waits
- * for its counterparts' flags and copies the rows they wrote into y, so when the kernel completes
- * y is whole. K: each CTA writes its fp32 partial sums into every rank's exchange buffer, waits
- * likewise, and writes y = the ranks' partials added in rank order (bit-identical on every rank).
+ * ROWS: the shard's rows are columns [col0, col0 + n) of y; each CTA writes its outputs, each
+ * tagged with the call number in the same 8-byte store, into every rank's exchange buffer over
+ * NVLink (peer stores), then copies the rows its counterpart CTAs wrote into y as their tags show
+ * this call, so when the kernel completes y is whole. K: each CTA writes its fp32 partial sums,
+ * tagged, into every rank's exchange buffer and writes y = the ranks' partials added in rank order
+ * (bit-identical on every rank).
  * Every rank must make the same sequence of calls with the same m, n, k (so each launches the
- * same CTAs). A wait on a peer is bounded (2 s); when it runs out the kernel records status 3
- * (int4gemv_device_status) and finishes with an undefined y. */
+ * same CTAs). A wait on a peer's word is bounded (2 s); when it runs out the kernel records
+ * status 3 (int4gemv_device_status) and finishes with an undefined y. */
 int int4gemv_w4a16_exchange(void* y, const void* x, const void* qweight, const void* scales,
                             const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
                             const int4gemv_peers_t* peers, void* stream);
 
 /* int4gemv_w4a16_exchange for a single rank (world 1, rank 0) with no allocation at all: its
- * exchange buffer and flag / call-counter words are a static device array in the library
- * (4 MiB + 8 KiB per device), so no int4gemv_peer_alloc and no caller buffers. mode
+ * exchange buffer and call-counter words are static device arrays in the library
+ * (4 MiB + 4 KiB per device), so no int4gemv_peer_alloc and no caller buffers. mode
  * INT4GEMV_SHARD_ROWS or INT4GEMV_SHARD_K; y [m, n] fp16 as int4gemv_w4a16 computes it, through
- * the exchange epilogue. Sizes needing more than the static buffer (ROWS: m x n > 1 Mi; K:
- * m x n > 512 Ki) are rejected with INT4GEMV_ERR_INVALID and a message giving the limit.
- * The first call on a device does the setup (looks up the array with cudaGetSymbolAddress and
- * clears the flag words, synchronously), so it must come before any stream capture. All calls on
+ * the exchange epilogue. Sizes needing more than the static buffer (m x n > 256 Ki in either
+ * mode) are rejected with INT4GEMV_ERR_INVALID and a message giving the limit.
+ * The first call on a device does the setup (looks up the arrays with cudaGetSymbolAddress and
+ * clears the exchange buffer and the counters, synchronously), so it must come before any stream capture. All calls on
  * a device share the one buffer: calls that overlap in time (different streams, or other host
  * threads) race. No counterpart in the reference. */
 int int4gemv_w4a16_exchange_static(void* y, const void* x, const void* qweight,

@@ -178,22 +178,21 @@ int run_picked(const char* name, const i4::GemvArgs& a, cudaStream_t st) {
 }  // namespace
 
 // ---- Scratch of int4gemv_w4a16_exchange_static: static device memory, no allocation ---------
-// A single rank's exchange buffer (two halves) and its flag and call-counter words
-// (INT4GEMV_PEER_FLAG_BYTES(1)), in module memory of every device the library is loaded on.
+// A single rank's exchange buffer (two halves of 8-byte tagged words) and its call counters
+// (INT4GEMV_PEER_COUNTER_BYTES), in module memory of every device the library is loaded on.
 constexpr int64_t kStaticExchangeBytes = 4 << 20;
-constexpr int kStaticFlagWords = 2 * INT4GEMV_PEER_FLAG_STRIDE;
 static __device__ __align__(256) unsigned char g_static_exchange[kStaticExchangeBytes];
-static __device__ __align__(256) unsigned g_static_flags[kStaticFlagWords];
+static __device__ __align__(256) unsigned char g_static_counters[INT4GEMV_PEER_COUNTER_BYTES];
 
 namespace {
 constexpr int kMaxDevices = 64;
 std::mutex g_static_mu;
 void* g_static_out[kMaxDevices];
-void* g_static_flag_ptr[kMaxDevices];
+void* g_static_counter_ptr[kMaxDevices];
 
 // The current device's static scratch. The first call on a device looks the symbols up and
-// clears the flag words (synchronously: it must not happen inside a stream capture).
-int static_scratch(const char* name, void** out, void** flags) {
+// clears both arrays (synchronously: it must not happen inside a stream capture).
+int static_scratch(const char* name, void** out, void** counters) {
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return cuda_fail(name, err);
@@ -205,15 +204,16 @@ int static_scratch(const char* name, void** out, void** flags) {
     void* o = nullptr;
     void* f = nullptr;
     err = cudaGetSymbolAddress(&o, g_static_exchange);
-    if (err == cudaSuccess) err = cudaGetSymbolAddress(&f, g_static_flags);
-    if (err == cudaSuccess) err = cudaMemset(f, 0, sizeof(unsigned) * kStaticFlagWords);
+    if (err == cudaSuccess) err = cudaGetSymbolAddress(&f, g_static_counters);
+    if (err == cudaSuccess) err = cudaMemset(o, 0, kStaticExchangeBytes);
+    if (err == cudaSuccess) err = cudaMemset(f, 0, INT4GEMV_PEER_COUNTER_BYTES);
     if (err == cudaSuccess) err = cudaDeviceSynchronize();
     if (err != cudaSuccess) return cuda_fail(name, err);
-    g_static_flag_ptr[dev] = f;
+    g_static_counter_ptr[dev] = f;
     g_static_out[dev] = o;
   }
   *out = g_static_out[dev];
-  *flags = g_static_flag_ptr[dev];
+  *counters = g_static_counter_ptr[dev];
   return INT4GEMV_OK;
 }
 }  // namespace
@@ -605,7 +605,7 @@ int int4gemv_repack_gptq(void* qweight, void* scales, void* zeros, const void* g
 
 static_assert(INT4GEMV_MAX_PEERS == i4::kMaxPeers, "peer count");
 static_assert(INT4GEMV_MAX_GROUP == i4::kMaxGroup, "group count");
-static_assert(INT4GEMV_PEER_FLAG_STRIDE == i4::kPeerFlagStride, "flag stride");
+static_assert(INT4GEMV_PEER_COUNTER_BYTES == 4 * i4::kPeerCounters, "counter words");
 
 size_t int4gemv_peers_struct_bytes(void) { return sizeof(int4gemv_peers_t); }
 
@@ -660,10 +660,9 @@ int int4gemv_w4a16_exchange(void* y, const void* x, const void* qweight, const v
                 peers->rank, peers->world, INT4GEMV_MAX_PEERS);
   }
   for (int r = 0; r < peers->world; ++r) {
-    if (!peers->out[r] || !peers->flags[r]) {
-      return fail(INT4GEMV_ERR_INVALID, "%s: null buffer of rank %d", name, r);
-    }
+    if (!peers->out[r]) return fail(INT4GEMV_ERR_INVALID, "%s: null buffer of rank %d", name, r);
   }
+  if (!peers->counters) return fail(INT4GEMV_ERR_INVALID, "%s: null counters", name);
   if (int e = check_sizes(name, m, n, k, group_size)) return e;
   if (m == 0 || n == 0 || k == 0) {
     return fail(INT4GEMV_ERR_INVALID, "%s: M, N and K must be positive", name);
@@ -679,7 +678,7 @@ int int4gemv_w4a16_exchange(void* y, const void* x, const void* qweight, const v
                 peers->world, static_cast<long long>(peers->col0), static_cast<long long>(n),
                 peers->rank);
   }
-  const int64_t need = mode == INT4GEMV_SHARD_ROWS ? m * n_out * 2 : peers->world * m * n * 4;
+  const int64_t need = 8 * (mode == INT4GEMV_SHARD_ROWS ? m * n_out : peers->world * m * n);
   if (peers->out_bytes < 2 * need) {
     return fail(INT4GEMV_ERR_INVALID, "%s: out buffers of %lld bytes, %lld needed (two halves)",
                 name, static_cast<long long>(peers->out_bytes), static_cast<long long>(2 * need));
@@ -690,10 +689,8 @@ int int4gemv_w4a16_exchange(void* y, const void* x, const void* qweight, const v
   const char* why = "unsupported shape";
   if (!i4::stream_mma_supported(a, &why)) return fail(INT4GEMV_ERR_INVALID, "%s: %s", name, why);
   i4::PeerSet ps{};
-  for (int r = 0; r < peers->world; ++r) {
-    ps.out[r] = peers->out[r];
-    ps.flags[r] = static_cast<unsigned*>(peers->flags[r]);
-  }
+  for (int r = 0; r < peers->world; ++r) ps.out[r] = peers->out[r];
+  ps.counters = static_cast<unsigned*>(peers->counters);
   ps.out_half = (peers->out_bytes / 2) / 16 * 16;
   ps.world = peers->world;
   ps.rank = peers->rank;
@@ -710,19 +707,18 @@ int int4gemv_w4a16_exchange_static(void* y, const void* x, const void* qweight,
     return fail(INT4GEMV_ERR_INVALID, "%s: unknown mode %d", name, mode);
   }
   if (m < 0 || n < 0) return fail(INT4GEMV_ERR_INVALID, "%s: negative size", name);
-  const int64_t half = m * n * (mode == INT4GEMV_SHARD_ROWS ? 2 : 4);
+  const int64_t half = 8 * m * n;  // one tagged word per output, either mode
   if (2 * half > kStaticExchangeBytes) {
     return fail(INT4GEMV_ERR_INVALID,
                 "%s: M = %lld, N = %lld needs %lld bytes of exchange buffer; the static buffer "
-                "holds %lld (M x N <= %lld in this mode)",
+                "holds %lld (M x N <= %lld)",
                 name, static_cast<long long>(m), static_cast<long long>(n),
                 static_cast<long long>(2 * half), static_cast<long long>(kStaticExchangeBytes),
-                static_cast<long long>(kStaticExchangeBytes / 2 /
-                                       (mode == INT4GEMV_SHARD_ROWS ? 2 : 4)));
+                static_cast<long long>(kStaticExchangeBytes / 16));
   }
   void* out = nullptr;
-  void* flags = nullptr;
-  if (int e = static_scratch(name, &out, &flags)) return e;
+  void* counters = nullptr;
+  if (int e = static_scratch(name, &out, &counters)) return e;
   int4gemv_peers_t peers{};
   peers.world = 1;
   peers.rank = 0;
@@ -731,7 +727,7 @@ int int4gemv_w4a16_exchange_static(void* y, const void* x, const void* qweight,
   peers.col0 = 0;
   peers.out_bytes = kStaticExchangeBytes;
   peers.out[0] = out;
-  peers.flags[0] = flags;
+  peers.counters = counters;
   return int4gemv_w4a16_exchange(y, x, qweight, scales, zeros, m, n, k, group_size, &peers,
                                  stream);
 }

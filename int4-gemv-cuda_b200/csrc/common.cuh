@@ -132,40 +132,40 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   return true;
 }
 
-// ---- flags between ranks (peer memory over NVLink) ----------------------------------------------
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// A release fence at system scope; followed by relaxed flag stores it forms one release pattern
-// for all of them (one fence, however many ranks are signalled).
-__device__ __forceinline__ void fence_release_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
-
-__device__ __forceinline__ void st_relaxed_sys(unsigned* p, unsigned v) {
-  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
+// ---- words between ranks (peer memory over NVLink) -----------------------------------------------
 __device__ __forceinline__ unsigned long long global_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
 
-// Waits until *flag has reached `epoch` (modulo 2^32), at most `limit_ns` nanoseconds.
-__device__ __forceinline__ bool wait_flag_bounded(const unsigned* flag, unsigned epoch,
-                                                  unsigned long long limit_ns) {
-  if (static_cast<int>(ld_acquire_sys(flag) - epoch) >= 0) return true;
-  const unsigned long long start = global_ns();
-  while (static_cast<int>(ld_acquire_sys(flag) - epoch) < 0) {
-    if (global_ns() - start > limit_ns) return false;
-    __nanosleep(100);
+// Tagged words between ranks: 32 bits of data and a 32-bit tag (the call number) in one naturally
+// aligned 64-bit store, which is single-copy atomic, so a reader that sees the tag sees the data
+// that came with it: no fence and no separate flag.
+__device__ __forceinline__ void st_tagged(unsigned long long* p, unsigned data, unsigned tag) {
+  const unsigned long long v = (static_cast<unsigned long long>(tag) << 32) | data;
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_tagged(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Waits until the word at p carries `tag`, at most `limit_ns` nanoseconds; its data in *data.
+__device__ __forceinline__ bool wait_tagged(const unsigned long long* p, unsigned tag,
+                                            unsigned* data, unsigned long long limit_ns) {
+  unsigned long long v = ld_tagged(p);
+  if (static_cast<unsigned>(v >> 32) != tag) {
+    const unsigned long long start = global_ns();
+    do {
+      if (global_ns() - start > limit_ns) return false;
+      __nanosleep(64);
+      v = ld_tagged(p);
+    } while (static_cast<unsigned>(v >> 32) != tag);
   }
+  *data = static_cast<unsigned>(v);
   return true;
 }
 

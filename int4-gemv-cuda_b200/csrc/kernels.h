@@ -19,23 +19,22 @@ namespace i4 {
 enum Epilogue : int { kStoreY = 0, kSiluMul = 1, kGatherPeers = 2, kReducePeers = 3, kGroupedY = 4 };
 
 constexpr int kMaxPeers = 8;
-constexpr int kPeerFlagStride = 1024;  // flag words per source rank (>= CTAs of any launch)
-constexpr unsigned long long kPeerWaitNs = 2000000000ull;  // limit of one wait on a peer's flag
+constexpr int kPeerCounters = 1024;  // counter words per rank (two used: call number, CTAs done)
+constexpr unsigned long long kPeerWaitNs = 2000000000ull;  // limit of one wait on a peer's word
 
-// Peer buffers of a sharded layer. out[r] and flags[r] are rank r's buffers, mapped into this
-// process (out[rank] and flags[rank] are this rank's own). Each out buffer has two halves of
-// out_half bytes, used by alternate calls (a rank can run at most one call ahead of another).
-// kGatherPeers: a half is y [m, n_total] fp16; this rank writes columns [col0, col0 + n) of
-// every rank's half, then each CTA copies the rows it waited for into this rank's y.
-// kReducePeers: a half is [world, m, n] fp32; this rank writes slot `rank` of every rank's half.
-// flags[r] holds world * kPeerFlagStride flag words, then kPeerFlagStride control words (rank r's
-// own): CTA c's number of its last completed call. A call's number is that + 1, read on the
-// device, so a captured graph replays correctly. CTA c sets word
-// rank * kPeerFlagStride + c of every rank to the call number after its stores and waits for word
-// r * kPeerFlagStride + c of its own flags, for every r.
+// Peer buffers of a sharded layer. out[r] is rank r's exchange buffer mapped into this process
+// (out[rank] is this rank's own): two halves of out_half bytes used by alternate calls (a rank
+// can run at most one call ahead of another), each an array of 64-bit tagged words (32 bits of
+// data, 32 bits of call number). kGatherPeers: a half is [m, n_total] words (fp16 bits of y);
+// this rank writes columns [col0, col0 + n) of every rank's half, then each CTA copies the rows
+// it needs into this rank's y as their tags show this call. kReducePeers: a half is
+// [world, m, n] words (fp32 partial sums); this rank writes slot `rank` of every rank's half.
+// counters: this rank's kPeerCounters words: [0] the number of the last completed call, [1] the
+// CTAs of the running call that have finished. A call's number is [0] + 1, read on the device,
+// so a captured graph replays correctly.
 struct PeerSet {
   void* out[kMaxPeers];
-  unsigned* flags[kMaxPeers];
+  unsigned* counters;
   long long out_half;
   int world, rank;
   int n_total, col0;

@@ -593,46 +593,45 @@ __device__ __forceinline__ void wide_stage(const unsigned char* st, const unsign
   }
 }
 
-// Call number of this exchange for this CTA: one more than the CTA's last completed call (its
-// control word in this rank's flags). Every call runs the same CTAs, so the per-CTA counters
-// advance together and need no cross-CTA coordination. Read after the dependency wait, so the
-// previous call's update is visible.
-__device__ __forceinline__ unsigned* exchange_counter(const PeerSet& peers) {
-  return peers.flags[peers.rank] + peers.world * kPeerFlagStride + blockIdx.x;
-}
-
+// Call number of this exchange: one more than the last completed call that used these buffers
+// (counters[0] of this rank). Read by every consumer thread at the same point, after the
+// dependency wait (so the previous call's update is visible), and followed by a barrier before
+// any thread of the CTA can reach exchange_done.
 __device__ __forceinline__ unsigned exchange_epoch(const PeerSet& peers) {
-  return __ldcg(exchange_counter(peers)) + 1u;
+  return __ldcg(peers.counters) + 1u;
 }
 
-// The consumers' half of a peer exchange, after each has issued its stores into the ranks'
-// buffers: the CTA synchronises (which orders every thread's stores before thread 0's next
-// operations), thread 0 publishes this CTA's flag on every rank with one system-scope release
-// fence and relaxed stores (the release is cumulative: it makes the whole CTA's stores visible
-// first; one fence per CTA, not one per thread or per rank), and threads 0 .. world - 1 each wait (acquire, bounded) for the flag of this CTA's
-// counterpart on one rank. Then the CTA synchronises again, so its threads may read what the
-// other ranks wrote. A wait that runs out records kStatusPeerTimeout and stops waiting.
-template <int kConsumerThreads>
-__device__ __forceinline__ void exchange_flags(const PeerSet& peers, unsigned epoch, int* status,
-                                               int tid) {
-  named_barrier(kConsumerBarrier, kConsumerThreads);
+// The last CTA of the call to finish (counters[1] counts them) records `epoch` as the last
+// completed call. One global number per call, whatever the shapes of earlier calls on the same
+// buffers, so a word left by an earlier call of the same parity always carries an older tag.
+__device__ __forceinline__ void exchange_done(const PeerSet& peers, unsigned epoch, int tid) {
   if (tid == 0) {
-    fence_release_sys();
-    for (int q = 0; q < peers.world; ++q) {
-      st_relaxed_sys(peers.flags[q] + peers.rank * kPeerFlagStride + blockIdx.x, epoch);
+    __threadfence();
+    if (atomicAdd(peers.counters + 1, 1u) == gridDim.x - 1) {
+      peers.counters[1] = 0;
+      peers.counters[0] = epoch;
+      __threadfence();
     }
   }
-  if (tid < peers.world) {
-    const unsigned* f = peers.flags[peers.rank] + tid * kPeerFlagStride + blockIdx.x;
-    if (!wait_flag_bounded(f, epoch, kPeerWaitNs)) atomicExch(status, kStatusPeerTimeout);
-  }
-  named_barrier(kConsumerBarrier, kConsumerThreads);
 }
 
-// Records `epoch` as this CTA's last completed call (read by the next call, after its
-// dependency wait on this kernel).
-__device__ __forceinline__ void exchange_done(const PeerSet& peers, unsigned epoch, int tid) {
-  if (tid == 0) *exchange_counter(peers) = epoch;
+// The exchange words of this call: rank q's buffer, this call's half, as tagged 64-bit words.
+__device__ __forceinline__ unsigned long long* exchange_words(const PeerSet& peers, int q,
+                                                              unsigned epoch) {
+  return reinterpret_cast<unsigned long long*>(static_cast<char*>(peers.out[q]) +
+                                               (epoch & 1u) * peers.out_half);
+}
+
+// Reads the data of a tagged word of this call; after a wait has run out (*live false) it stops
+// waiting and the kernel's result is undefined (status kStatusPeerTimeout).
+__device__ __forceinline__ unsigned exchange_read(const unsigned long long* w, unsigned epoch,
+                                                  bool* live, int* status) {
+  unsigned data = static_cast<unsigned>(ld_tagged(w));
+  if (*live && !wait_tagged(w, epoch, &data, kPeerWaitNs)) {
+    *live = false;
+    atomicExch(status, kStatusPeerTimeout);
+  }
+  return data;
 }
 
 // MP: M rounded up to 2 or 4 (narrow path) or 8 (wide path, MT tiles of 8 rows of x). MC: M when
@@ -843,61 +842,54 @@ __global__ void __maxnreg__(CW == 16 ? 96 : 168)
       if (in.ok) go.y[gi][static_cast<int64_t>(m) * ng + row - base] = __float2half_rn(sum);
     }
   } else if (a.epilogue == kGatherPeers) {
-    // This rank's columns of y into the current half of every rank's gather buffer; once this
-    // CTA's counterparts on every rank have done the same, the rows they wrote (the same row
-    // range of every rank's shard) are copied into this rank's y.
+    // This rank's columns of y, each as a tagged word (fp16 bits, call number), into every rank's
+    // gather buffer. The rows this CTA then copies into y are the same row range of every rank's
+    // shard: the words its counterpart CTAs write; each is read once its tag shows this call.
     const unsigned epoch = exchange_epoch(peers);
-    const long long off = (epoch & 1u) * peers.out_half;  // this call's half
+    named_barrier(kConsumerBarrier, kConsumerThreads);  // every thread has read the call number
     for (int o = tid; o < rows * a.m; o += kConsumerThreads) {
       const int m = o / rows;
       const int r = o - m * rows;
-      const half h = __float2half_rn(row_sum(r, m));
+      const unsigned h = __half_as_ushort(__float2half_rn(row_sum(r, m)));
       const int64_t at = static_cast<int64_t>(m) * peers.n_total + peers.col0 + row_begin + r;
-      if (in.ok) {
-        for (int q = 0; q < peers.world; ++q) {
-          reinterpret_cast<half*>(static_cast<char*>(peers.out[q]) + off)[at] = h;
-        }
-      }
+      for (int q = 0; q < peers.world; ++q) st_tagged(exchange_words(peers, q, epoch) + at, h, epoch);
     }
-    exchange_flags<kConsumerThreads>(peers, epoch, p.status, tid);
-    const half* buf =
-        reinterpret_cast<const half*>(static_cast<const char*>(peers.out[peers.rank]) + off);
+    const unsigned long long* buf = exchange_words(peers, peers.rank, epoch);
+    bool live = true;
     for (int o = tid; o < peers.world * rows * a.m; o += kConsumerThreads) {
       const int q = o / (rows * a.m);
       const int rem = o - q * rows * a.m;
       const int m = rem / rows;
       const int r = rem - m * rows;
       const int64_t at = static_cast<int64_t>(m) * peers.n_total + q * a.n + row_begin + r;
-      if (in.ok) a.y[at] = __ldcg(buf + at);
+      const unsigned h = exchange_read(buf + at, epoch, &live, p.status);
+      if (in.ok) a.y[at] = __ushort_as_half(static_cast<unsigned short>(h));
     }
     exchange_done(peers, epoch, tid);
   } else if (a.epilogue == kReducePeers) {
-    // This rank's fp32 partial sums into slot `rank` of the current half of every rank's receive
-    // buffer; then, once every rank's partials for these rows are in, their sum in rank order
-    // (the same on every rank, so all ranks hold bit-identical y).
+    // This rank's fp32 partial sums, as tagged words, into slot `rank` of every rank's receive
+    // buffer; then the sum of the ranks' partials for this CTA's rows in rank order (the same on
+    // every rank, so all ranks hold bit-identical y), each read once its tag shows this call.
     const unsigned epoch = exchange_epoch(peers);
-    const long long off = (epoch & 1u) * peers.out_half;  // this call's half
+    named_barrier(kConsumerBarrier, kConsumerThreads);  // every thread has read the call number
     const int64_t slot = static_cast<int64_t>(a.m) * a.n;
     for (int o = tid; o < rows * a.m; o += kConsumerThreads) {
       const int m = o / rows;
       const int r = o - m * rows;
-      const float sum = row_sum(r, m);
+      const unsigned bits = __float_as_uint(row_sum(r, m));
       const int64_t at = peers.rank * slot + static_cast<int64_t>(m) * a.n + row_begin + r;
-      if (in.ok) {
-        for (int q = 0; q < peers.world; ++q) {
-          reinterpret_cast<float*>(static_cast<char*>(peers.out[q]) + off)[at] = sum;
-        }
-      }
+      for (int q = 0; q < peers.world; ++q) st_tagged(exchange_words(peers, q, epoch) + at, bits, epoch);
     }
-    exchange_flags<kConsumerThreads>(peers, epoch, p.status, tid);
-    const float* mine =
-        reinterpret_cast<const float*>(static_cast<const char*>(peers.out[peers.rank]) + off);
+    const unsigned long long* mine = exchange_words(peers, peers.rank, epoch);
+    bool live = true;
     for (int o = tid; o < rows * a.m; o += kConsumerThreads) {
       const int m = o / rows;
       const int r = o - m * rows;
       const int64_t at = static_cast<int64_t>(m) * a.n + row_begin + r;
       float total = 0.0f;
-      for (int q = 0; q < peers.world; ++q) total += __ldcg(mine + q * slot + at);
+      for (int q = 0; q < peers.world; ++q) {
+        total += __uint_as_float(exchange_read(mine + q * slot + at, epoch, &live, p.status));
+      }
       if (in.ok) a.y[at] = store_value(a, m, row_begin + r, total);
     }
     exchange_done(peers, epoch, tid);
@@ -1001,9 +993,7 @@ cudaError_t launch_stream_mma(const GemvArgs& a, cudaStream_t stream, bool stric
   MmaPlan p;
   if (!make_plan(a, &p, nullptr)) return cudaErrorInvalidValue;
   const bool exchange = a.epilogue == kGatherPeers || a.epilogue == kReducePeers;
-  if (exchange != (peers != nullptr) || (exchange && p.ctas > kPeerFlagStride)) {
-    return cudaErrorInvalidValue;
-  }
+  if (exchange != (peers != nullptr)) return cudaErrorInvalidValue;
   if ((a.epilogue == kGroupedY) != (groups != nullptr)) return cudaErrorInvalidValue;
   EpilogueExtra ex{};
   if (peers) ex.peers = *peers;

@@ -55,7 +55,7 @@ _PROTOTYPES = {
 
 MAX_PEERS = 8
 SHARD_ROWS, SHARD_K = 0, 1
-PEER_FLAG_STRIDE = 1024
+PEER_COUNTER_BYTES = 4096
 IPC_HANDLE_BYTES = 64
 
 
@@ -65,12 +65,7 @@ class Peers(ctypes.Structure):
     _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("mode", ctypes.c_int32),
                 ("reserved", ctypes.c_int32), ("n_total", ctypes.c_int64),
                 ("col0", ctypes.c_int64), ("out_bytes", ctypes.c_int64),
-                ("out", _p * MAX_PEERS), ("flags", _p * MAX_PEERS)]
-
-
-def peer_flag_bytes(world: int) -> int:
-    """INT4GEMV_PEER_FLAG_BYTES(world)."""
-    return (world + 1) * PEER_FLAG_STRIDE * 4
+                ("out", _p * MAX_PEERS), ("counters", _p)]
 
 
 class CapiError(RuntimeError):

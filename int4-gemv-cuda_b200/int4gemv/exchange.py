@@ -3,14 +3,14 @@
 Same two layouts as int4gemv.sharded (rows split with an all-gather of y; K split with a sum of
 the partial y), but instead of a NCCL collective after the GEMV, the GEMV's own epilogue writes
 its outputs straight into the other ranks' buffers over NVLink (peer stores into CUDA-IPC-mapped
-memory) and each CTA then waits, bounded, for the flags of its counterparts on the other ranks
-(int4gemv_w4a16_exchange in the C ABI). One kernel per call, no collective launch, and the exchange
+memory), each output tagged with the call number in the same 8-byte store, and each CTA reads the
+words its counterparts on the other ranks wrote as their tags arrive (bounded waits; no fence and
+no separate flag; int4gemv_w4a16_exchange in the C ABI). One kernel per call, no collective launch, and the exchange
 of a CTA's rows overlaps the other CTAs' weight streaming.
 
 Buffers: each rank allocates one exchange buffer with two halves, used by alternate calls (a rank
-can run at most one call ahead of the slowest one), and a flag buffer whose words carry call
-numbers; the call counter itself lives in device memory, so a call needs no host-side state and
-can be captured in a CUDA graph and replayed. The handles travel over the process group once, at
+can run at most one call ahead of the slowest one), and a call counter in device memory, so a call
+needs no host-side state and can be captured in a CUDA graph and replayed. The handles travel over the process group once, at
 construction. Each call returns a new y tensor.
 
 Constraints: the fast path's shapes (group 128, the rank's K a multiple of 1024, M <= 32); rows
@@ -93,7 +93,7 @@ class FusedShardedW4A16:
             n0, n1 = split_range(self.n, self.world, self.rank)
             self.q, self.s, self.z = (t[n0:n1].contiguous() for t in (qweight, scales, zeros))
             self.span = (n0, n1)
-            half_bytes = max_m * self.n * 2
+            half_bytes = max_m * self.n * 8  # one 8-byte tagged word per output
         else:
             if self.k % _STAGE_K or self.k < _STAGE_K * self.world:
                 raise ValueError(f"K = {self.k} must be a multiple of {_STAGE_K} and at least "
@@ -104,16 +104,20 @@ class FusedShardedW4A16:
             self.s = scales[:, k0 // g:k1 // g].contiguous()
             self.z = zeros[:, k0 // g:k1 // g].contiguous()
             self.span = (k0, k1)
-            half_bytes = self.world * max_m * self.n * 4
+            half_bytes = self.world * max_m * self.n * 8
         self.out_bytes = 2 * half_bytes
         self.out = PeerBuffer(self.out_bytes, process_group)
-        self.flags = PeerBuffer(capi.peer_flag_bytes(self.world), process_group)
+        self.counters = ctypes.c_void_p()
+        handle = (ctypes.c_char * capi.IPC_HANDLE_BYTES)()
+        capi.check(capi.lib().int4gemv_peer_alloc(capi.PEER_COUNTER_BYTES,
+                                                  ctypes.byref(self.counters),
+                                                  ctypes.addressof(handle)))
         self.peers = capi.Peers()
         self.peers.world, self.peers.rank = self.world, self.rank
         self.peers.out_bytes = self.out_bytes
         for r in range(self.world):
             self.peers.out[r] = self.out.ptrs[r]
-            self.peers.flags[r] = self.flags.ptrs[r]
+        self.peers.counters = self.counters.value
         if mode == "n":
             self.peers.mode, self.peers.n_total = capi.SHARD_ROWS, self.n
             self.peers.col0 = self.span[0]
@@ -124,7 +128,7 @@ class FusedShardedW4A16:
         torch.cuda.synchronize()
         dist.barrier(group=self.pg)  # no rank still writes into another's buffers
         self.out.close()
-        self.flags.close()
+        capi.check(capi.lib().int4gemv_peer_free(self.counters.value))
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         if x.dim() != 2 or x.shape[1] != self.k or x.dtype != torch.float16 or not x.is_cuda:

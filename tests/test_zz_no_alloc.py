@@ -26,11 +26,11 @@ def test_static_matches_existing_entry_two_calls(mode):
     m, n, k = 2, 4096, 4096
     _, q, s, z = oracle.synthetic(1, n, k, 128, seed=21)
     tq, ts, tz = (torch.from_numpy(a).cuda() for a in (q, s, z))
-    out_bytes = 2 * m * n * (2 if mode == capi.SHARD_ROWS else 4)
-    out, flags = _alloc(out_bytes), _alloc(capi.peer_flag_bytes(1))
+    out_bytes = 2 * m * n * 8  # two halves of one 8-byte tagged word per output
+    out, counters = _alloc(out_bytes), _alloc(capi.PEER_COUNTER_BYTES)
     peers = capi.Peers()
     peers.world, peers.rank, peers.mode, peers.n_total, peers.col0 = 1, 0, mode, n, 0
-    peers.out_bytes, peers.out[0], peers.flags[0] = out_bytes, out, flags
+    peers.out_bytes, peers.out[0], peers.counters = out_bytes, out, counters
     stream = torch.cuda.current_stream().cuda_stream
     try:
         for call in range(2):
@@ -50,11 +50,11 @@ def test_static_matches_existing_entry_two_calls(mode):
         assert capi.device_status() == 0
     finally:
         capi.check(capi.lib().int4gemv_peer_free(out))
-        capi.check(capi.lib().int4gemv_peer_free(flags))
+        capi.check(capi.lib().int4gemv_peer_free(counters))
 
 
 def test_static_rejects_oversize():
     x = torch.zeros(32, 1024, dtype=torch.float16, device="cuda")
     with pytest.raises(capi.CapiError, match="static buffer holds"):
         capi.call("int4gemv_w4a16_exchange_static", x.data_ptr(), x.data_ptr(), x.data_ptr(),
-                  x.data_ptr(), x.data_ptr(), 32, 65536, 1024, 128, capi.SHARD_K, None)
+                  x.data_ptr(), x.data_ptr(), 32, 16384, 1024, 128, capi.SHARD_K, None)
