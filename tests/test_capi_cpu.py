@@ -116,3 +116,80 @@ def test_exchange_rejects_bad_peers():
     with pytest.raises(capi.CapiError, match="null buffer"):
         capi.call("int4gemv_w4a16_exchange", None, 16, 16, 16, 16, 1, 64, 1024, 128,
                   ctypes.addressof(peers), None)
+
+
+FAKE = 4096  # a 16-byte-aligned address that is never dereferenced: the checks below fail first
+
+
+@pytest.mark.parametrize("count,ns,message", [
+    (0, [1], "w4a16_grouped: count 0 must be in [1, 8] with ys and ns given"),
+    (9, [1] * 9, "w4a16_grouped: count 9 must be in [1, 8] with ys and ns given"),
+    (2, [4, -1], "w4a16_grouped: ns[1] = -1 < 0"),
+])
+def test_grouped_argument_errors(count, ns, message):
+    ys = (ctypes.c_void_p * max(count, 1))(*([FAKE] * max(count, 1)))
+    sizes = (ctypes.c_int64 * max(count, 1))(*(ns or [0]))
+    res = capi.lib().int4gemv_w4a16_grouped(count, ys, sizes, FAKE, FAKE, FAKE, FAKE, 1, 1024,
+                                            128, None)
+    assert res == capi.ERR_INVALID
+    assert capi.last_error() == message
+
+
+def test_grouped_and_bias_empty_calls_launch_nothing():
+    ys = (ctypes.c_void_p * 2)(FAKE, FAKE)
+    sizes = (ctypes.c_int64 * 2)(0, 0)
+    assert capi.lib().int4gemv_w4a16_grouped(2, ys, sizes, FAKE, FAKE, FAKE, FAKE, 1, 1024, 128,
+                                             None) == capi.OK
+    assert capi.lib().int4gemv_w4a16_bias_residual(FAKE, FAKE, FAKE, FAKE, FAKE, None, None, 0, 64,
+                                                   1024, 128, None) == capi.OK
+    res = capi.lib().int4gemv_w4a16_bias_residual(FAKE, FAKE, FAKE, FAKE, FAKE, None, None, 1, 64,
+                                                  1000, 128, None)
+    assert res == capi.ERR_INVALID and "group_size 128" in capi.last_error()
+
+
+def test_quantize_pack_repack_argument_errors():
+    lib = capi.lib()
+    cases = [
+        (lambda: lib.int4gemv_quantize(FAKE, FAKE, FAKE, FAKE, 7, 4, 256, 128, None),
+         "quantize: unknown weight dtype 7"),
+        (lambda: lib.int4gemv_quantize(FAKE, FAKE, FAKE, FAKE, 0, 4, 256, 100, None),
+         "quantize: group_size 100 must be a positive multiple of 8 dividing K = 256"),
+        (lambda: lib.int4gemv_quantize(FAKE, FAKE, FAKE, FAKE + 4, 0, 4, 256, 128, None),
+         "quantize: w must be 16-byte aligned"),
+        (lambda: lib.int4gemv_pack(FAKE, FAKE, 4, 12, None),
+         "pack: N = 4, K = 12: K must be a non-negative multiple of 8"),
+        (lambda: lib.int4gemv_pack(FAKE, FAKE + 8, 4, 16, None), "pack: q must be 16-byte aligned"),
+        (lambda: lib.int4gemv_repack_awq(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 60, 256, 128, None),
+         "repack_awq: N = 60 must be a multiple of 8 (packed zero points)"),
+        (lambda: lib.int4gemv_repack_gptq(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 2, 64, 256, 128,
+                                          None),
+         "repack_gptq: zero_offset 2 must be 0 or 1"),
+    ]
+    for call, message in cases:
+        assert call() == capi.ERR_INVALID
+        assert capi.last_error() == message
+    assert lib.int4gemv_quantize(FAKE, FAKE, FAKE, FAKE, 1, 0, 256, 128, None) == capi.OK
+
+
+def test_exchange_size_checks():
+    peers = capi.Peers()
+    peers.world, peers.rank, peers.mode = 2, 1, capi.SHARD_ROWS
+    peers.out[0], peers.out[1], peers.counters = FAKE, FAKE, FAKE
+    peers.n_total, peers.col0, peers.out_bytes = 100, 64, 1 << 20
+    res = capi.lib().int4gemv_w4a16_exchange(FAKE, FAKE, FAKE, FAKE, FAKE, 1, 64, 1024, 128,
+                                             ctypes.addressof(peers), None)
+    assert res == capi.ERR_INVALID and "equal shards" in capi.last_error()
+    peers.n_total = 128
+    peers.out_bytes = 1024  # two halves of 1 x 128 tagged 8-byte words need 2048
+    res = capi.lib().int4gemv_w4a16_exchange(FAKE, FAKE, FAKE, FAKE, FAKE, 1, 64, 1024, 128,
+                                             ctypes.addressof(peers), None)
+    assert res == capi.ERR_INVALID
+    assert capi.last_error() == ("w4a16_exchange: out buffers of 1024 bytes, 2048 needed "
+                                 "(two halves)")
+    res = capi.lib().int4gemv_w4a16_exchange_static(FAKE, FAKE, FAKE, FAKE, FAKE, 32, 16384, 1024,
+                                                    128, capi.SHARD_K, None)
+    assert res == capi.ERR_INVALID and "the static buffer holds 4194304" in capi.last_error()
+    res = capi.lib().int4gemv_w4a16_exchange_static(FAKE, FAKE, FAKE, FAKE, FAKE, 1, 64, 1024,
+                                                    128, 5, None)
+    assert res == capi.ERR_INVALID
+    assert capi.last_error() == "w4a16_exchange_static: unknown mode 5"
