@@ -661,6 +661,14 @@ def run_profile_case(args):
     global M, N, K
     M, N, K = args.m, args.n, args.k
     torch.cuda.set_device(0)
+    if args.profile == "quantize":  # device quantize of an fp16 [N, K] matrix
+        gen = torch.Generator(device="cuda").manual_seed(7)
+        w = torch.randn(N, K, generator=gen, device="cuda", dtype=torch.float16) * 0.02
+        for _ in range(args.calls):
+            ops.quantize(w, GROUP)
+        torch.cuda.synchronize()
+        print(f"profile case quantize N={N} K={K}: {args.calls} calls")
+        return
     set_bytes = N * K // 2 + 2 * N * (K // GROUP) * 2
     n_sets = max(2, math.ceil(L2_BYTES / set_bytes) + 1)
     sets, x = make_sets(n_sets, seed=7)
@@ -684,7 +692,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--profile", default=None,
                     help="run --calls launches of one kernel (w4a16, vectorized, naive, coalesced, "
-                         "load_only, cublas, reference_vectorized) for ncu, then exit")
+                         "load_only, quantize, cublas, reference_vectorized) for ncu, then exit")
     ap.add_argument("--m", type=int, default=M)
     ap.add_argument("--n", type=int, default=N)
     ap.add_argument("--k", type=int, default=K)
