@@ -1,8 +1,8 @@
 """ctypes front end of the C ABI in include/int4gemv_b200.h (libint4gemv_b200.so).
 
-This is the binding a non-torch caller writes; the tests and the end-to-end
-leg of bench.py use it to call the library exactly as such a caller would: plain pointers, sizes
-and a stream handle. Errors raise CapiError with the library's message.
+This is the binding a non-torch caller writes; the tests and the end-to-end leg of bench.py use it
+to call the library exactly as such a caller would: plain pointers, sizes and a stream handle.
+Errors raise CapiError with the library's message.
 """
 
 from __future__ import annotations

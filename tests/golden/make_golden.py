@@ -1,6 +1,7 @@
 """Generate the golden vectors in tests/golden/*.npz from the REFERENCE itself.
 
-Run in the build container, where the reference checkout exists (default /root/reference):
+Run where a checkout of the reference exists (--reference names it; the default is the build
+container's checkout):
 
     python tests/golden/make_golden.py [--reference PATH]
 
