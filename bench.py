@@ -661,6 +661,48 @@ def run_ours(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+SWEEP = ([(m, 8192, 8192) for m in (1, 2, 4, 8, 16, 32)]
+         + [(1, 4096, 4096), (1, 14336, 4096), (1, 4096, 14336), (1, 28672, 8192),
+            (1, 8192, 28672), (8, 28672, 8192), (8, 8192, 28672)])
+
+
+def run_sweep(args):
+    """--sweep: the BASELINE shapes (M sweep at 8192 x 8192, the MLP shapes, the unsharded
+    multi-GPU shapes), one JSON line each: ops.w4a16 and cuBLAS FP16 back to back from CUDA graphs
+    over weight rotations larger than 2x L2, plus one isolated call after an L2 flush."""
+    from int4gemv import ops
+    import torch.nn.functional as F
+
+    torch.cuda.set_device(0)
+    peak, _ = measured_peak()
+    for m, n, k in SWEEP:
+        gen = torch.Generator(device="cuda").manual_seed(m * 7 + n + k)
+        set_bytes = n * k // 2 + 2 * n * (k // GROUP) * 2
+        n_sets = max(2, math.ceil(2 * L2_BYTES / set_bytes) + 1)
+        sets = [ops.quantize(torch.randn(n, k, generator=gen, device="cuda",
+                                         dtype=torch.float16) * 0.02, GROUP)
+                for _ in range(n_sets)]
+        x = torch.randn(m, k, generator=gen, device="cuda", dtype=torch.float16)
+        calls = [(lambda st=st: ops.w4a16(x, *st, GROUP)) for st in sets]
+        ours = time_graph_calls(calls * max(1, 32 // n_sets), 2000, 100)
+        rot = iter(range(10**9))
+        iso = time_isolated(lambda: calls[next(rot) % n_sets]())
+        kernel = ops.w4a16_kernel(x, *sets[0], GROUP)
+        del sets, calls
+        w16 = [torch.randn(n, k, generator=gen, device="cuda", dtype=torch.float16) * 0.02
+               for _ in range(max(2, math.ceil(2 * L2_BYTES / (n * k * 2)) + 1))]
+        cub = [(lambda w=w: F.linear(x, w)) for w in w16]
+        cublas = time_graph_calls(cub * max(1, 16 // len(cub)), 1000, 50)
+        del w16, cub
+        b = int4_bytes(m, n, k, GROUP)
+        print(json.dumps({"m": m, "n": n, "k": k, "kernel": kernel,
+                          "us": round(ours * 1e6, 2), "gb_s": round(b / ours / 1e9, 1),
+                          "frac_of_hbm": round(b / ours / 1e9 / peak, 3),
+                          "isolated_us": round(iso * 1e6, 2),
+                          "cublas_fp16_us": round(cublas * 1e6, 2),
+                          "speedup_vs_cublas": round(cublas / ours, 2)}), flush=True)
+
+
 def run_profile_case(args):
     """A few launches of one kernel for ncu (no timing, no JSON): --profile KERNEL."""
     from int4gemv import ops
@@ -711,12 +753,17 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", action="store_true",
+                    help="time the BASELINE shapes (one JSON line each) instead of the headline")
     ap.add_argument("--no-sharded", action="store_true",
                     help="with more than one GPU, skip the sharded-layer timing")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.profile:
         run_profile_case(args)
+        return
+    if args.sweep:
+        run_sweep(args)
         return
     world, rank, local = (int(os.environ.get("WORLD_SIZE", "1")),
                           int(os.environ.get("RANK", "0")),
