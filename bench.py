@@ -676,6 +676,8 @@ def run_sweep(args):
     torch.cuda.set_device(0)
     peak, _ = measured_peak()
     for m, n, k in SWEEP:
+        if m < args.sweep_min_m:
+            continue
         gen = torch.Generator(device="cuda").manual_seed(m * 7 + n + k)
         set_bytes = n * k // 2 + 2 * n * (k // GROUP) * 2
         n_sets = max(2, math.ceil(2 * L2_BYTES / set_bytes) + 1)
@@ -755,6 +757,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true",
                     help="time the BASELINE shapes (one JSON line each) instead of the headline")
+    ap.add_argument("--sweep-min-m", type=int, default=1, help="--sweep: only shapes with M >= this")
     ap.add_argument("--no-sharded", action="store_true",
                     help="with more than one GPU, skip the sharded-layer timing")
     args = ap.parse_args()

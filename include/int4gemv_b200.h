@@ -81,13 +81,16 @@ int int4gemv_sequential(void* y, const void* x, const void* qweight, const void*
 
 /* ---- The B200 fast path (new; no counterpart in the reference) ------------------------------- */
 
-/* Bytes of device workspace int4gemv_w4a16 needs for this shape (0 if none). */
+/* Bytes of device workspace int4gemv_w4a16 can use for this shape (0 if none): for M >= 5 on the
+ * fast path's shapes, room for x permuted once per call by a pre-kernel instead of in every CTA. */
 int64_t int4gemv_w4a16_workspace_size(int64_t m, int64_t n, int64_t k, int64_t group_size);
 
 /* y = x @ dequant(W)^T through the fastest kernel for the shape: a persistent, TMA-bulk-fed,
  * tensor-core dequant GEMV when the shape allows it, else the SIMT kernels. Same inputs and result
  * contract as the operators above (csrc/w4a16.h:10-16), parity with int4gemv/reference.py within
- * rtol = 1e-2, atol = 1e-2. workspace may be NULL when int4gemv_w4a16_workspace_size returns 0. */
+ * rtol = 1e-2, atol = 1e-2. workspace is optional: NULL (or smaller than
+ * int4gemv_w4a16_workspace_size) gives the same result through the slower path. It is used only
+ * within the call, in stream order. */
 int int4gemv_w4a16(void* y, const void* x, const void* qweight, const void* scales,
                    const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
                    void* workspace, int64_t workspace_bytes, void* stream);

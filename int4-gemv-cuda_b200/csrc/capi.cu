@@ -345,14 +345,19 @@ int int4gemv_sequential(void* y, const void* x, const void* qweight, const void*
 }
 
 int64_t int4gemv_w4a16_workspace_size(int64_t m, int64_t n, int64_t k, int64_t group_size) {
-  (void)m, (void)n, (void)k, (void)group_size;
-  return 0;
+  if (m <= 0 || n <= 0 || k <= 0 || m > INT_MAX || n > INT_MAX || k > INT_MAX ||
+      group_size <= 0 || group_size % 8 || k % group_size) {
+    return 0;
+  }
+  // The size depends on the shape only; aligned stand-in pointers pass the alignment checks.
+  const void* aligned = reinterpret_cast<const void*>(static_cast<uintptr_t>(256));
+  const i4::GemvArgs a = make_args(nullptr, aligned, aligned, aligned, aligned, m, n, k, group_size);
+  return i4::stream_mma_workspace_bytes(a);
 }
 
 int int4gemv_w4a16(void* y, const void* x, const void* qweight, const void* scales,
                    const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
                    void* workspace, int64_t workspace_bytes, void* stream) {
-  (void)workspace, (void)workspace_bytes;
   const char* name = "w4a16";
   if (int e = check_sizes(name, m, n, k, group_size)) return e;
   if (int e = check_pointers(name, m, n, k, y, x, qweight, scales, zeros)) return e;
@@ -360,7 +365,12 @@ int int4gemv_w4a16(void* y, const void* x, const void* qweight, const void* scal
   const auto st = static_cast<cudaStream_t>(stream);
   int e = empty_cases(name, y, m, n, k, st, &done);
   if (done) return e;
-  return run_picked(name, make_args(y, x, qweight, scales, zeros, m, n, k, group_size), st);
+  const i4::GemvArgs a = make_args(y, x, qweight, scales, zeros, m, n, k, group_size);
+  if (workspace && workspace_bytes > 0 && pick_kernel(a) == Pick::kStreamMma) {
+    return launched(name, i4::launch_stream_mma(a, st, false, nullptr, nullptr, workspace,
+                                                workspace_bytes));
+  }
+  return run_picked(name, a, st);
 }
 
 int int4gemv_w4a16_grouped(int count, void* const* ys, const int64_t* ns, const void* x,

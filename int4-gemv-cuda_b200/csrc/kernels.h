@@ -109,8 +109,13 @@ cudaError_t tc_gemv_attrs(int m, KernelAttrs* out);
 // TMA-tile-fed mma.sync GEMV for M <= 32, group 128 (stream_mma.cu): the fast path. Launched
 // with programmatic stream serialization like launch_tc_gemv.
 bool stream_mma_supported(const GemvArgs& a, const char** why);
+// With a workspace of at least stream_mma_workspace_bytes(a) bytes (> 0 for the wide path, M >= 5,
+// plain stores), a small pre-kernel permutes x once and the GEMV's CTAs copy it instead of each
+// permuting all of x; without one, each CTA permutes x itself.
 cudaError_t launch_stream_mma(const GemvArgs& a, cudaStream_t stream, bool strict,
-                              const PeerSet* peers = nullptr, const GroupOut* groups = nullptr);
+                              const PeerSet* peers = nullptr, const GroupOut* groups = nullptr,
+                              void* workspace = nullptr, int64_t workspace_bytes = 0);
+int64_t stream_mma_workspace_bytes(const GemvArgs& a);
 cudaError_t stream_mma_attrs(int m, KernelAttrs* out);
 
 // TMA-bulk-fed mma.sync pipeline (mma_pipeline.cu). `why` gets a reason when unsupported.

@@ -76,6 +76,10 @@ struct MmaPlan {
   int off_xr, off_xs, off_corr, off_red, off_stage, smem_bytes;
   int strict;       // 1: read the weights only after griddepcontrol.wait
   int* status;
+  // Wide path with a workspace: x permuted once per call by stream_mma_xprep_kernel; panel pi is
+  // xslot bytes at xpre + pi * xslot (the xs rows, then the corr table), copied into xr.
+  const unsigned char* xpre;
+  int xslot;
 };
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
@@ -133,8 +137,8 @@ __device__ __forceinline__ uint4 permute_block(const uint4& v, float& bsum, floa
 // xs[m][item][j][c][8 halves] for word 4 c + j, item stride 256.
 template <bool NARROW, int kConsumerThreads>
 __device__ __forceinline__ void permute_x_panel(const GemvArgs& a, const MmaPlan& p, int pk,
-                                                const unsigned char* xr, unsigned char* xs,
-                                                float2* corr, int tid) {
+                                                const unsigned char* xr, int xr_stride,
+                                                unsigned char* xs, float2* corr, int tid) {
   const int pairs = pk / 16;        // word pairs per row of x in this panel
   const int count = a.m * pairs;    // a multiple of 8: eight lanes share one (m, item)
   for (int base = 0; base < count; base += kConsumerThreads) {
@@ -145,7 +149,8 @@ __device__ __forceinline__ void permute_x_panel(const GemvArgs& a, const MmaPlan
     if (active) {
       m = idx / pairs;
       v = idx - m * pairs;
-      const uint4* src = reinterpret_cast<const uint4*>(xr + (static_cast<int64_t>(m) * pk + 16 * v) * 2);
+      const uint4* src =
+          reinterpret_cast<const uint4*>(xr + (static_cast<int64_t>(m) * xr_stride + 16 * v) * 2);
       const uint4 o0 = permute_block(src[0], bsum, xsum);
       const uint4 o1 = permute_block(src[1], bsum, xsum);
       const int item = v >> 3, t = v & 7;
@@ -167,6 +172,39 @@ __device__ __forceinline__ void permute_x_panel(const GemvArgs& a, const MmaPlan
     }
     if (active && (v & 7) == 0) corr[(v >> 3) * p.mc + m] = make_float2(1024.0f * bsum, xsum);
   }
+}
+
+// The same panel from a workspace slot already permuted by stream_mma_xprep_kernel (landed in the
+// raw x buffer): the xs rows and the corr table, copied 16 bytes at a time.
+template <int kThreads>
+__device__ __forceinline__ void copy_x_slot(const unsigned char* slot, int x_bytes, int corr_bytes,
+                                            unsigned char* xs, float2* corr, int tid) {
+  const uint4* sx = reinterpret_cast<const uint4*>(slot);
+  uint4* dx = reinterpret_cast<uint4*>(xs);
+  for (int i = tid; i < x_bytes / 16; i += kThreads) dx[i] = sx[i];
+  const uint4* sc = reinterpret_cast<const uint4*>(slot + x_bytes);
+  uint4* dc = reinterpret_cast<uint4*>(corr);
+  for (int i = tid; i < corr_bytes / 16; i += kThreads) dc[i] = sc[i];
+}
+
+// Permutes x once per call for the wide path: block pi writes into workspace slot pi exactly what
+// permute_x_panel writes into a CTA's shared memory for k-panel pi (the xs rows, then the corr
+// table), so the GEMV's CTAs copy it instead of each permuting all of x.
+constexpr int kXprepThreads = 256;
+
+__global__ void __launch_bounds__(kXprepThreads)
+    stream_mma_xprep_kernel(GemvArgs a, MmaPlan p, unsigned char* ws) {
+  // The GEMV (launched with programmatic serialization) may start its weight stream now; it
+  // reads the workspace only after its dependency wait, i.e. after this grid has completed.
+  if (threadIdx.x == 0) launch_dependents();
+  const int pi = blockIdx.x;
+  const int p0 = pi * p.panel_steps;
+  const int pk = min(p.panel_steps, p.steps - p0) * kItemsPerStage * kItemK;
+  unsigned char* slot = ws + static_cast<int64_t>(pi) * p.xslot;
+  const half* x0 = a.x + static_cast<int64_t>(p0) * kItemsPerStage * kItemK;
+  permute_x_panel<false, kXprepThreads>(
+      a, p, pk, reinterpret_cast<const unsigned char*>(x0), a.k, slot,
+      reinterpret_cast<float2*>(slot + static_cast<int64_t>(a.m) * p.xs_stride), threadIdx.x);
 }
 
 // The consumers' side of the stage ring (slot and phase kept incrementally: no division).
@@ -203,8 +241,19 @@ __device__ __forceinline__ void issue_x_panel(const GemvArgs& a, int k0, int pk,
   }
 }
 
+// Copies workspace slot pi (the permuted x panel and its corr table) into the raw x buffer.
+__device__ __forceinline__ void issue_x_slot(const MmaPlan& p, int pi, unsigned char* xr,
+                                             uint64_t* xfull, uint64_t policy, int lane) {
+  if (lane == 0) {
+    mbar_arrive_expect_tx(xfull, static_cast<uint32_t>(p.xslot));
+    bulk_g2s(xr, p.xpre + static_cast<int64_t>(pi) * p.xslot, static_cast<uint32_t>(p.xslot),
+             xfull, policy);
+  }
+  __syncwarp();
+}
+
 // Streams the CTA's weights (panel by panel, block by block, stage by stage) and, per panel, its
-// raw x. The first p.pre_stages weight stages go out before the dependency wait (unless strict);
+// raw x (or, with a workspace, its pre-permuted x slot). The first p.pre_stages weight stages go out before the dependency wait (unless strict);
 // x for panel 0 right after it, ahead of the remaining weight stages.
 __device__ __forceinline__ void produce(const GemvArgs& a, const MmaPlan& p, const WeightMaps& maps,
                                         int row_begin, int rows, unsigned char* smem) {
@@ -222,8 +271,12 @@ __device__ __forceinline__ void produce(const GemvArgs& a, const MmaPlan& p, con
   bool x0_sent = false;
   if (pre == 0) {
     if (!p.strict) grid_dependency_wait();
-    issue_x_panel(a, 0, min(p.panel_steps, p.steps) * kItemsPerStage * kItemK, xr,
-                  &bars[kBarXFull], xpolicy, lane);
+    if (p.xpre) {
+      issue_x_slot(p, 0, xr, &bars[kBarXFull], xpolicy, lane);
+    } else {
+      issue_x_panel(a, 0, min(p.panel_steps, p.steps) * kItemsPerStage * kItemK, xr,
+                    &bars[kBarXFull], xpolicy, lane);
+    }
     x0_sent = true;
   }
   bool ok = true;
@@ -235,7 +288,9 @@ __device__ __forceinline__ void produce(const GemvArgs& a, const MmaPlan& p, con
         ok = false;
         if (lane == 0) atomicExch(p.status, kStatusEmptyBarrierTimeout);
       }
-      if (ok) {
+      if (ok && p.xpre) {
+        issue_x_slot(p, pi, xr, &bars[kBarXFull], xpolicy, lane);
+      } else if (ok) {
         issue_x_panel(a, p0 * kItemsPerStage * kItemK, (p1 - p0) * kItemsPerStage * kItemK, xr,
                       &bars[kBarXFull], xpolicy, lane);
       }
@@ -247,8 +302,12 @@ __device__ __forceinline__ void produce(const GemvArgs& a, const MmaPlan& p, con
       for (int j = p0; j < p1; ++j, ++it) {
         if (!x0_sent && it == pre) {
           grid_dependency_wait();
-          issue_x_panel(a, 0, (p1 - p0) * kItemsPerStage * kItemK, xr, &bars[kBarXFull], xpolicy,
-                        lane);
+          if (p.xpre) {
+            issue_x_slot(p, 0, xr, &bars[kBarXFull], xpolicy, lane);
+          } else {
+            issue_x_panel(a, 0, (p1 - p0) * kItemsPerStage * kItemK, xr, &bars[kBarXFull],
+                          xpolicy, lane);
+          }
           x0_sent = true;
         }
         if (ok && use > 0 && !mbar_wait_bounded(&empty[slot], (use - 1) & 1)) {
@@ -712,8 +771,13 @@ __global__ void __maxnreg__(CW == 16 ? 96 : 168)
       in.ok = false;
       atomicExch(p.status, kStatusFullBarrierTimeout);
     }
-    permute_x_panel<kNarrow, kConsumerThreads>(a, p, psteps * kItemsPerStage * kItemK, xr, xs,
-                                               corr, tid);
+    if (!kNarrow && p.xpre) {
+      copy_x_slot<kConsumerThreads>(xr, a.m * p.xs_stride, psteps * kItemsPerStage * p.mc * 8,
+                                    xs, corr, tid);
+    } else {
+      const int pk = psteps * kItemsPerStage * kItemK;
+      permute_x_panel<kNarrow, kConsumerThreads>(a, p, pk, xr, pk, xs, corr, tid);
+    }
     named_barrier(kConsumerBarrier, kConsumerThreads);
     if (tid == 0) mbar_arrive(&bars[kBarXEmpty]);  // the raw x buffer may be refilled
 
@@ -911,14 +975,18 @@ int consumer_warps_for(int m) { return m == 1 || m > 8 ? 8 : 16; }
 
 // Lays out shared memory for `panel_steps` stages per panel; true if it fits with at least
 // `min_stages` stages.
-bool plan_smem(const GemvArgs& a, MmaPlan* p, int min_stages) {
+bool plan_smem(const GemvArgs& a, MmaPlan* p, int min_stages, bool xpre) {
   const bool narrow = pad_of(a.m) < 8;
   const int pk = p->panel_steps * kItemsPerStage * kItemK;
   const int items = pk / kItemK;
   p->xs_stride = narrow ? (items * kNarrowItemBytes + 127) / 128 * 128 + 16 : pk * 2 + 64;
+  // A workspace slot: the permuted panel's xs rows, then its corr table (16-byte multiples).
+  const int64_t xslot =
+      static_cast<int64_t>(a.m) * p->xs_stride + static_cast<int64_t>(items) * p->mc * 8;
+  p->xslot = xpre ? static_cast<int>(xslot) : 0;
   int64_t off = 1024 + kZeroBytes;  // mbarriers, zeros
   p->off_xr = static_cast<int>(off);
-  off += static_cast<int64_t>(a.m) * pk * 2;
+  off += xpre ? xslot : static_cast<int64_t>(a.m) * pk * 2;
   p->off_xs = static_cast<int>(off);
   off += static_cast<int64_t>(a.m) * p->xs_stride;
   off = (off + 15) / 16 * 16;
@@ -938,7 +1006,7 @@ bool plan_smem(const GemvArgs& a, MmaPlan* p, int min_stages) {
   return true;
 }
 
-bool make_plan(const GemvArgs& a, MmaPlan* p, const char** why) {
+bool make_plan(const GemvArgs& a, MmaPlan* p, const char** why, bool xpre = false) {
   auto fail = [&](const char* reason) {
     if (why) *why = reason;
     return false;
@@ -953,11 +1021,13 @@ bool make_plan(const GemvArgs& a, MmaPlan* p, const char** why) {
   p->steps = a.k / (kItemK * kItemsPerStage);
   p->mc = (a.m + 1) & ~1;
   p->strict = 0;
+  p->xpre = nullptr;
+  xpre = xpre && pad_of(a.m) == 8;  // the wide path only
   // Fewest k-panels that leave a deep ring; then accept a shallower one.
   for (const int min_stages : {8, 4, 3}) {
     for (int panels = 1; panels <= p->steps; ++panels) {
       p->panel_steps = (p->steps + panels - 1) / panels;
-      if (plan_smem(a, p, min_stages)) return true;
+      if (plan_smem(a, p, min_stages, xpre)) return true;
     }
   }
   return fail("x does not fit in shared memory");
@@ -988,10 +1058,22 @@ bool stream_mma_supported(const GemvArgs& a, const char** why) {
   return make_plan(a, &p, why);
 }
 
-cudaError_t launch_stream_mma(const GemvArgs& a, cudaStream_t stream, bool strict,
-                              const PeerSet* peers, const GroupOut* groups) {
+int64_t stream_mma_workspace_bytes(const GemvArgs& a) {
   MmaPlan p;
-  if (!make_plan(a, &p, nullptr)) return cudaErrorInvalidValue;
+  if (a.epilogue != kStoreY || !make_plan(a, &p, nullptr, true) || p.xslot == 0) return 0;
+  const int64_t panels = (p.steps + p.panel_steps - 1) / p.panel_steps;
+  return panels * p.xslot;
+}
+
+cudaError_t launch_stream_mma(const GemvArgs& a, cudaStream_t stream, bool strict,
+                              const PeerSet* peers, const GroupOut* groups, void* workspace,
+                              int64_t workspace_bytes) {
+  MmaPlan p;
+  // With a large enough workspace the wide path takes x permuted once by the pre-kernel.
+  const int64_t ws_need = workspace ? stream_mma_workspace_bytes(a) : 0;
+  const bool xpre = ws_need > 0 && workspace_bytes >= ws_need;
+  if (!make_plan(a, &p, nullptr, xpre)) return cudaErrorInvalidValue;
+  if (xpre) p.xpre = static_cast<const unsigned char*>(workspace);
   const bool exchange = a.epilogue == kGatherPeers || a.epilogue == kReducePeers;
   if (exchange != (peers != nullptr)) return cudaErrorInvalidValue;
   if ((a.epilogue == kGroupedY) != (groups != nullptr)) return cudaErrorInvalidValue;
@@ -1007,6 +1089,13 @@ cudaError_t launch_stream_mma(const GemvArgs& a, cudaStream_t stream, bool stric
   int dev = 0;
   const cudaError_t derr = cudaGetDevice(&dev);
   if (derr != cudaSuccess) return derr;
+  if (xpre) {
+    const int panels = (p.steps + p.panel_steps - 1) / p.panel_steps;
+    stream_mma_xprep_kernel<<<panels, kXprepThreads, 0, stream>>>(
+        a, p, static_cast<unsigned char*>(workspace));
+    const cudaError_t perr = cudaGetLastError();
+    if (perr != cudaSuccess) return perr;
+  }
   return with_shape(a.m, [&]<int MP, int MT, int CW, int MC>() {
     cudaError_t result = cudaSuccess;
     std::call_once(g_attr_once[shape_index(a.m)][dev & 63], [&] {
