@@ -92,6 +92,18 @@ def test_workspace_size_is_nonnegative():
     assert capi.lib().int4gemv_w4a16_workspace_size(1, 8192, 8192, 128) >= 0
 
 
+def test_workspace_only_for_the_wide_fast_path():
+    """The fast path uses a workspace (x permuted once per call) for M >= 5 only, and only on its
+    own shapes (group 128, K % 1024 == 0)."""
+    size = capi.lib().int4gemv_w4a16_workspace_size
+    assert size(1, 8192, 8192, 128) == 0 and size(4, 8192, 8192, 128) == 0
+    big = size(32, 8192, 8192, 128)
+    assert size(5, 8192, 8192, 128) > 0 and big > size(16, 8192, 8192, 128) > 0
+    assert big >= 32 * 8192 * 2  # at least x itself, permuted
+    assert size(16, 8192, 8192, 64) == 0 and size(16, 8192, 1152, 128) == 0
+    assert size(0, 8192, 8192, 128) == 0 and size(16, 8192, 8192, 100) == 0
+
+
 def test_peers_struct_layout():
     """The ctypes mirror of int4gemv_peers_t has the C struct's size."""
     import ctypes
