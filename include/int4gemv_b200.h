@@ -232,9 +232,10 @@ size_t int4gemv_peers_struct_bytes(void);
  * this call, so when the kernel completes y is whole. K: each CTA writes its fp32 partial sums,
  * tagged, into every rank's exchange buffer and writes y = the ranks' partials added in rank order
  * (bit-identical on every rank).
- * Every rank must make the same sequence of calls with the same m, n, k (so each launches the
- * same CTAs), and a rank's calls on one set of buffers must be ordered on one stream (each after
- * the previous one has completed or, with programmatic dependent launch, past its dependency). A wait on a peer's word is bounded (2 s); when it runs out the kernel records
+ * Every rank must make the same sequence of calls on a set of buffers with the same m and n (the
+ * call number advances once per call on every rank), and a rank's calls on one set of buffers
+ * must be ordered on one stream (each after the previous one has completed or, with programmatic
+ * dependent launch, past its dependency). A wait on a peer's word is bounded (2 s); when it runs out the kernel records
  * status 3 (int4gemv_device_status) and finishes with an undefined y. */
 int int4gemv_w4a16_exchange(void* y, const void* x, const void* qweight, const void* scales,
                             const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,

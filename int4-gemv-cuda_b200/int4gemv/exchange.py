@@ -14,9 +14,9 @@ needs no host-side state and can be captured in a CUDA graph and replayed. The h
 construction. Each call returns a new y tensor.
 
 Constraints: the fast path's shapes (group 128, the rank's K a multiple of 1024, M <= 32); rows
-split needs N % world == 0 (equal shards, so every rank launches the same CTAs); K split cuts K in
-whole 1024-weight stages, as evenly as they go (28672 over 8 ranks: 4 ranks of 4096, 4 of 3072);
-at most 8 ranks; every rank makes the same calls in the same order.
+split needs N % world == 0 (equal shards, so a rank knows where every other rank's columns go); K
+split cuts K in whole 1024-weight stages, as evenly as they go (28672 over 8 ranks: 4 ranks of
+4096, 4 of 3072); at most 8 ranks; every rank makes the same calls in the same order.
 """
 
 from __future__ import annotations
