@@ -74,3 +74,11 @@ def test_interleave_rows():
     assert torch.equal(r[0::2], g) and torch.equal(r[1::2], u)
     with pytest.raises(ValueError):
         quant.interleave_rows(g, u[:2])
+
+
+def test_stack_rows():
+    a = torch.arange(6, dtype=torch.int32).reshape(2, 3)
+    b = torch.arange(6, 15, dtype=torch.int32).reshape(3, 3)
+    st = quant.stack_rows(a, b)
+    assert st.shape == (5, 3) and st.is_contiguous()
+    assert torch.equal(st[:2], a) and torch.equal(st[2:], b)

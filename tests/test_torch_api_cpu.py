@@ -101,3 +101,22 @@ def test_cuda_op_rejects_cpu_tensors():
             getattr(ops, name)(x, q, s, s, 128)
         assert str(e.value).splitlines()[0] == (
             f"{name}: expected all inputs on one cuda device, got cpu and cpu")
+
+
+def test_new_ops_reject_cpu_tensors():
+    """The B200 additions refuse CPU tensors with a clear message (no CPU fallback)."""
+    x = torch.zeros(1, 1024, dtype=torch.float16)
+    q = torch.zeros(8, 128, dtype=torch.int32)
+    s = torch.zeros(8, 8, dtype=torch.float16)
+    for call in (lambda: ops.w4a16_silu_mul(x, q, s, s, 128),
+                 lambda: ops.w4a16_bias_residual(x, q, s, s, 128),
+                 lambda: ops.w4a16_grouped(x, q, s, s, 128, [8])):
+        with pytest.raises(RuntimeError, match="cuda"):
+            call()
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.quantize(torch.zeros(8, 1024), 128)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.pack(torch.zeros(8, 1024, dtype=torch.int32))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.repack_gptq(torch.zeros(128, 8, dtype=torch.int32), torch.zeros(8, 1, dtype=torch.int32),
+                        torch.zeros(8, 8, dtype=torch.float16), 128)
