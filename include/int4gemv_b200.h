@@ -11,12 +11,14 @@
  *   y        [M, N]          fp16 (written)
  * Unless stated otherwise pointers are DEVICE pointers on the current CUDA device, `stream` is a
  * cudaStream_t (NULL = the legacy default stream), and calls are asynchronous: they enqueue work on
- * `stream` and return. No entry point synchronises the device.
+ * `stream` and return. Only int4gemv_device_status, int4gemv_peer_alloc / _open / _close / _free
+ * and the first call of int4gemv_w4a16_exchange_static on a device synchronise.
  *
  * Every entry point returns INT4GEMV_OK (0) or an error code; int4gemv_last_error() then gives a
  * message for the calling thread. Argument errors use the reference's check messages
  * (csrc/checks.cpp:9-44, csrc/common.cuh:84-112), prefixed by the operator name.
- * M, N or K equal to 0 is valid: nothing is launched (y is empty).
+ * M or N equal to 0 is valid and launches nothing (y is empty); K = 0 gives y = 0 (plus bias and
+ * residual where the entry point takes them).
  */
 #ifndef INT4GEMV_B200_H_
 #define INT4GEMV_B200_H_
