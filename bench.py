@@ -7,9 +7,13 @@ step = one call of the operator (int4gemv.ops.w4a16) on one batch.
 Measurement:
   value       effective HBM bandwidth, algorithmic bytes (N K/2 + N K/32 + 2 M K + 2 M N, the
               reference's int4_bytes) per call / device time per call, summed over ranks;
-              K back-to-back calls replayed from CUDA graphs, each call on a different weight
-              set from a rotation whose total size is > 2x the L2, so every call reads its
-              weights from HBM (no flush kernel in the timed region)
+              exactly K (--steps) back-to-back calls captured in one CUDA graph and replayed
+              once after W (--warmup) eager calls, each call on a different weight set from a
+              rotation whose total size is > 2x the L2, so every call reads its weights from HBM
+              (no flush kernel in the timed region; one 1 GiB write just before it)
+  eager / host  the same calls launched one by one from the host (eager_us_per_call, device
+              time) and the host's own time per ops.w4a16 call (host_us_per_call)
+  sweep       the BASELINE shapes (M sweep at 8192 x 8192, the MLP shapes) against cuBLAS FP16
   e2e         the same metric through the public API with host buffers: per step, copy x from
               pinned host memory, call ops.w4a16, copy y back to pinned host memory and wait
   roofline    achieved bytes/s of the GEMV kernel (algorithmic bytes / its average launch
@@ -275,6 +279,67 @@ def time_isolated(fn, iters: int = 100, warmup: int = 10) -> float:
     return statistics.median(a.elapsed_time(b) for a, b in zip(starts, ends)) / 1e3
 
 
+def time_steps_graph(calls, steps: int, warmup: int, world: int = 1):
+    """Seconds per call of exactly `steps` calls (calls[i % len(calls)]) captured in one CUDA graph
+    and replayed once, timed with CUDA events on the replaying stream; `warmup` untimed eager calls
+    first. A 1 GiB write is queued right before the start event, so the GPU is busy while the host
+    launches the graph and the first timed call starts from a flushed L2. Returns (seconds per
+    call, wall-clock start, wall-clock end) of the timed region."""
+    global _flush_buf
+    if _flush_buf is None:
+        _flush_buf = torch.ones(256 * 1024 * 1024, device="cuda")
+    for i in range(warmup):
+        calls[i % len(calls)]()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(steps):
+            calls[i % len(calls)]()
+    barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    _flush_buf.fill_(1.0)
+    start.record()
+    g.replay()
+    end.record()
+    end.synchronize()
+    t1 = time.perf_counter()
+    barrier(world)
+    del g
+    return start.elapsed_time(end) / 1e3 / steps, t0, t1
+
+
+def time_eager_calls(calls, n: int) -> float:
+    """Seconds per call of `n` calls launched one by one from the host (no graph), CUDA events."""
+    for i in range(8):
+        calls[i % len(calls)]()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(n):
+        calls[i % len(calls)]()
+    end.record()
+    end.synchronize()
+    return start.elapsed_time(end) / 1e3 / n
+
+
+def host_time_per_call(calls, n: int) -> float:
+    """Host seconds per call (argument checks, allocation of y, launch) with the GPU queue kept
+    non-empty, so no call waits for the device: wall clock over `n` calls, before any sync."""
+    torch.cuda.synchronize()
+    global _flush_buf
+    if _flush_buf is None:
+        _flush_buf = torch.ones(256 * 1024 * 1024, device="cuda")
+    _flush_buf.fill_(1.0)  # a few hundred microseconds of device work ahead of the calls
+    t0 = time.perf_counter()
+    for i in range(n):
+        calls[i % len(calls)]()
+    t1 = time.perf_counter()
+    torch.cuda.synchronize()
+    return (t1 - t0) / n
+
+
 def cpu_sample(ref, x_cpu, q_cpu, s_cpu, z_cpu, budget_s: float, threads: int):
     """Time the reference's CPU path on growing row samples until budget_s is spent."""
     if ref is not None:
@@ -516,38 +581,19 @@ def run_ours(args, world, rank, local):
         return lambda: ops.w4a16(x, *sets[i], GROUP)
 
     calls = [call(i) for i in range(n_sets)]
-    per_graph = n_sets * max(1, 64 // n_sets)
-    calls = [calls[i % n_sets] for i in range(per_graph)]
-    g = graph_of(calls)
-    reps_w = max(1, math.ceil(args.warmup / per_graph))
-    for _ in range(reps_w):
-        g.replay()
-    torch.cuda.synchronize()
-
-    # ---- timed region: exactly `steps` calls (full graphs, then the remainder launched directly)
-    full, rem = divmod(args.steps, per_graph)
+    # ---- timed region: exactly `steps` back-to-back calls, captured in one CUDA graph (each call
+    # on the next weight set of the rotation) and replayed once; `warmup` eager calls before it
     sampler = ClockSampler(torch.cuda.current_device()).start()
-    barrier(world)
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    for _ in range(full):
-        g.replay()
-    for i in range(rem):
-        calls[i]()
-    end.record()
-    end.synchronize()
-    t1 = time.perf_counter()
-    barrier(world)
+    per_call_s, t0, t1 = time_steps_graph(calls, args.steps, args.warmup, world)
     sampler.stop()
-    local_s = start.elapsed_time(end) / 1e3
-    total_s = max_over_ranks(local_s, world)
+    total_s = max_over_ranks(per_call_s * args.steps, world)
     per_call_s = total_s / args.steps
     bytes_call = int4_bytes(M, N, K, GROUP)
     value = world * bytes_call * args.steps / total_s / 1e9
     clocks = sampler.summary(t0, t1)
-    del g
+    # the same calls launched one by one from the host (no graph), and the host's own time per call
+    eager_s = time_eager_calls(calls, 200)
+    host_s = host_time_per_call(calls, 200)
 
     # ---- one isolated call, the reference's way (L2 read-flush before each call, events around
     # the call): the per-launch duration the roofline fraction uses
@@ -583,6 +629,9 @@ def run_ours(args, world, rank, local):
         extra["vectorized_us"] = round(time_graph_calls(vv * max(1, 64 // n_sets), 5000, 100) * 1e6, 3)
         extra["quantize"] = time_quantize()
         extra["grouped_qkv"] = time_grouped()
+        if not args.no_sweep:
+            peak_gbs = measured_peak()[0]
+            extra["sweep"] = [sweep_one(m, n, k, peak_gbs) for m, n, k in SWEEP_DEFAULT]
 
     # ---- end to end through the public API with host buffers
     x_host = x.cpu().pin_memory()
@@ -626,8 +675,9 @@ def run_ours(args, world, rank, local):
                 "traffic": traffic.get("bytes_per_launch") if traffic else None,
                 "algorithmic_bytes": bytes_call,
                 "kernel": kernel, "launch_us": round(per_call_s * 1e6, 3),
-                "launch_timing": "average over the timed region (back-to-back launches, graph "
-                                 "replays, CUDA events on the launching stream)",
+                "launch_timing": "the timed region's average: exactly `steps` back-to-back "
+                                 "launches replayed from one CUDA graph, CUDA events on the "
+                                 "replaying stream",
                 "isolated_launch_us": round(launch_s * 1e6, 3),
                 "isolated_frac": round(bytes_call / launch_s / 1e9 / peak, 4)}
 
@@ -649,9 +699,12 @@ def run_ours(args, world, rank, local):
                    "m": M, "n": N, "k": K, "group_size": GROUP, "kernel": kernel,
                    "l2": f"no flush; {n_sets} rotating weight sets of {set_bytes / 2**20:.1f} MiB "
                          f"(> 2x the 126 MB L2) so every call reads its weights from HBM",
-                   "timing": "CUDA graphs of back-to-back calls, CUDA events",
+                   "timing": f"one CUDA graph of exactly {args.steps} back-to-back calls, replayed "
+                             f"once after {args.warmup} eager warm-up calls, CUDA events",
                    "parallelism": f"independent weights per GPU x{world}"},
         "roofline": roofline, "clocks": clocks, "e2e": e2e, "gpu_launches": args.steps,
+        "eager_us_per_call": round(eager_s * 1e6, 3),
+        "host_us_per_call": round(host_s * 1e6, 3),
         **extra, "parity": msg,
     }
     if cpu is not None:
@@ -666,43 +719,54 @@ SWEEP = ([(m, 8192, 8192) for m in (1, 2, 4, 8, 16, 32)]
             (1, 8192, 28672), (8, 28672, 8192), (8, 8192, 28672)])
 
 
-def run_sweep(args):
-    """--sweep: the BASELINE shapes (M sweep at 8192 x 8192, the MLP shapes, the unsharded
-    multi-GPU shapes), one JSON line each: ops.w4a16 and cuBLAS FP16 back to back from CUDA graphs
-    over weight rotations larger than 2x L2, plus one isolated call after an L2 flush."""
+# The shapes of the default line's "sweep" key: BASELINE's M sweep at 8192 x 8192 and the M = 1
+# shapes of the other single-GPU configs.
+SWEEP_DEFAULT = ([(m, 8192, 8192) for m in (1, 2, 4, 8, 16, 32)]
+                 + [(1, 4096, 4096), (1, 14336, 4096), (1, 4096, 14336)])
+
+
+def sweep_one(m: int, n: int, k: int, peak: float, calls_timed: int = 1000) -> dict:
+    """One BASELINE shape: ops.w4a16 and cuBLAS FP16 (F.linear on fp16 weights) back to back from
+    CUDA graphs over weight rotations larger than 2x L2, plus one isolated call after an L2 flush."""
     from int4gemv import ops
     import torch.nn.functional as F
 
+    gen = torch.Generator(device="cuda").manual_seed(m * 7 + n + k)
+    set_bytes = n * k // 2 + 2 * n * (k // GROUP) * 2
+    n_sets = max(2, math.ceil(2 * L2_BYTES / set_bytes) + 1)
+    sets = [ops.quantize(torch.randn(n, k, generator=gen, device="cuda",
+                                     dtype=torch.float16) * 0.02, GROUP)
+            for _ in range(n_sets)]
+    x = torch.randn(m, k, generator=gen, device="cuda", dtype=torch.float16)
+    calls = [(lambda st=st: ops.w4a16(x, *st, GROUP)) for st in sets]
+    ours = time_graph_calls(calls * max(1, 32 // n_sets), calls_timed, 100)
+    rot = iter(range(10**9))
+    iso = time_isolated(lambda: calls[next(rot) % n_sets](), iters=50)
+    kernel = ops.w4a16_kernel(x, *sets[0], GROUP)
+    del sets, calls
+    w16 = [torch.randn(n, k, generator=gen, device="cuda", dtype=torch.float16) * 0.02
+           for _ in range(max(2, math.ceil(2 * L2_BYTES / (n * k * 2)) + 1))]
+    cub = [(lambda w=w: F.linear(x, w)) for w in w16]
+    cublas = time_graph_calls(cub * max(1, 16 // len(cub)), calls_timed, 50)
+    del w16, cub
+    b = int4_bytes(m, n, k, GROUP)
+    return {"m": m, "n": n, "k": k, "kernel": kernel,
+            "us": round(ours * 1e6, 2), "gb_s": round(b / ours / 1e9, 1),
+            "frac_of_hbm": round(b / ours / 1e9 / peak, 3),
+            "isolated_us": round(iso * 1e6, 2),
+            "cublas_fp16_us": round(cublas * 1e6, 2),
+            "speedup_vs_cublas": round(cublas / ours, 2)}
+
+
+def run_sweep(args):
+    """--sweep: the BASELINE shapes (M sweep at 8192 x 8192, the MLP shapes, the unsharded
+    multi-GPU shapes), one JSON line each (sweep_one)."""
     torch.cuda.set_device(0)
     peak, _ = measured_peak()
     for m, n, k in SWEEP:
         if m < args.sweep_min_m:
             continue
-        gen = torch.Generator(device="cuda").manual_seed(m * 7 + n + k)
-        set_bytes = n * k // 2 + 2 * n * (k // GROUP) * 2
-        n_sets = max(2, math.ceil(2 * L2_BYTES / set_bytes) + 1)
-        sets = [ops.quantize(torch.randn(n, k, generator=gen, device="cuda",
-                                         dtype=torch.float16) * 0.02, GROUP)
-                for _ in range(n_sets)]
-        x = torch.randn(m, k, generator=gen, device="cuda", dtype=torch.float16)
-        calls = [(lambda st=st: ops.w4a16(x, *st, GROUP)) for st in sets]
-        ours = time_graph_calls(calls * max(1, 32 // n_sets), 2000, 100)
-        rot = iter(range(10**9))
-        iso = time_isolated(lambda: calls[next(rot) % n_sets]())
-        kernel = ops.w4a16_kernel(x, *sets[0], GROUP)
-        del sets, calls
-        w16 = [torch.randn(n, k, generator=gen, device="cuda", dtype=torch.float16) * 0.02
-               for _ in range(max(2, math.ceil(2 * L2_BYTES / (n * k * 2)) + 1))]
-        cub = [(lambda w=w: F.linear(x, w)) for w in w16]
-        cublas = time_graph_calls(cub * max(1, 16 // len(cub)), 1000, 50)
-        del w16, cub
-        b = int4_bytes(m, n, k, GROUP)
-        print(json.dumps({"m": m, "n": n, "k": k, "kernel": kernel,
-                          "us": round(ours * 1e6, 2), "gb_s": round(b / ours / 1e9, 1),
-                          "frac_of_hbm": round(b / ours / 1e9 / peak, 3),
-                          "isolated_us": round(iso * 1e6, 2),
-                          "cublas_fp16_us": round(cublas * 1e6, 2),
-                          "speedup_vs_cublas": round(cublas / ours, 2)}), flush=True)
+        print(json.dumps(sweep_one(m, n, k, peak, 2000)), flush=True)
 
 
 def run_profile_case(args):
@@ -758,6 +822,8 @@ def main():
     ap.add_argument("--sweep", action="store_true",
                     help="time the BASELINE shapes (one JSON line each) instead of the headline")
     ap.add_argument("--sweep-min-m", type=int, default=1, help="--sweep: only shapes with M >= this")
+    ap.add_argument("--no-sweep", action="store_true",
+                    help="skip the 'sweep' key (the BASELINE shapes against cuBLAS) of the line")
     ap.add_argument("--no-sharded", action="store_true",
                     help="with more than one GPU, skip the sharded-layer timing")
     args = ap.parse_args()

@@ -97,14 +97,16 @@ int int4gemv_w4a16(void* y, const void* x, const void* qweight, const void* scal
                    const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
                    void* workspace, int64_t workspace_bytes, void* stream);
 
-/* Name of the kernel int4gemv_w4a16 picks for this shape and these pointers ("stream_mma",
- * "mma_pipeline", "vectorized", "coalesced"); for tests and the benchmark. Static storage. */
+/* Name of the kernel int4gemv_w4a16 picks for this shape and these pointers ("stripe_mma",
+ * "stream_mma", "mma_pipeline", "vectorized", "coalesced"); for tests and the benchmark. Static
+ * storage. */
 const char* int4gemv_w4a16_kernel_name(const void* x, const void* qweight, const void* scales,
                                        const void* zeros, int64_t m, int64_t n, int64_t k,
                                        int64_t group_size);
 
-/* Runs one named kernel instead of the automatic choice: "stream_mma", "tcgen05", "mma_pipeline",
- * "vectorized" (128 threads, 2 rows per warp), "coalesced" or "naive". For tests and benchmarks.
+/* Runs one named kernel instead of the automatic choice: "stripe_mma", "stream_mma", "tcgen05",
+ * "mma_pipeline", "vectorized" (128 threads, 2 rows per warp), "coalesced" or "naive". For tests
+ * and benchmarks.
  * Fails with
  * INT4GEMV_ERR_INVALID if that kernel does not support the shape or the pointers' alignment. */
 int int4gemv_w4a16_kernel(const char* kernel, void* y, const void* x, const void* qweight,
@@ -142,6 +144,15 @@ int int4gemv_w4a16_bias_residual(void* y, const void* x, const void* qweight, co
 int int4gemv_w4a16_grouped(int count, void* const* ys, const int64_t* ns, const void* x,
                            const void* qweight, const void* scales, const void* zeros, int64_t m,
                            int64_t k, int64_t group_size, void* stream);
+
+/* y [M, N] fp32 = x @ W^T, the fp32 row sums themselves with no rounding to fp16: the local partial
+ * sums of a layer split along K over several GPUs, which are added across ranks and rounded to
+ * fp16 once (int4gemv/sharded.py). Same inputs and checks as int4gemv_w4a16; needs the fast path's
+ * shapes (group_size 128, K a multiple of 1024, M <= 32, 16-byte aligned x, qweight, scales,
+ * zeros), INT4GEMV_ERR_INVALID with the reason otherwise. New: the reference returns fp16 only. */
+int int4gemv_w4a16_f32(void* y, const void* x, const void* qweight, const void* scales,
+                       const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
+                       void* stream);
 
 /* ---- Packed-format helpers on the device (int4gemv/quant.py:40-53), bit-exact ---------------- */
 
@@ -248,14 +259,34 @@ int int4gemv_w4a16_exchange(void* y, const void* x, const void* qweight, const v
  * (4 MiB + 4 KiB per device), so no int4gemv_peer_alloc and no caller buffers. mode
  * INT4GEMV_SHARD_ROWS or INT4GEMV_SHARD_K; y [m, n] fp16 as int4gemv_w4a16 computes it, through
  * the exchange epilogue. Sizes needing more than the static buffer (m x n > 256 Ki in either
- * mode) are rejected with INT4GEMV_ERR_INVALID and a message giving the limit.
- * The first call on a device does the setup (looks up the arrays with cudaGetSymbolAddress and
- * clears the exchange buffer and the counters, synchronously), so it must come before any stream capture. All calls on
- * a device share the one buffer: calls that overlap in time (different streams, or other host
- * threads) race. No counterpart in the reference. */
+ * mode) are rejected with INT4GEMV_ERR_INVALID and a message giving the limit; so are the shapes
+ * the fast path does not take (same checks as int4gemv_w4a16_exchange). Every such check runs
+ * before the setup below, so a rejected call does no setup.
+ * The first valid call on a device does the setup (looks up the arrays with cudaGetSymbolAddress
+ * and clears the exchange buffer and the counters, synchronously), so it must come before any
+ * stream capture. The looked-up addresses are kept for the life of the process: after
+ * cudaDeviceReset on a device this entry point must not be used on that device again. All calls
+ * on a device share the one buffer, whatever their shapes: calls that overlap in time (different
+ * streams, or other host threads) race. No counterpart in the reference. */
 int int4gemv_w4a16_exchange_static(void* y, const void* x, const void* qweight,
                                    const void* scales, const void* zeros, int64_t m, int64_t n,
                                    int64_t k, int64_t group_size, int mode, void* stream);
+
+/* ---- Stream ordering of the weights ---------------------------------------------------------- */
+
+/* The pipelined kernels (stripe_mma, stream_mma, tcgen05, and the fused epilogues and exchange on
+ * them) are launched with programmatic dependent launch: a call may start while the previous
+ * kernel in the stream is still running, and by default it already streams its qweight, scales
+ * and zeros then; x is read, and y written, only after that kernel has completed. This is what
+ * lets back-to-back GEMVs keep HBM busy, and it is safe whenever the weights were not written by
+ * the kernel right before the call in the same stream (weights loaded or repacked earlier, or
+ * written by work that was followed by another kernel, an event or a copy, are fine). A caller
+ * that does write the weights in the immediately preceding kernel (e.g. re-quantising in place
+ * and then multiplying) calls int4gemv_set_strict_weights(1): every pipelined kernel then reads
+ * its weights only after the previous kernel has completed, at some cost in overlap. Process-wide;
+ * 0 restores the default. INT4GEMV_ERR_INVALID for other values. No counterpart in the reference
+ * (its kernels use plain stream order). */
+int int4gemv_set_strict_weights(int strict);
 
 /* ---- Device-side status --------------------------------------------------------------------- */
 

@@ -34,7 +34,8 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++20", "-Xcompiler", "-fPIC",
                      f"-I{INCLUDE}", f"-I{CSRC}"]
 CU_SOURCES = [
-    "capi.cu", "simt.cu", "mma_pipeline.cu", "tc_gemv.cu", "stream_mma.cu", "weight_stream.cu",
+    "capi.cu", "simt.cu", "mma_pipeline.cu", "tc_gemv.cu", "stream_mma.cu", "stripe_mma.cu",
+    "weight_stream.cu",
     "packed.cu", "quantize.cu", "repack.cu",
 ]
 # The CPU path must keep one IEEE rounding per operation: no contraction, no fast-math.

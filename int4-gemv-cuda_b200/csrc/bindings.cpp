@@ -153,6 +153,18 @@ at::Tensor w4a16_silu_mul(const at::Tensor& x, const at::Tensor& qweight,
   return y;
 }
 
+at::Tensor w4a16_f32(const at::Tensor& x, const at::Tensor& qweight, const at::Tensor& scales,
+                     const at::Tensor& zeros, int64_t group_size) {
+  check_inputs("w4a16_f32", x, qweight, scales, zeros, group_size, c10::DeviceType::CUDA);
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t m = x.size(0), n = qweight.size(0), k = x.size(1);
+  at::Tensor y = at::empty({m, n}, x.options().dtype(at::kFloat));
+  check_status(int4gemv_w4a16_f32(y.data_ptr(), x.data_ptr(), qweight.data_ptr(),
+                                  scales.data_ptr(), zeros.data_ptr(), m, n, k, group_size,
+                                  stream_of(x)));
+  return y;
+}
+
 std::vector<at::Tensor> w4a16_grouped(const at::Tensor& x, const at::Tensor& qweight,
                                       const at::Tensor& scales, const at::Tensor& zeros,
                                       int64_t group_size, const std::vector<int64_t>& sizes) {
@@ -359,6 +371,8 @@ PYBIND11_MODULE(int4gemv_ops, m) {
   m.def("w4a16_info", &int4gemv::w4a16_info, py::arg("m"));
   m.def("w4a16_silu_mul", &int4gemv::w4a16_silu_mul, py::arg("x"), py::arg("qweight"),
         py::arg("scales"), py::arg("zeros"), py::arg("group_size"));
+  m.def("w4a16_f32", &int4gemv::w4a16_f32, py::arg("x"), py::arg("qweight"), py::arg("scales"),
+        py::arg("zeros"), py::arg("group_size") = 128);
   m.def("w4a16_with", &int4gemv::w4a16_with, py::arg("x"), py::arg("qweight"), py::arg("scales"),
         py::arg("zeros"), py::arg("group_size"), py::arg("kernel"));
   m.def("w4a16_kernel", &int4gemv::w4a16_kernel, py::arg("x"), py::arg("qweight"),

@@ -2,6 +2,7 @@
 // the launchers, and error reporting through int4gemv_last_error(). No torch; the only device
 // allocation is int4gemv_peer_alloc's, which the caller asks for.
 #include <algorithm>
+#include <atomic>
 #include <climits>
 #include <cstdarg>
 #include <cstdio>
@@ -21,6 +22,11 @@ void sequential_cpu(uint16_t* y, const uint16_t* x, const uint32_t* q, const uin
 namespace {
 
 thread_local std::string g_last_error;
+
+// int4gemv_set_strict_weights: when set, the pipelined kernels read the weights only after the
+// previous kernel in the stream has completed (see the header).
+std::atomic<int> g_strict_weights{0};
+bool strict_weights() { return g_strict_weights.load(std::memory_order_relaxed) != 0; }
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -147,9 +153,10 @@ int empty_cases(const char* name, void* y, int64_t m, int64_t n, int64_t k, cuda
 
 int launched(const char* name, cudaError_t err) { return err == cudaSuccess ? ok() : cuda_fail(name, err); }
 
-enum class Pick { kStreamMma, kTcgen05, kMmaPipeline, kVectorized, kCoalesced };
+enum class Pick { kStripeMma, kStreamMma, kTcgen05, kMmaPipeline, kVectorized, kCoalesced };
 
 Pick pick_kernel(const i4::GemvArgs& a) {
+  if (i4::stripe_mma_supported(a, nullptr)) return Pick::kStripeMma;
   if (i4::stream_mma_supported(a, nullptr)) return Pick::kStreamMma;
   if (i4::mma_pipeline_supported(a, nullptr)) return Pick::kMmaPipeline;
   if (a.group % 32 == 0 && reinterpret_cast<uintptr_t>(a.x) % 16 == 0 &&
@@ -162,10 +169,12 @@ Pick pick_kernel(const i4::GemvArgs& a) {
 // Launches the kernel pick_kernel chooses for `a` (the dispatch of int4gemv_w4a16).
 int run_picked(const char* name, const i4::GemvArgs& a, cudaStream_t st) {
   switch (pick_kernel(a)) {
+    case Pick::kStripeMma:
+      return launched(name, i4::launch_stripe_mma(a, st, strict_weights()));
     case Pick::kStreamMma:
-      return launched(name, i4::launch_stream_mma(a, st, false));
+      return launched(name, i4::launch_stream_mma(a, st, strict_weights()));
     case Pick::kTcgen05:
-      return launched(name, i4::launch_tc_gemv(a, st, false));
+      return launched(name, i4::launch_tc_gemv(a, st, strict_weights()));
     case Pick::kMmaPipeline:
       return launched(name, i4::launch_mma_pipeline(a, st));
     case Pick::kVectorized:
@@ -312,8 +321,9 @@ int int4gemv_kernel_info(const char* kernel, int64_t m, int64_t threads_per_bloc
   } else if (std::strcmp(kernel, "naive") == 0 || std::strcmp(kernel, "coalesced") == 0) {
     err = i4::simt_attrs(kernel, static_cast<int>(m), 0, 1, &at);
   } else if (std::strcmp(kernel, "w4a16") == 0) {
-    err = m <= 32 ? i4::stream_mma_attrs(static_cast<int>(m), &at)
-                  : i4::mma_pipeline_attrs(16, &at);
+    err = m <= 2    ? i4::stripe_mma_attrs(static_cast<int>(m), &at)
+          : m <= 32 ? i4::stream_mma_attrs(static_cast<int>(m), &at)
+                    : i4::mma_pipeline_attrs(16, &at);
   } else {
     return fail(INT4GEMV_ERR_INVALID, "kernel_info: unknown kernel '%s'", kernel);
   }
@@ -367,8 +377,8 @@ int int4gemv_w4a16(void* y, const void* x, const void* qweight, const void* scal
   if (done) return e;
   const i4::GemvArgs a = make_args(y, x, qweight, scales, zeros, m, n, k, group_size);
   if (workspace && workspace_bytes > 0 && pick_kernel(a) == Pick::kStreamMma) {
-    return launched(name, i4::launch_stream_mma(a, st, false, nullptr, nullptr, workspace,
-                                                workspace_bytes));
+    return launched(name, i4::launch_stream_mma(a, st, strict_weights(), nullptr, nullptr,
+                                                workspace, workspace_bytes));
   }
   return run_picked(name, a, st);
 }
@@ -401,7 +411,7 @@ int int4gemv_w4a16_grouped(int count, void* const* ys, const int64_t* ns, const 
   i4::GemvArgs a = make_args(ys[0], x, qweight, scales, zeros, m, total, k, group_size);
   if (k > 0 && i4::stream_mma_supported(a, nullptr)) {
     a.epilogue = i4::kGroupedY;
-    return launched(name, i4::launch_stream_mma(a, st, false, nullptr, &go));
+    return launched(name, i4::launch_stream_mma(a, st, strict_weights(), nullptr, &go));
   }
   // Other shapes: one launch per matrix on its rows of the stacked weights.
   int64_t row0 = 0;
@@ -444,6 +454,8 @@ const char* int4gemv_w4a16_kernel_name(const void* x, const void* qweight, const
   }
   const i4::GemvArgs a = make_args(nullptr, x, qweight, scales, zeros, m, n, k, group_size);
   switch (pick_kernel(a)) {
+    case Pick::kStripeMma:
+      return "stripe_mma";
     case Pick::kStreamMma:
       return "stream_mma";
     case Pick::kTcgen05:
@@ -472,11 +484,15 @@ int int4gemv_w4a16_kernel(const char* kernel, void* y, const void* x, const void
   const char* why = "unsupported shape";
   if (std::strcmp(kernel, "stream_mma") == 0) {
     if (!i4::stream_mma_supported(a, &why)) return fail(INT4GEMV_ERR_INVALID, "stream_mma: %s", why);
-    return launched(name, i4::launch_stream_mma(a, st, false));
+    return launched(name, i4::launch_stream_mma(a, st, strict_weights()));
+  }
+  if (std::strcmp(kernel, "stripe_mma") == 0) {
+    if (!i4::stripe_mma_supported(a, &why)) return fail(INT4GEMV_ERR_INVALID, "stripe_mma: %s", why);
+    return launched(name, i4::launch_stripe_mma(a, st, strict_weights()));
   }
   if (std::strcmp(kernel, "tcgen05") == 0) {
     if (!i4::tc_gemv_supported(a, &why)) return fail(INT4GEMV_ERR_INVALID, "tcgen05: %s", why);
-    return launched(name, i4::launch_tc_gemv(a, st, false));
+    return launched(name, i4::launch_tc_gemv(a, st, strict_weights()));
   }
   if (std::strcmp(kernel, "mma_pipeline") == 0) {
     if (!i4::mma_pipeline_supported(a, &why)) return fail(INT4GEMV_ERR_INVALID, "mma_pipeline: %s", why);
@@ -511,7 +527,26 @@ int int4gemv_w4a16_silu_mul(void* y, const void* x, const void* qweight, const v
   a.epilogue = i4::kSiluMul;
   const char* why = "unsupported shape";
   if (!i4::stream_mma_supported(a, &why)) return fail(INT4GEMV_ERR_INVALID, "%s: %s", name, why);
-  return launched(name, i4::launch_stream_mma(a, st, false));
+  return launched(name, i4::launch_stream_mma(a, st, strict_weights()));
+}
+
+int int4gemv_w4a16_f32(void* y, const void* x, const void* qweight, const void* scales,
+                       const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
+                       void* stream) {
+  const char* name = "w4a16_f32";
+  if (int e = check_sizes(name, m, n, k, group_size)) return e;
+  if (int e = check_pointers(name, m, n, k, y, x, qweight, scales, zeros)) return e;
+  const auto st = static_cast<cudaStream_t>(stream);
+  if (m == 0 || n == 0) return ok();
+  if (k == 0) {
+    const cudaError_t err = cudaMemsetAsync(y, 0, static_cast<size_t>(m * n * 4), st);
+    return err == cudaSuccess ? ok() : cuda_fail(name, err);
+  }
+  i4::GemvArgs a = make_args(y, x, qweight, scales, zeros, m, n, k, group_size);
+  a.epilogue = i4::kStoreF32;
+  const char* why = "unsupported shape";
+  if (!i4::stream_mma_supported(a, &why)) return fail(INT4GEMV_ERR_INVALID, "%s: %s", name, why);
+  return launched(name, i4::launch_stream_mma(a, st, strict_weights()));
 }
 
 int int4gemv_unpack(void* q, const void* qweight, int64_t n, int64_t k, void* stream) {
@@ -706,7 +741,8 @@ int int4gemv_w4a16_exchange(void* y, const void* x, const void* qweight, const v
   ps.rank = peers->rank;
   ps.n_total = static_cast<int>(n_out);
   ps.col0 = static_cast<int>(mode == INT4GEMV_SHARD_ROWS ? peers->col0 : 0);
-  return launched(name, i4::launch_stream_mma(a, static_cast<cudaStream_t>(stream), false, &ps));
+  return launched(name, i4::launch_stream_mma(a, static_cast<cudaStream_t>(stream),
+                                              strict_weights(), &ps));
 }
 
 int int4gemv_w4a16_exchange_static(void* y, const void* x, const void* qweight,
@@ -716,15 +752,28 @@ int int4gemv_w4a16_exchange_static(void* y, const void* x, const void* qweight,
   if (mode != INT4GEMV_SHARD_ROWS && mode != INT4GEMV_SHARD_K) {
     return fail(INT4GEMV_ERR_INVALID, "%s: unknown mode %d", name, mode);
   }
-  if (m < 0 || n < 0) return fail(INT4GEMV_ERR_INVALID, "%s: negative size", name);
-  const int64_t half = 8 * m * n;  // one tagged word per output, either mode
-  if (2 * half > kStaticExchangeBytes) {
+  // Every check that can reject the call runs before the first-call setup below, so an invalid
+  // call never triggers the synchronous setup.
+  if (int e = check_sizes(name, m, n, k, group_size)) return e;
+  if (m == 0 || n == 0 || k == 0) {
+    return fail(INT4GEMV_ERR_INVALID, "%s: M, N and K must be positive", name);
+  }
+  if (int e = check_pointers(name, m, n, k, y, x, qweight, scales, zeros)) return e;
+  // One 8-byte tagged word per output in each of two halves, either mode: M x N <= bytes / 16.
+  // Compared by division, so no product of the (int-sized) M and N can overflow.
+  constexpr int64_t kMaxOutputs = kStaticExchangeBytes / 16;
+  if (n > kMaxOutputs / m) {
     return fail(INT4GEMV_ERR_INVALID,
-                "%s: M = %lld, N = %lld needs %lld bytes of exchange buffer; the static buffer "
-                "holds %lld (M x N <= %lld)",
+                "%s: M = %lld, N = %lld needs more exchange buffer than there is; the static "
+                "buffer holds %lld bytes (M x N <= %lld)",
                 name, static_cast<long long>(m), static_cast<long long>(n),
-                static_cast<long long>(2 * half), static_cast<long long>(kStaticExchangeBytes),
-                static_cast<long long>(kStaticExchangeBytes / 16));
+                static_cast<long long>(kStaticExchangeBytes), static_cast<long long>(kMaxOutputs));
+  }
+  {
+    i4::GemvArgs a = make_args(y, x, qweight, scales, zeros, m, n, k, group_size);
+    a.epilogue = mode == INT4GEMV_SHARD_ROWS ? i4::kGatherPeers : i4::kReducePeers;
+    const char* why = "unsupported shape";
+    if (!i4::stream_mma_supported(a, &why)) return fail(INT4GEMV_ERR_INVALID, "%s: %s", name, why);
   }
   void* out = nullptr;
   void* counters = nullptr;
@@ -740,6 +789,14 @@ int int4gemv_w4a16_exchange_static(void* y, const void* x, const void* qweight,
   peers.counters = counters;
   return int4gemv_w4a16_exchange(y, x, qweight, scales, zeros, m, n, k, group_size, &peers,
                                  stream);
+}
+
+int int4gemv_set_strict_weights(int strict) {
+  if (strict != 0 && strict != 1) {
+    return fail(INT4GEMV_ERR_INVALID, "set_strict_weights: strict must be 0 or 1, got %d", strict);
+  }
+  g_strict_weights.store(strict, std::memory_order_relaxed);
+  return ok();
 }
 
 int int4gemv_device_status(int* status) {

@@ -60,6 +60,43 @@ __device__ __forceinline__ void unpack_pairs(uint32_t w, uint32_t (&h)[4]) {
   }
 }
 
+// Word i (0..3) of a 16-byte vector.
+__device__ __forceinline__ uint32_t word_of4(const uint4& v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+// x0..x7 (one 8-weight block of x, fp16) -> the B halves that match unpack_x16's A halves:
+// (x0, x4), (x1/16, x5/16), (x2, x6), (x3/16, x7/16). Adds the block's B values to bsum and the x
+// they stand for (16 times each x/16 half) to xsum, both in fp32.
+__device__ __forceinline__ uint4 permute_x_block(const uint4& v, float& bsum, float& xsum) {
+  uint32_t lo02, hi02, lo13, hi13;
+  asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(lo02) : "r"(v.x), "r"(v.z));  // (x0, x4)
+  asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(hi02) : "r"(v.x), "r"(v.z));  // (x1, x5)
+  asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(lo13) : "r"(v.y), "r"(v.w));  // (x2, x6)
+  asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(hi13) : "r"(v.y), "r"(v.w));  // (x3, x7)
+  const __half2 sixteenth = __float2half2_rn(0.0625f);
+  __half2 a, b;
+  memcpy(&a, &hi02, 4);
+  memcpy(&b, &hi13, 4);
+  a = __hmul2(a, sixteenth);
+  b = __hmul2(b, sixteenth);
+  uint4 o;
+  o.x = lo02;
+  memcpy(&o.y, &a, 4);
+  o.z = lo13;
+  memcpy(&o.w, &b, 4);
+  __half2 l0, l1;
+  memcpy(&l0, &lo02, 4);
+  memcpy(&l1, &lo13, 4);
+  const float2 f0 = __half22float2(l0), f1 = __half22float2(l1);
+  const float2 f2 = __half22float2(a), f3 = __half22float2(b);
+  const float ones = (f0.x + f0.y) + (f1.x + f1.y);
+  const float sixteenths = (f2.x + f2.y) + (f3.x + f3.y);
+  bsum += ones + sixteenths;
+  xsum += ones + 16.0f * sixteenths;
+  return o;
+}
+
 __device__ __forceinline__ float2 half2_bits_to_float2(uint32_t bits) {
   __half2 h;
   memcpy(&h, &bits, sizeof(h));
@@ -131,6 +168,43 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
   return true;
 }
+
+// Releasing a ring stage right after loading it. mbarrier.arrive does not wait for the warp's
+// shared-memory loads that are still in flight (measured on B200: with the weights in L2, a refill
+// landed before such loads had read the stage). So before the release every lane folds the
+// registers it loaded from the stage into one word (XOR) and stores it to a scratch word: that
+// store cannot issue before the loads have returned, and the arrive, issued after it in program
+// order, then hands back a stage that has been read. Call it from every lane, then __syncwarp(),
+// then one lane arrives. `scratch` is 32 words of otherwise unused shared memory.
+__device__ __forceinline__ uint32_t fold4(const uint4& v) { return v.x ^ v.y ^ v.z ^ v.w; }
+
+__device__ __forceinline__ void stage_reads_done(uint32_t folded, uint32_t* scratch, int lane) {
+  reinterpret_cast<volatile uint32_t*>(scratch)[lane] = folded;
+}
+
+// The consumers' side of a stage ring whose full barriers expect one arrival plus the bytes: slot
+// and phase kept incrementally (no division). next() waits (bounded) for the next stage and
+// returns its slot; after a timeout it records `status` once and stops waiting (ok = false).
+struct StageRingSx {
+  uint64_t* full;
+  int stages;
+  int* status;
+  bool ok;
+  int slot;
+  uint32_t phase;
+  __device__ __forceinline__ int next() {
+    const int s = slot;
+    if (ok && !mbar_wait_bounded(&full[s], phase)) {
+      ok = false;
+      atomicExch(status, kStatusFullBarrierTimeout);
+    }
+    if (++slot == stages) {
+      slot = 0;
+      phase ^= 1u;
+    }
+    return s;
+  }
+};
 
 // ---- words between ranks (peer memory over NVLink) -----------------------------------------------
 __device__ __forceinline__ unsigned long long global_ns() {

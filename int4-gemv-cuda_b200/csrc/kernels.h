@@ -16,7 +16,11 @@ namespace i4 {
 // gets this rank's fp32 partial sums, then each adds all ranks' partials in rank order).
 // kGroupedY: the rows of W are several matrices stacked (GroupOut below) and each matrix's
 // outputs go to its own y.
-enum Epilogue : int { kStoreY = 0, kSiluMul = 1, kGatherPeers = 2, kReducePeers = 3, kGroupedY = 4 };
+// kStoreF32: y [m, n] fp32, the row sums themselves (the partial sums of a K-split layer, added
+// across ranks before the one rounding to fp16).
+enum Epilogue : int {
+  kStoreY = 0, kSiluMul = 1, kGatherPeers = 2, kReducePeers = 3, kGroupedY = 4, kStoreF32 = 5
+};
 
 constexpr int kMaxPeers = 8;
 constexpr int kPeerCounters = 1024;  // counter words per rank (two used: call number, CTAs done)
@@ -117,6 +121,12 @@ cudaError_t launch_stream_mma(const GemvArgs& a, cudaStream_t stream, bool stric
                               void* workspace = nullptr, int64_t workspace_bytes = 0);
 int64_t stream_mma_workspace_bytes(const GemvArgs& a);
 cudaError_t stream_mma_attrs(int m, KernelAttrs* out);
+
+// Stripe-fed mma.sync GEMV for M <= 2, group 128, K % 2048 == 0 (stripe_mma.cu): 2-D TMA tiles of
+// 32 rows x 2048 weights, the whole ring issued before the dependency wait unless strict.
+bool stripe_mma_supported(const GemvArgs& a, const char** why);
+cudaError_t launch_stripe_mma(const GemvArgs& a, cudaStream_t stream, bool strict);
+cudaError_t stripe_mma_attrs(int m, KernelAttrs* out);
 
 // TMA-bulk-fed mma.sync pipeline (mma_pipeline.cu). `why` gets a reason when unsupported.
 bool mma_pipeline_supported(const GemvArgs& a, const char** why);

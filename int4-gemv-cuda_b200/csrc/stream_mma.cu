@@ -451,7 +451,7 @@ __host__ __device__ constexpr int narrow_acc() {  // accumulator chains per D se
 template <int MP, int NR>
 __device__ __forceinline__ void narrow_load(const NarrowThread<MP, NR>& t, const unsigned char* st,
                                             NarrowRegs<MP, NR>& r, uint64_t* empty_bar,
-                                            int lane) {
+                                            uint32_t* scratch, int lane) {
   if (MP == 4) {
 #pragma unroll
     for (int j = 0; j < NR; ++j)
@@ -471,6 +471,26 @@ __device__ __forceinline__ void narrow_load(const NarrowThread<MP, NR>& t, const
     r.sb[h].load(sp + row * kSzRowBytes, t.item0);
     if (t.q == 0) r.zb[h].load(zp + row * kSzRowBytes, t.item0);
   }
+  // release only once every load above has returned (see stage_reads_done)
+  constexpr int kSets = NarrowThread<MP, NR>::kSets;
+  constexpr int kWords = MP == 2 ? kSets : (kSets == 2 ? 1 : 2);  // SzBits words loaded
+  uint32_t folded = 0;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    if (MP == 4) {
+#pragma unroll
+      for (int j = 0; j < NR; ++j) folded ^= r.wb[j][h].x ^ r.wb[j][h].y;
+    } else {
+#pragma unroll
+      for (int i = 0; i < NR / 2; ++i) folded ^= fold4(r.wa[i][h]);
+    }
+#pragma unroll
+    for (int w = 0; w < kWords; ++w) {
+      folded ^= r.sb[h].w[w];
+      if (t.q == 0) folded ^= r.zb[h].w[w];
+    }
+  }
+  stage_reads_done(folded, scratch, lane);
   __syncwarp();
   if (lane == 0) mbar_arrive(empty_bar);  // the stage may be refilled
 }
@@ -585,16 +605,20 @@ __device__ __forceinline__ void wide_stage(const unsigned char* st, const unsign
                                            const float2* corr, int xs_stride, int mc, int m_rows,
                                            int j_panel, int item0, int g, int c, int r_lo,
                                            int r_hi, float (&acc)[2][MT][2], uint64_t* empty_bar,
-                                           int lane) {
+                                           uint32_t* scratch, int lane) {
   uint4 aw[NI][2];
   uint32_t sz[NI][2];  // scale bits | zero bits << 16 of item item0 + ii, rows r_lo and r_hi
+  uint32_t folded = 0;
 #pragma unroll
   for (int ii = 0; ii < NI; ++ii) {
     aw[ii][0] = stage_words(st, r_lo, item0 + ii, c);
     aw[ii][1] = stage_words(st, r_hi, item0 + ii, c);
     sz[ii][0] = stage_sz(st, r_lo, item0 + ii);
     sz[ii][1] = stage_sz(st, r_hi, item0 + ii);
+    folded ^= fold4(aw[ii][0]) ^ fold4(aw[ii][1]) ^ sz[ii][0] ^ sz[ii][1];
   }
+  // release only once every load above has returned (see stage_reads_done)
+  stage_reads_done(folded, scratch, lane);
   __syncwarp();
   if (lane == 0) mbar_arrive(empty_bar);  // the stage may be refilled
 
@@ -716,6 +740,7 @@ __global__ void __maxnreg__(CW == 16 ? 96 : 168)
   uint64_t* full = bars + kBarFull;
   uint64_t* empty = bars + kBarEmpty;
   unsigned char* zero = smem + 1024;
+  uint32_t* scratch = reinterpret_cast<uint32_t*>(smem + 512);  // see stage_reads_done
   const unsigned char* xr = smem + p.off_xr;
   unsigned char* xs = smem + p.off_xs;
   float2* corr = reinterpret_cast<float2*>(smem + p.off_corr);
@@ -800,20 +825,20 @@ __global__ void __maxnreg__(CW == 16 ? 96 : 168)
           using Acc = float[NarrowThread<MP, kNR>::kSets][narrow_acc<MP>()][4];
           Regs ra, rb;
           int slot = in.next();
-          narrow_load(nt, stages + slot * kStageBytes, ra, &empty[slot], lane);
+          narrow_load(nt, stages + slot * kStageBytes, ra, &empty[slot], scratch, lane);
           for (int j = 0; j < psteps; j += 2) {
             Acc d;
             narrow_mma(ra, xs + nt.b_base + j * nt.b_step, d);
             if (j + 1 < psteps) {
               slot = in.next();
-              narrow_load(nt, stages + slot * kStageBytes, rb, &empty[slot], lane);
+              narrow_load(nt, stages + slot * kStageBytes, rb, &empty[slot], scratch, lane);
             }
             narrow_epilogue(nt, ra, d, corr + j * kItemsPerStage * p.mc, p.mc, m_rows, acc);
             if (j + 1 >= psteps) break;
             narrow_mma(rb, xs + nt.b_base + (j + 1) * nt.b_step, d);
             if (j + 2 < psteps) {
               slot = in.next();
-              narrow_load(nt, stages + slot * kStageBytes, ra, &empty[slot], lane);
+              narrow_load(nt, stages + slot * kStageBytes, ra, &empty[slot], scratch, lane);
             }
             narrow_epilogue(nt, rb, d, corr + (j + 1) * kItemsPerStage * p.mc, p.mc, m_rows, acc);
           }
@@ -842,7 +867,8 @@ __global__ void __maxnreg__(CW == 16 ? 96 : 168)
             continue;
           }
           wide_stage<MT, kNI>(stages + slot * kStageBytes, xs, corr, p.xs_stride, p.mc, a.m, j,
-                              2 * group + hs, g, c, r_lo, r_hi, acc, &empty[slot], lane);
+                              2 * group + hs, g, c, r_lo, r_hi, acc, &empty[slot], scratch,
+                              lane);
         }
         if (active) {
 #pragma unroll
@@ -957,6 +983,14 @@ __global__ void __maxnreg__(CW == 16 ? 96 : 168)
       if (in.ok) a.y[at] = store_value(a, m, row_begin + r, total);
     }
     exchange_done(peers, epoch, tid);
+  } else if (a.epilogue == kStoreF32) {
+    float* yf = reinterpret_cast<float*>(a.y);
+    for (int o = tid; o < rows * a.m; o += kConsumerThreads) {
+      const int m = o / rows;
+      const int r = o - m * rows;
+      const float sum = row_sum(r, m);
+      if (in.ok) yf[static_cast<int64_t>(m) * a.n + row_begin + r] = sum;
+    }
   } else {
     for (int o = tid; o < rows * a.m; o += kConsumerThreads) {
       const int m = o / rows;

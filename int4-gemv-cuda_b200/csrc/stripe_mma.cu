@@ -1,0 +1,686 @@
+// The B200 fast path for M <= 2: stripes of 32 rows x 2048 weights streamed by TMA into a ring of
+// shared-memory stages, and warp-level tensor-core MMAs (mma.sync m16n8k16, f16 x f16 -> f32) on
+// the nibbles unpacked in registers.
+//
+// Memory side. One CTA per SM; CTA c owns rows [4 u0, 4 u1), an equal share of 4-row units. Its
+// rows are taken in blocks of up to 32, each block in stripes of 2048 weights along K. A stripe is
+// one 2-D TMA tile of the packed weights (32 rows x 1 KB, no swizzle) plus two tiles of its scales
+// and zeros (32 rows x 16 groups), 34 KB in all; blocks of fewer rows use boxes of 16 / 8 / 4 rows,
+// so a CTA never fetches a row it does not own. On B200 these 1 KB-wide tiles stream a W4A16
+// matrix about 20 % faster than 128-byte-wide ones (measured). The ring takes nearly all of shared
+// memory (five stripes at K = 8192, three quarters of a CTA's bytes), and unless the caller asks
+// for strict ordering the producer warp issues the whole ring before griddepcontrol.wait: while
+// the previous kernel in the stream finishes, the weights of this call are already on their way,
+// so HBM does not idle between back-to-back calls.
+//
+// x. Right after the dependency wait every consumer thread loads its share of x with 16-byte loads
+// (one round trip), permutes each 8-weight block to the order of the unpacked A halves,
+// [x0, x4, x1/16, x5/16, x2, x6, x3/16, x7/16], and stores it with per-item (128-weight) padding so
+// the B loads of different items hit different banks. The same pass builds two small tables:
+// bq[item][granule][m] = the sum of the B values of each 4-word granule, and xs[item][m] = the sum
+// of the item's x.
+//
+// Math side. Sixteen consumer warps. Warp w takes items 4 (w % 4) .. + 3 of every stripe and one
+// word granule (4 words) of each; lane (g, c) takes item 4 (w % 4) + c ("narrow" layout: the eight
+// MMA columns are four items x two rows of x, and lane c's k-slots hold its own item's words, so
+// one MMA covers 256 weights of four different groups), granule (w / 4 + c / 2) % 4 (rotated so
+// the 16-byte loads of one shared-memory phase hit distinct banks), and rows g, g + 8, 16 + g,
+// 24 + g of the block. Per packed word one shift and four LOP3s give the fp16 A halves 1024 + q
+// and 1024 + 16 q exactly; the B registers of a word are reused for both 16-row tiles. Each tile's
+// low-half MMA chain starts from C = -1024 * (sum of the B values of the granule), which removes
+// the magic-number offset inside the tensor core, so after the stripe the accumulators hold
+// sum_k q_k x_k per (row, item) and the stripe epilogue is one scale multiply-add per row:
+//     sum_k (q_k - z) s x_k = s * (sum_k q_k x_k - z * sum_k x_k),
+// the z term added by the granule-0 warps only. The weights are bit-exact; the arithmetic is
+// fp32 accumulation of exact fp16 products.
+//
+// Results. After a block the four item lanes of each row are added with two shuffles and each
+// warp writes one partial per (row, m) to shared memory; after the last block the sixteen
+// partials of every output are added in a fixed order, so results are deterministic. Every
+// mbarrier wait is bounded; on timeout the kernel records a status word and runs to completion
+// without writing y.
+#include <algorithm>
+#include <mutex>
+#include <vector>
+
+#include "weight_stream.cuh"
+
+namespace i4 {
+namespace {
+
+constexpr int kSxRows = 32;                            // rows per block (tallest box)
+constexpr int kSxK = 2048;                             // weights per stripe along K
+constexpr int kSxItems = kSxK / kItemK;                // 16 groups per stripe
+constexpr int kSxRowBytes = kSxK / 2;                  // 1024 packed bytes per row and stripe
+constexpr int kSxQBytes = kSxRows * kSxRowBytes;       // 32 KB
+constexpr int kSxMetaRow = kSxItems * 2;               // 32 bytes of scales (or zeros) per row
+constexpr int kSxSOff = kSxQBytes;
+constexpr int kSxZOff = kSxQBytes + kSxRows * kSxMetaRow;
+constexpr int kSxStageBytes = kSxQBytes + 2 * kSxRows * kSxMetaRow;  // 34816
+constexpr int kSxTxPerRow = kSxRowBytes + 2 * kSxMetaRow;           // 1088 bytes land per row
+constexpr int kSxItemBytes = 272;   // one item of permuted x for one row of x (256 + 16 pad)
+constexpr int kSxMaxStages = 8;
+constexpr int kSxMaxConsumers = 16 * kWarp;  // the most consumer threads of any instance
+constexpr int kSxSmemLimit = 227 * 1024;
+constexpr int kSxMinStages = 3;
+constexpr int kSxBarrier = 1;       // named barrier of the consumer warps
+constexpr int kSxZeroOff = 1024;    // 512 zero bytes: the B source of lanes without x
+constexpr int kSxHeader = 1536;     // mbarriers + zero block
+
+// qweight as [N][K / 8] 32-bit words (boxes of 256 words = one stripe row); scales and zeros as
+// [N][K / 128] halves (boxes of 16 groups); each with boxes of 32, 16, 8 and 4 rows.
+struct StripeMaps {
+  CUtensorMap q[4];
+  CUtensorMap s[4];
+  CUtensorMap z[4];
+};
+
+struct StripePlan {
+  int ctas;
+  int units;       // 4-row units in N
+  int rows_cap;    // rows of the largest CTA share
+  int stripes;     // K / 2048
+  int items;       // K / 128
+  int xs_stride;   // bytes of permuted x per row of x
+  int stages;
+  int off_xs, off_bq, off_xsum, off_red, off_stage, smem_bytes;
+  int strict;      // 1: read the weights only after griddepcontrol.wait
+  int* status;
+};
+
+// The box this lane issues for a block of rows4 rows (a multiple of 4, at most 32): boxes are the
+// binary decomposition of rows4 into 32 / 16 / 8 / 4 rows, largest first; lane 3 b + t issues box
+// b of tensor t (0 weights, 1 scales, 2 zeros). Returns false if the lane has no box.
+struct StripeBox {
+  const CUtensorMap* map;
+  int dst;    // byte offset in the stage
+  int row;    // first row (global)
+  int kind;   // 0 weights, 1 scales, 2 zeros
+};
+
+__device__ __forceinline__ bool stripe_box(const StripeMaps& maps, int lane, int rows4, int row0,
+                                           StripeBox* b) {
+  const int box = lane / 3, kind = lane % 3;
+  int n = 0, off = 0;
+  for (int hi = 0; hi < 4; ++hi) {
+    const int h = kSxRows >> hi;
+    if (rows4 & h) {
+      if (n == box && lane < 12) {
+        b->kind = kind;
+        b->row = row0 + off;
+        b->map = kind == 0 ? &maps.q[hi] : kind == 1 ? &maps.s[hi] : &maps.z[hi];
+        b->dst = kind == 0 ? off * kSxRowBytes : (kind == 1 ? kSxSOff : kSxZOff) + off * kSxMetaRow;
+        return true;
+      }
+      ++n;
+      off += h;
+    }
+  }
+  return false;
+}
+
+__device__ __forceinline__ void issue_stripe(const StripeBox& b, bool has_box, int stripe,
+                                             int rows4, unsigned char* stage, uint64_t* full_bar,
+                                             uint64_t policy, int lane) {
+  if (lane == 0) mbar_arrive_expect_tx(full_bar, static_cast<uint32_t>(rows4 * kSxTxPerRow));
+  __syncwarp();
+  if (has_box) {
+    // x coordinate in elements: 256 words per stripe for the weights, 16 groups for scales/zeros
+    const int x = b.kind == 0 ? stripe * (kSxRowBytes / 4) : stripe * kSxItems;
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_addr(stage + b.dst)),
+        "l"(b.map), "r"(x), "r"(b.row), "r"(smem_addr(full_bar)), "l"(policy)
+        : "memory");
+  }
+}
+
+// The producer warp: the CTA's blocks x stripes through the ring. Unless strict, the first
+// min(stages, total) stripes go out before griddepcontrol.wait. empty[s] expects one arrival per
+// consumer warp.
+__device__ __forceinline__ void stripe_produce(const StripePlan& p, const StripeMaps& maps,
+                                               int row_begin, int rows, unsigned char* smem) {
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + kSxMaxStages;
+  unsigned char* stages = smem + p.off_stage;
+  const int lane = threadIdx.x % kWarp;
+  const uint64_t policy = l2_evict_first_policy();
+  const int blocks = (rows + kSxRows - 1) / kSxRows;
+  const int total = blocks * p.stripes;
+  const int pre = p.strict ? 0 : min(p.stages, total);
+  if (pre == 0) grid_dependency_wait();
+  bool ok = true;
+  int it = 0, slot = 0, use = 0;
+  for (int blk = 0; blk < blocks; ++blk) {
+    const int rows4 = (min(kSxRows, rows - blk * kSxRows) + 3) & ~3;
+    StripeBox b;
+    const bool has_box = stripe_box(maps, lane, rows4, row_begin + blk * kSxRows, &b);
+    for (int j = 0; j < p.stripes; ++j, ++it) {
+      if (it == pre && pre > 0) grid_dependency_wait();
+      if (ok && use > 0 && !mbar_wait_bounded(&empty[slot], (use - 1) & 1)) {
+        ok = false;
+        if (lane == 0) atomicExch(p.status, kStatusEmptyBarrierTimeout);
+      }
+      if (ok) issue_stripe(b, has_box, j, rows4, stages + slot * kSxStageBytes, &full[slot],
+                           policy, lane);
+      if (++slot == p.stages) {
+        slot = 0;
+        ++use;
+      }
+    }
+  }
+  if (pre == total) grid_dependency_wait();  // every stripe fit in the ring
+  // Do not leave while copies into this CTA's shared memory may be in flight.
+  if (ok) {
+    for (int back = 1; back <= min(it, p.stages); ++back) {
+      const int j = it - back;
+      if (!mbar_wait_bounded(&full[j % p.stages], (j / p.stages) & 1)) break;
+    }
+  }
+}
+
+// x -> the permuted B layout and the two tables (see the file comment). Thread t handles blocks
+// (8 weights of one row of x) 2 t and 2 t + 1 of each 2 x NT-block step; a thread pair
+// covers one 4-word granule, eight threads one item.
+template <int NT>
+__device__ __forceinline__ void stripe_prepare_x(const GemvArgs& a, const StripePlan& p,
+                                                 unsigned char* smem, int tid) {
+  const int kw_per_m = a.k / 8;
+  const int total = a.m * kw_per_m;
+  unsigned char* xs = smem + p.off_xs;
+  float* bq = reinterpret_cast<float*>(smem + p.off_bq);    // [items][4][2]
+  float* xsum = reinterpret_cast<float*>(smem + p.off_xsum);  // [items][2]
+  for (int base = 0; base < total; base += 4 * NT) {
+    // Two steps per round: all four 16-byte loads are in flight together.
+    uint4 v[4];
+    int idx[2];
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      idx[s] = base + s * 2 * NT + 2 * tid;
+      if (idx[s] < total) {
+        const int m = idx[s] / kw_per_m, kw = idx[s] - m * kw_per_m;
+        const uint4* src = reinterpret_cast<const uint4*>(a.x + static_cast<int64_t>(m) * a.k) + kw;
+        v[2 * s] = ld_stream_v4(src);
+        v[2 * s + 1] = ld_stream_v4(src + 1);
+      }
+    }
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      if (base + s * 2 * NT >= total) break;  // uniform over the CTA
+      const bool valid = idx[s] < total;
+      float bsum = 0.0f, xsm = 0.0f;
+      int m = 0, kw = 0;
+      if (valid) {
+        m = idx[s] / kw_per_m;
+        kw = idx[s] - m * kw_per_m;
+        const uint4 o0 = permute_x_block(v[2 * s], bsum, xsm);
+        const uint4 o1 = permute_x_block(v[2 * s + 1], bsum, xsm);
+        unsigned char* row = xs + m * p.xs_stride + (kw >> 4) * kSxItemBytes + (kw & 15) * 16;
+        reinterpret_cast<uint4*>(row)[0] = o0;
+        reinterpret_cast<uint4*>(row)[1] = o1;
+      }
+      bsum += __shfl_xor_sync(0xffffffffu, bsum, 1);  // the granule (4 words) of a thread pair
+      xsm += __shfl_xor_sync(0xffffffffu, xsm, 1);
+      xsm += __shfl_xor_sync(0xffffffffu, xsm, 2);
+      xsm += __shfl_xor_sync(0xffffffffu, xsm, 4);  // the item (16 words) of eight threads
+      if (valid) {
+        const int item = kw >> 4, gran = (kw >> 2) & 3;
+        if ((tid & 1) == 0) {
+          bq[(item * 4 + gran) * 2 + m] = -1024.0f * bsum;
+          if (a.m == 1) bq[(item * 4 + gran) * 2 + 1] = 0.0f;
+        }
+        if ((tid & 7) == 0) {
+          xsum[item * 2 + m] = xsm;
+          if (a.m == 1) xsum[item * 2 + 1] = 0.0f;
+        }
+      }
+    }
+  }
+}
+
+// One stage's operands of a consumer lane: the A words of its GPW granules in rows g, g + 8
+// (tile 0) and 16 + g, 24 + g (tile 1), and those rows' scale (and zero) bits of its item.
+template <int GPW>
+struct StripeRegs {
+  uint4 aw[GPW][2][2];  // [granule][tile][row g / g + 8]
+  uint32_t sb[2][2], zb[2][2];
+};
+
+// The lane's B registers of one stripe (four words of x per granule in the permuted order), the C
+// value that starts its first low-half MMA chain per tile (-1024 x the B sum of its granules, per
+// row of x) and the item's x sum.
+template <int GPW>
+struct StripeX {
+  uint4 bx[GPW][4];
+  float2 cinit, xsm;
+};
+
+template <int GPW>
+__device__ __forceinline__ void stripe_load(const unsigned char* st, const int (&a_off)[GPW],
+                                            int s_off, int z_off, bool zero_term, bool two_tiles,
+                                            StripeRegs<GPW>& r) {
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    if (t == 1 && !two_tiles) break;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int row = 16 * t + 8 * h;
+#pragma unroll
+      for (int q = 0; q < GPW; ++q) {
+        r.aw[q][t][h] = *reinterpret_cast<const uint4*>(st + a_off[q] + row * kSxRowBytes);
+      }
+      r.sb[t][h] = *reinterpret_cast<const uint16_t*>(st + s_off + row * kSxMetaRow);
+      if (zero_term) r.zb[t][h] = *reinterpret_cast<const uint16_t*>(st + z_off + row * kSxMetaRow);
+    }
+  }
+}
+
+template <int GPW>
+__device__ __forceinline__ void stripe_load_x(const unsigned char* const (&b_base)[GPW], int b_step,
+                                              const float* bq, const float* xsum, int j, int item,
+                                              const int (&gran)[GPW], bool zero_term,
+                                              StripeX<GPW>& x) {
+  const int tab = j * kSxItems + item;
+  float2 ci = make_float2(0.0f, 0.0f);
+#pragma unroll
+  for (int q = 0; q < GPW; ++q) {
+    const unsigned char* bsrc = b_base[q] + j * b_step;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) x.bx[q][u] = *reinterpret_cast<const uint4*>(bsrc + u * 16);
+    const float2 v = *reinterpret_cast<const float2*>(bq + (tab * 4 + gran[q]) * 2);
+    ci.x += v.x;
+    ci.y += v.y;
+  }
+  x.cinit = ci;
+  x.xsm = zero_term ? *reinterpret_cast<const float2*>(xsum + tab * 2) : make_float2(0.0f, 0.0f);
+}
+
+// The stage's 16 GPW MMAs: per tile and granule a low-half and a high-half chain over the
+// granule's four words (the first low-half chain started from C = cinit, the others from zero),
+// added at the end: d[t] = sum_k q_k x_k for the lane's (rows, item) as the MMA D fragment (rows
+// g, g + 8 x columns 2c, 2c + 1).
+template <int GPW>
+__device__ __forceinline__ void stripe_mma(const StripeRegs<GPW>& r, const StripeX<GPW>& x,
+                                           bool two_tiles, float (&d)[2][4]) {
+  float ch[2][2 * GPW - 1][4];  // the chains other than the first low-half one
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    d[t][0] = d[t][2] = x.cinit.x;
+    d[t][1] = d[t][3] = x.cinit.y;
+  }
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+#pragma unroll
+    for (int q = 0; q < GPW; ++q) {
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        if (t == 1 && !two_tiles) break;
+        uint32_t hg[4], h8[4];
+        unpack_x16(word_of4(r.aw[q][t][0], u), hg);
+        unpack_x16(word_of4(r.aw[q][t][1], u), h8);
+        const uint32_t alo[4] = {hg[0], h8[0], hg[1], h8[1]};
+        const uint32_t ahi[4] = {hg[2], h8[2], hg[3], h8[3]};
+        if (q == 0) {
+          mma_16816(d[t], alo, x.bx[q][u].x, x.bx[q][u].y);
+        } else if (u == 0) {
+          mma_16816_first(ch[t][2 * q - 1], alo, x.bx[q][u].x, x.bx[q][u].y);
+        } else {
+          mma_16816(ch[t][2 * q - 1], alo, x.bx[q][u].x, x.bx[q][u].y);
+        }
+        if (u == 0) {
+          mma_16816_first(ch[t][2 * q], ahi, x.bx[q][u].z, x.bx[q][u].w);
+        } else {
+          mma_16816(ch[t][2 * q], ahi, x.bx[q][u].z, x.bx[q][u].w);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    if (t == 1 && !two_tiles) break;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+#pragma unroll
+      for (int i = 0; i < 2 * GPW - 1; ++i) d[t][e] += ch[t][i][e];
+    }
+  }
+}
+
+// One scale per (row, item) into the row accumulators; the granule-0 warps add the zero term.
+template <int MC, int GPW>
+__device__ __forceinline__ void stripe_epilogue(const StripeRegs<GPW>& r, const float (&d)[2][4],
+                                                float2 xsm, bool zero_term, bool two_tiles,
+                                                float (&acc)[2][2][MC]) {
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    if (t == 1 && !two_tiles) break;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float s = __half2float(__ushort_as_half(static_cast<uint16_t>(r.sb[t][h])));
+      const float z =
+          zero_term ? __half2float(__ushort_as_half(static_cast<uint16_t>(r.zb[t][h]))) : 0.0f;
+#pragma unroll
+      for (int m = 0; m < MC; ++m) {
+        const float xz = m == 0 ? xsm.x : xsm.y;
+        acc[t][h][m] = fmaf(s, fmaf(-z, xz, d[t][2 * h + m]), acc[t][h][m]);
+      }
+    }
+  }
+}
+
+// MC: rows of x (1 or 2). CW: consumer warps, 16 (one 4-word granule per lane and stage) or 8
+// (two); plus one producer warp.
+template <int MC, int CW>
+__global__ void __launch_bounds__((CW + 1) * kWarp, 1)
+    stripe_mma_kernel(GemvArgs a, StripePlan p, const __grid_constant__ StripeMaps maps) {
+  constexpr int kGPW = 16 / CW;            // granules per lane and stage
+  constexpr int kConsumers = CW * kWarp;
+  extern __shared__ __align__(1024) unsigned char smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + kSxMaxStages;
+  unsigned char* stages = smem + p.off_stage;
+  float* red = reinterpret_cast<float*>(smem + p.off_red);  // [CW warps][rows_cap][MC]
+
+  const int tid = threadIdx.x;
+  const int warp = tid / kWarp;
+  const int lane = tid % kWarp;
+
+  const int u0 = static_cast<int>(static_cast<int64_t>(blockIdx.x) * p.units / p.ctas);
+  const int u1 = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * p.units / p.ctas);
+  const int row_begin = 4 * u0;
+  const int rows = min(4 * u1, a.n) - row_begin;
+  const int blocks = (rows + kSxRows - 1) / kSxRows;
+
+  if (tid == kConsumers) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], CW);
+    }
+    fence_mbar_init();
+  }
+  for (int i = tid; i < 512 / 16; i += (CW + 1) * kWarp) {
+    reinterpret_cast<uint4*>(smem + kSxZeroOff)[i] = make_uint4(0, 0, 0, 0);
+  }
+  __syncthreads();
+  if (tid == 0) launch_dependents();  // the next GEMV may launch as SMs free up
+
+  if (warp == CW) {
+    stripe_produce(p, maps, row_begin, rows, smem);
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  grid_dependency_wait();  // x may come from the previous kernel in the stream
+  stripe_prepare_x<kConsumers>(a, p, smem, tid);
+  named_barrier(kSxBarrier, kConsumers);
+
+  const int g = lane >> 2, c = lane & 3;
+  const int iq = warp & 3, wq = warp >> 2;     // item quad; granule set (kGPW granules each)
+  const int item = 4 * iq + c;                 // item of this lane within a stripe
+  const bool zero_term = wq == 0;              // these warps add the zero term of their items
+  const int xm = g - 2 * c;                    // the row of x whose B values this lane holds
+  const bool has_x = xm >= 0 && xm < MC;
+  const unsigned char* xs = smem + p.off_xs;
+  const float* bq = reinterpret_cast<const float*>(smem + p.off_bq);
+  const float* xsum = reinterpret_cast<const float*>(smem + p.off_xsum);
+  int gran[kGPW], a_off[kGPW];
+  const unsigned char* b_base[kGPW];
+#pragma unroll
+  for (int q = 0; q < kGPW; ++q) {
+    // granules rotated by c / 2 so the 16-byte loads of one shared-memory phase hit distinct banks
+    gran[q] = (kGPW * wq + q + (c >> 1)) & 3;
+    a_off[q] = g * kSxRowBytes + item * 64 + gran[q] * 16;
+    b_base[q] = has_x ? xs + xm * p.xs_stride + item * kSxItemBytes + gran[q] * 64
+                      : smem + kSxZeroOff;
+  }
+  const int b_step = has_x ? kSxItems * kSxItemBytes : 0;
+  const int s_off = kSxSOff + g * kSxMetaRow + item * 2;
+  const int z_off = kSxZOff + g * kSxMetaRow + item * 2;
+
+  // Per stage: wait for it, load the lane's weights, scales and x, issue the MMAs, run the stage
+  // epilogue, release the stage. (Loading the next stage's operands during this stage's MMAs was
+  // measured slower on B200.)
+  StageRingSx ring{full, p.stages, p.status, true, 0, 0u};
+  for (int blk = 0; blk < blocks; ++blk) {
+    const int rows_b = min(kSxRows, rows - blk * kSxRows);
+    const bool two_tiles = rows_b > 16;  // uniform over the CTA
+    float acc[2][2][MC];                 // [tile][row g / g + 8][m]
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int m = 0; m < MC; ++m) acc[t][h][m] = 0.0f;
+    for (int j = 0; j < p.stripes; ++j) {
+      const int slot = ring.next();
+      StripeRegs<kGPW> r;
+      stripe_load<kGPW>(stages + slot * kSxStageBytes, a_off, s_off, z_off, zero_term,
+                        two_tiles, r);
+      StripeX<kGPW> xr;
+      stripe_load_x<kGPW>(b_base, b_step, bq, xsum, j, item, gran, zero_term, xr);
+      float d[2][4];
+      stripe_mma<kGPW>(r, xr, two_tiles, d);
+      stripe_epilogue<MC, kGPW>(r, d, xr.xsm, zero_term, two_tiles, acc);
+      // Release the stage only after its values have been used: mbarrier.arrive does not wait
+      // for shared-memory loads still in flight, and a refill served from L2 can land within a
+      // few hundred nanoseconds. (Releasing here measured as fast as releasing right after the
+      // loads.)
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);  // the stage may be refilled
+    }
+    // the four items of this warp's quad, then one partial per (row, m) and warp
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int m = 0; m < MC; ++m) {
+          float v = acc[t][h][m];
+          v += __shfl_xor_sync(0xffffffffu, v, 1);
+          v += __shfl_xor_sync(0xffffffffu, v, 2);
+          if (c == 0 && 16 * t + 8 * h + g < rows_b) {
+            red[(warp * p.rows_cap + blk * kSxRows + 16 * t + 8 * h + g) * MC + m] = v;
+          }
+        }
+  }
+
+  // ---- add the CW partials of every output in a fixed order; store fp16 ---------------------
+  named_barrier(kSxBarrier, kConsumers);
+  for (int o = tid; o < rows * MC; o += kConsumers) {
+    const int m = o / rows;
+    const int r = o - m * rows;
+    float sum = 0.0f;
+#pragma unroll
+    for (int w = 0; w < CW; ++w) sum += red[(w * p.rows_cap + r) * MC + m];
+    if (ring.ok) {
+      a.y[static_cast<int64_t>(m) * a.n + row_begin + r] = store_value(a, m, row_begin + r, sum);
+    }
+  }
+}
+
+// ---- host ---------------------------------------------------------------------------------------
+
+bool stripe_plan(const GemvArgs& a, StripePlan* p, const char** why) {
+  auto fail = [&](const char* reason) {
+    if (why) *why = reason;
+    return false;
+  };
+  if (a.m < 1 || a.m > 2) return fail("M must be 1 or 2");
+  if (a.group != kItemK) return fail("group_size must be 128");
+  if (a.k % kSxK != 0) return fail("K must be a multiple of 2048");
+  if (a.epilogue != kStoreY) return fail("plain stores only");
+  if (reinterpret_cast<uintptr_t>(a.q) % 16 || reinterpret_cast<uintptr_t>(a.s) % 16 ||
+      reinterpret_cast<uintptr_t>(a.z) % 16 || reinterpret_cast<uintptr_t>(a.x) % 16) {
+    return fail("x, qweight, scales and zeros must be 16-byte aligned");
+  }
+  p->units = (a.n + 3) / 4;
+  p->ctas = std::min(sm_count(), p->units);
+  p->rows_cap = 4 * ((p->units + p->ctas - 1) / p->ctas);
+  p->stripes = a.k / kSxK;
+  p->items = a.k / kItemK;
+  p->xs_stride = p->items * kSxItemBytes;
+  int64_t off = kSxHeader;
+  p->off_xs = static_cast<int>(off);
+  off += static_cast<int64_t>(a.m) * p->xs_stride;
+  p->off_bq = static_cast<int>(off);
+  off += static_cast<int64_t>(p->items) * 4 * 2 * 4;
+  p->off_xsum = static_cast<int>(off);
+  off += static_cast<int64_t>(p->items) * 2 * 4;
+  p->off_red = static_cast<int>(off);
+  off += static_cast<int64_t>(16) * p->rows_cap * a.m * 4;  // partials of up to 16 warps
+  off = (off + 1023) / 1024 * 1024;
+  p->off_stage = static_cast<int>(off);
+  if (off >= kSxSmemLimit) return fail("x does not fit in shared memory");
+  const int64_t stages =
+      std::min<int64_t>((kSxSmemLimit - off) / kSxStageBytes, kSxMaxStages);
+  if (stages < kSxMinStages) return fail("x does not fit in shared memory");
+  p->stages = static_cast<int>(stages);
+  p->smem_bytes = static_cast<int>(off + stages * kSxStageBytes);
+  p->strict = 0;
+  p->status = nullptr;
+  return true;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 stripe_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      f = nullptr;
+    }
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }();
+  return fn;
+}
+
+struct StripeMapEntry {
+  int dev;
+  const void* q;
+  const void* s;
+  const void* z;
+  int n, k;
+  StripeMaps maps;
+};
+std::mutex g_stripe_mu;
+std::vector<StripeMapEntry> g_stripe_maps;  // most recently used first
+constexpr size_t kStripeMapCache = 64;
+
+cudaError_t stripe_maps_for(const GemvArgs& a, StripeMaps* out) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  std::lock_guard<std::mutex> lock(g_stripe_mu);
+  for (size_t i = 0; i < g_stripe_maps.size(); ++i) {
+    const StripeMapEntry& e = g_stripe_maps[i];
+    if (e.dev == dev && e.q == a.q && e.s == a.s && e.z == a.z && e.n == a.n && e.k == a.k) {
+      *out = e.maps;
+      if (i != 0) std::swap(g_stripe_maps[i], g_stripe_maps[0]);
+      return cudaSuccess;
+    }
+  }
+  auto encode = stripe_encode_fn();
+  if (!encode) return cudaErrorNotSupported;
+  StripeMapEntry e{dev, a.q, a.s, a.z, a.n, a.k, {}};
+  const cuuint32_t estr[2] = {1, 1};
+  const int groups = a.k / a.group;
+  for (int hi = 0; hi < 4; ++hi) {
+    const cuuint32_t h = static_cast<cuuint32_t>(kSxRows >> hi);
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(a.k / 8), static_cast<cuuint64_t>(a.n)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a.k / 2)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kSxRowBytes / 4), h};
+    if (encode(&e.maps.q[hi], CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t*>(a.q), dims,
+               strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+      return cudaErrorInvalidValue;
+    }
+    const cuuint64_t sdims[2] = {static_cast<cuuint64_t>(groups), static_cast<cuuint64_t>(a.n)};
+    const cuuint64_t sstrides[1] = {static_cast<cuuint64_t>(groups) * 2};
+    const cuuint32_t sbox[2] = {static_cast<cuuint32_t>(kSxItems), h};
+    for (int which = 0; which < 2; ++which) {
+      if (encode(which == 0 ? &e.maps.s[hi] : &e.maps.z[hi], CU_TENSOR_MAP_DATA_TYPE_UINT16, 2,
+                 const_cast<half*>(which == 0 ? a.s : a.z), sdims, sstrides, sbox, estr,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                 CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+        return cudaErrorInvalidValue;
+      }
+    }
+  }
+  g_stripe_maps.insert(g_stripe_maps.begin(), e);
+  if (g_stripe_maps.size() > kStripeMapCache) g_stripe_maps.pop_back();
+  *out = e.maps;
+  return cudaSuccess;
+}
+
+#ifndef STRIPE_CW
+#define STRIPE_CW 16
+#endif
+// Kernel instances (rows of x, consumer warps).
+template <typename F>
+cudaError_t with_stripe_m(int m, F&& f) {
+  if (m <= 1) return f.template operator()<1, STRIPE_CW>();
+  return f.template operator()<2, STRIPE_CW>();
+}
+
+std::once_flag g_stripe_attr_once[2][64];
+
+}  // namespace
+
+bool stripe_mma_supported(const GemvArgs& a, const char** why) {
+  StripePlan p;
+  return stripe_plan(a, &p, why);
+}
+
+cudaError_t launch_stripe_mma(const GemvArgs& a, cudaStream_t stream, bool strict) {
+  StripePlan p;
+  if (!stripe_plan(a, &p, nullptr)) return cudaErrorInvalidValue;
+  p.strict = strict ? 1 : 0;
+  p.status = device_status_word();
+  if (!p.status) return cudaErrorInvalidSymbol;
+  StripeMaps maps;
+  const cudaError_t merr = stripe_maps_for(a, &maps);
+  if (merr != cudaSuccess) return merr;
+  int dev = 0;
+  const cudaError_t derr = cudaGetDevice(&dev);
+  if (derr != cudaSuccess) return derr;
+  return with_stripe_m(a.m, [&]<int MC, int CW>() {
+    cudaError_t result = cudaSuccess;
+    std::call_once(g_stripe_attr_once[MC - 1][dev & 63], [&] {
+      result = cudaFuncSetAttribute(stripe_mma_kernel<MC, CW>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kSxSmemLimit);
+    });
+    if (result != cudaSuccess) return result;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.ctas);
+    cfg.blockDim = dim3((CW + 1) * kWarp);
+    cfg.dynamicSmemBytes = p.smem_bytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, stripe_mma_kernel<MC, CW>, a, p, maps);
+  });
+}
+
+cudaError_t stripe_mma_attrs(int m, KernelAttrs* out) {
+  const int mm = m < 1 ? 1 : m > 2 ? 2 : m;
+  return with_stripe_m(mm, [&]<int MC, int CW>() {
+    cudaFuncAttributes fa;
+    cudaError_t err = cudaFuncGetAttributes(&fa, stripe_mma_kernel<MC, CW>);
+    if (err != cudaSuccess) return err;
+    out->registers = fa.numRegs;
+    out->local_bytes = static_cast<int>(fa.localSizeBytes);
+    out->max_threads_per_block = fa.maxThreadsPerBlock;
+    out->blocks_per_sm = 1;
+    out->threads_per_block = (CW + 1) * kWarp;
+    return cudaSuccess;
+  });
+}
+
+}  // namespace i4

@@ -61,6 +61,7 @@ constexpr int kBarEmpty = kMaxStages;          // [kMaxStages] stage consumed (4
 constexpr int kBarMma = 2 * kMaxStages;        // [2] MMAs of buffer b done (commit)
 constexpr int kBarA = 2 * kMaxStages + 2;      // [2] A operand of buffer b written (128 lanes)
 constexpr int kTmemSlot = 8 * (2 * kMaxStages + 4);
+constexpr int kScratchOff = 512;  // 32 words, see stage_reads_done
 
 struct TcPlan {
   int ctas;
@@ -358,6 +359,15 @@ __global__ void __launch_bounds__(kThreads, 2)
           szw[t] = static_cast<uint32_t>(ss[4 * t + quarter]) |
                    (static_cast<uint32_t>(zz[4 * t + quarter]) << 16);
         }
+      }
+      {
+        // release only once every load above has returned (see stage_reads_done)
+        uint32_t folded = szw[0] ^ szw[1];
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+          for (int w = 0; w < 16; ++w) folded ^= qw[t][w];
+        stage_reads_done(folded, reinterpret_cast<uint32_t*>(smem + kScratchOff), lane);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[kBarEmpty + slot]);  // stage may be refilled

@@ -34,6 +34,7 @@ _PROTOTYPES = {
     "int4gemv_w4a16_kernel_name": (ctypes.c_char_p, [_p] * 4 + [_i64] * 4),
     "int4gemv_w4a16_kernel": (ctypes.c_int, [ctypes.c_char_p] + [_p] * 5 + [_i64] * 4 + [_p]),
     "int4gemv_w4a16_silu_mul": (ctypes.c_int, [_p] * 5 + [_i64] * 4 + [_p]),
+    "int4gemv_w4a16_f32": (ctypes.c_int, [_p] * 5 + [_i64] * 4 + [_p]),
     "int4gemv_unpack": (ctypes.c_int, [_p, _p, _i64, _i64, _p]),
     "int4gemv_dequantize": (ctypes.c_int, [_p] * 4 + [_i64] * 3 + [_p]),
     "int4gemv_w4a16_grouped": (ctypes.c_int, [ctypes.c_int, _p, _p] + [_p] * 4 + [_i64] * 3
@@ -44,6 +45,7 @@ _PROTOTYPES = {
     "int4gemv_quantize": (ctypes.c_int, [_p] * 4 + [ctypes.c_int] + [_i64] * 3 + [_p]),
     "int4gemv_pack": (ctypes.c_int, [_p, _p, _i64, _i64, _p]),
     "int4gemv_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
+    "int4gemv_set_strict_weights": (ctypes.c_int, [ctypes.c_int]),
     "int4gemv_peers_struct_bytes": (ctypes.c_size_t, []),
     "int4gemv_peer_alloc": (ctypes.c_int, [_i64, ctypes.POINTER(_p), _p]),
     "int4gemv_peer_open": (ctypes.c_int, [_p, ctypes.POINTER(_p)]),

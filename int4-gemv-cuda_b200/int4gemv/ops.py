@@ -3,7 +3,8 @@
 Drop-in for the reference's int4gemv.ops (int4gemv/ops.py:11-36 of Yu-TingLee/int4-GEMV-cuda):
 the same names (sequential, naive, coalesced, vectorized, load_only), the same KERNELS and
 KERNEL_INFO tables, plus the B200 fast path `w4a16`, the fused epilogues `w4a16_silu_mul` and
-`w4a16_bias_residual`, and the bit-exact device `quantize` / `pack` / `unpack` / `dequantize`. As
+`w4a16_bias_residual`, the unrounded fp32 row sums `w4a16_f32` (K-split partial sums), and the
+bit-exact device `quantize` / `pack` / `unpack` / `dequantize`. As
 in the reference, INT4GEMV_BUILD_DIR may point at another build directory (its `python/`
 subdirectory or the directory itself is searched).
 
@@ -66,6 +67,7 @@ w4a16_kernel = int4gemv_ops.w4a16_kernel
 w4a16_with = int4gemv_ops.w4a16_with
 w4a16_silu_mul = int4gemv_ops.w4a16_silu_mul
 w4a16_bias_residual = int4gemv_ops.w4a16_bias_residual
+w4a16_f32 = int4gemv_ops.w4a16_f32
 w4a16_grouped = int4gemv_ops.w4a16_grouped
 unpack = int4gemv_ops.unpack
 dequantize = int4gemv_ops.dequantize

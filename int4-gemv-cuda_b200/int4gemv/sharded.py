@@ -7,11 +7,12 @@ Two layouts, each with one exchange step per call:
   rank.
 - K-split ("down" projections, e.g. 8192 x 28672): rank r holds columns [k0, k1) of the weights
   (k0, k1 multiples of the group size, so every rank owns whole groups and whole packed words) and
-  the same slice of x; the local GEMV gives a partial y, which is summed across ranks in fp32 by an
-  all-reduce and rounded to fp16 once.
+  the same slice of x; the local GEMV gives the partial y as fp32 row sums (`ops.w4a16_f32`, never
+  rounded to fp16), which an fp32 all-reduce adds across ranks before the one rounding to fp16.
 
-The local GEMV is `ops.w4a16` (the CUDA fast path) unless the caller passes another callable with
-the same signature: there is no CPU fallback in the product path.
+The local GEMVs are `ops.w4a16` (rows split) and `ops.w4a16_f32` (K split), the CUDA fast path,
+unless the caller passes other callables with the same signatures: there is no CPU fallback in the
+product path.
 """
 
 from __future__ import annotations
@@ -60,17 +61,24 @@ def _default_gemv() -> LocalGemv:
     return ops.w4a16
 
 
+def _default_partial() -> LocalGemv:
+    from . import ops
+
+    return ops.w4a16_f32
+
+
 class ShardedW4A16:
     """One weight matrix sharded over a process group; calling it with the full x returns the full
     y on every rank.
 
     mode "n": N-split + all-gather. mode "k": K-split + fp32 all-reduce. The constructor takes the
     full packed tensors (as every rank would load them) and keeps only this rank's shard.
+    local_gemv (rows split) returns fp16 y; local_partial (K split) returns the fp32 row sums.
     """
 
     def __init__(self, qweight: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor,
                  group_size: int, mode: str, process_group=None,
-                 local_gemv: LocalGemv | None = None):
+                 local_gemv: LocalGemv | None = None, local_partial: LocalGemv | None = None):
         if mode not in ("n", "k"):
             raise ValueError(f"mode must be 'n' or 'k', got {mode!r}")
         self.mode = mode
@@ -81,6 +89,7 @@ class ShardedW4A16:
         self.n = qweight.shape[0]
         self.k = qweight.shape[1] * 8
         self.gemv = local_gemv or _default_gemv()
+        self.partial = local_partial or _default_partial()
         if mode == "n":
             self.q, self.s, self.z, self.span = shard_rows(qweight, scales, zeros, self.rank,
                                                            self.world)
@@ -111,8 +120,10 @@ class ShardedW4A16:
             return torch.cat(parts, dim=1)
         k0, k1 = self.span
         if k1 > k0:
-            partial = self.gemv(x[:, k0:k1].contiguous(), self.q, self.s, self.z,
-                                self.group_size).float()
+            partial = self.partial(x[:, k0:k1].contiguous(), self.q, self.s, self.z,
+                                   self.group_size)
+            if partial.dtype != torch.float32:
+                raise TypeError(f"local_partial must return float32, got {partial.dtype}")
         else:
             partial = torch.zeros(m, self.n, dtype=torch.float32, device=x.device)
         dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=self.pg)

@@ -8,7 +8,8 @@ for sm_100a so the reference's GPU kernels can run on the B200 as a second oracl
 kernel to beat.
 
 Usage: python oracle/build_ref.py [--reference /path/to/reference]
-The reference checkout only exists in the build container; the GPU box uses the built .so.
+Without --reference the checkout is taken from $INT4GEMV_REFERENCE, else from BASELINE.json's
+"reference_path". The checkout only exists in the build container; the GPU box uses the built .so.
 """
 
 from __future__ import annotations
@@ -20,7 +21,23 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref"
-DEFAULT_REFERENCE = Path("/root/reference")
+REPO = HERE.parent
+
+
+def reference_dir() -> Path | None:
+    """The reference checkout: $INT4GEMV_REFERENCE, else BASELINE.json's reference_path."""
+    env = os.environ.get("INT4GEMV_REFERENCE")
+    if env:
+        return Path(env)
+    try:
+        import json
+
+        path = json.loads((REPO / "BASELINE.json").read_text()).get("reference_path")
+    except (OSError, ValueError):
+        path = None
+    return Path(path) if path else None
+
+
 SOURCES = ["checks.cpp", "sequential.cpp", "naive.cu", "coalesced.cu", "vectorized.cu",
            "load_only.cu"]
 
@@ -30,9 +47,10 @@ def built_module() -> Path | None:
     return hits[0] if hits else None
 
 
-def build(reference: Path = DEFAULT_REFERENCE, verbose: bool = False) -> Path | None:
-    csrc = reference / "csrc"
-    if not (csrc / "w4a16.h").exists():
+def build(reference: Path | None = None, verbose: bool = False) -> Path | None:
+    reference = reference or reference_dir()
+    csrc = reference / "csrc" if reference else None
+    if csrc is None or not (csrc / "w4a16.h").exists():
         print(f"build_ref: no reference sources at {csrc}; skipped", file=sys.stderr)
         return built_module()
     os.environ.setdefault("MAX_JOBS", str(os.cpu_count() or 4))
@@ -54,7 +72,7 @@ def build(reference: Path = DEFAULT_REFERENCE, verbose: bool = False) -> Path | 
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", type=Path, default=DEFAULT_REFERENCE)
+    ap.add_argument("--reference", type=Path, default=None)
     ap.add_argument("-v", "--verbose", action="store_true")
     args = ap.parse_args()
     print(build(args.reference, args.verbose))

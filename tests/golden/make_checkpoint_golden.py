@@ -22,6 +22,7 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
+REPO = HERE.parents[1]
 
 CASES = [("checkpoint_n64_k512_g128", 64, 512, 128, 5000),
          ("checkpoint_n48_k256_g32", 48, 256, 32, 5001)]
@@ -29,8 +30,17 @@ CASES = [("checkpoint_n64_k512_g128", 64, 512, 128, 5000),
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    ap.add_argument("--reference", type=Path, default=None,
+                    help="the reference checkout (default: $INT4GEMV_REFERENCE, else "
+                         "BASELINE.json's reference_path)")
     args = ap.parse_args()
+    if args.reference is None:
+        sys.path.insert(0, str(REPO / "oracle"))
+        import build_ref
+
+        args.reference = build_ref.reference_dir()
+    if args.reference is None or not args.reference.exists():
+        raise SystemExit("no reference checkout: pass --reference or set INT4GEMV_REFERENCE")
 
     import torch
     from vllm.model_executor.layers.quantization.utils.quant_utils import (awq_pack, gptq_pack,

@@ -67,8 +67,17 @@ def edge_weights() -> np.ndarray:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    ap.add_argument("--reference", type=Path, default=None,
+                    help="the reference checkout (default: $INT4GEMV_REFERENCE, else "
+                         "BASELINE.json's reference_path)")
     args = ap.parse_args()
+    if args.reference is None:
+        sys.path.insert(0, str(REPO / "oracle"))
+        import build_ref
+
+        args.reference = build_ref.reference_dir()
+    if args.reference is None or not args.reference.exists():
+        raise SystemExit("no reference checkout: pass --reference or set INT4GEMV_REFERENCE")
 
     import torch
 

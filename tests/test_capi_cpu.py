@@ -205,3 +205,39 @@ def test_exchange_size_checks():
                                                     128, 5, None)
     assert res == capi.ERR_INVALID
     assert capi.last_error() == "w4a16_exchange_static: unknown mode 5"
+
+
+def test_exchange_static_checks_come_before_setup():
+    """Every argument error of the no-allocation entry point is reported before its first-call
+    setup (which would need a GPU here): null pointers, bad group sizes, shapes the fast path does
+    not take, and sizes whose M x N would overflow if multiplied first."""
+    lib = capi.lib()
+    cases = [
+        ((None, None, None, None, None, 1, 4096, 4096, 128, capi.SHARD_ROWS),
+         "w4a16_exchange_static: null pointer for a non-empty tensor"),
+        ((FAKE, FAKE, FAKE, FAKE, FAKE, 1, 4096, 4096, 100, capi.SHARD_ROWS),
+         "w4a16_exchange_static: group_size 100 must be a positive multiple of 8 dividing "
+         "K = 4096"),
+        ((FAKE, FAKE, FAKE, FAKE, FAKE, 0, 4096, 4096, 128, capi.SHARD_K),
+         "w4a16_exchange_static: M, N and K must be positive"),
+        ((FAKE, FAKE, FAKE, FAKE, FAKE, 2**31 - 1, 2**31 - 1, 4096, 128, capi.SHARD_K),
+         None),
+        ((FAKE, FAKE, FAKE, FAKE, FAKE, 1, 4096, 1000, 8, capi.SHARD_ROWS), None),
+    ]
+    for args, message in cases:
+        assert lib.int4gemv_w4a16_exchange_static(*args, None) == capi.ERR_INVALID
+        if message is not None:
+            assert capi.last_error() == message
+    # the overflow case is the size limit, the last one a shape the fast path does not take
+    lib.int4gemv_w4a16_exchange_static(FAKE, FAKE, FAKE, FAKE, FAKE, 2**31 - 1, 2**31 - 1, 4096,
+                                       128, capi.SHARD_K, None)
+    assert "the static buffer holds 4194304 bytes (M x N <= 262144)" in capi.last_error()
+
+
+def test_set_strict_weights_values():
+    lib = capi.lib()
+    assert lib.int4gemv_set_strict_weights(2) == capi.ERR_INVALID
+    assert capi.last_error() == "set_strict_weights: strict must be 0 or 1, got 2"
+    assert lib.int4gemv_set_strict_weights(1) == capi.OK
+    assert lib.int4gemv_set_strict_weights(0) == capi.OK
+

@@ -24,7 +24,22 @@ KERNELS = [
     ("vectorized", {"threads_per_block": 64, "rows_per_warp": 4}),
     ("w4a16", {}),
 ]
-FAST = ["stream_mma", "tcgen05", "mma_pipeline"]
+FAST = ["stripe_mma", "stream_mma", "tcgen05", "mma_pipeline"]
+
+
+def expected_kernel(m, k, g=128, n=8192):
+    """The kernel int4gemv_w4a16 picks on the fast path's shapes: stripe_mma for M <= 2 and K a
+    multiple of 2048 when x (permuted, per-item padded), its tables and three 34 KB stripes fit in
+    227 KB of shared memory; stream_mma for the rest (M <= 32, K a multiple of 1024)."""
+    if m > 2 or k % 2048 or g != 128:
+        return "stream_mma"
+    units = (n + 3) // 4
+    rows_cap = 4 * (-(-units // min(torch.cuda.get_device_properties(0).multi_processor_count,
+                                    units)))
+    items = k // 128
+    off = 1536 + m * items * 272 + items * 40 + 16 * rows_cap * m * 4
+    off = -(-off // 1024) * 1024
+    return "stripe_mma" if (227 * 1024 - off) // 34816 >= 3 else "stream_mma"
 
 
 def cuda(*arrays):
@@ -84,7 +99,7 @@ def test_full_size_w4a16(m, n, k):
     y = ops.w4a16(*args, 128)
     ref = oracle.reference(x, q, s, z, 128)
     assert_close(y, ref, f"w4a16 {m}x{n}x{k} ({ops.w4a16_kernel(*args, 128)})")
-    assert ops.w4a16_kernel(*args, 128) == "stream_mma"
+    assert ops.w4a16_kernel(*args, 128) == expected_kernel(m, k, n=n)
 
 
 @pytest.mark.parametrize("name,cfg", KERNELS[:3] + [("w4a16", {})])
@@ -137,7 +152,8 @@ def test_each_fast_kernel(m, n, k, g):
 
 
 def test_fast_kernel_coverage():
-    """stream_mma takes every BASELINE shape; mma_pipeline takes group 32 / 64."""
+    """stream_mma takes every BASELINE shape (stripe_mma those with M <= 2); mma_pipeline takes
+    group 32 / 64."""
     x, q, s, z = cuda(*oracle.synthetic(1, 256, 8192, 128))
     assert [k for k, _ in fast_kernels_for([x, q, s, z], 128)] == FAST
     x, q, s, z = cuda(*oracle.synthetic(2, 256, 1024, 32))
@@ -159,10 +175,88 @@ STREAM = [
 def test_stream_mma_shapes(m, n, k):
     x, q, s, z = oracle.synthetic(m, n, k, 128, seed=11 * m + n + k)
     args = cuda(x, q, s, z)
-    assert ops.w4a16_kernel(*args, 128) == "stream_mma"
+    assert ops.w4a16_kernel(*args, 128) == expected_kernel(m, k, n=n)
     y = ops.w4a16_with(*args, 128, "stream_mma")
     torch.cuda.synchronize()
     assert_close(y, oracle.reference(x, q, s, z, 128), f"stream_mma {m}x{n}x{k}")
+
+
+# stripe_mma edge cases: rows per CTA below one 16-row tile, between one and two tiles, several
+# 32-row blocks, N not a multiple of 4, M = 1 and 2, K from one stripe (2048) to 28672.
+STRIPE = [
+    (1, 1, 2048), (2, 5, 2048), (1, 37, 8192), (2, 148 * 4 + 3, 4096), (1, 148 * 20 + 1, 6144),
+    (2, 148 * 24, 2048), (1, 148 * 36 + 2, 10240), (2, 4099, 8192), (1, 1000, 28672),
+    (2, 300, 14336), (1, 28672, 2048),
+]
+
+
+@pytest.mark.parametrize("m,n,k", STRIPE, ids=[f"m{m}_n{n}_k{k}" for m, n, k in STRIPE])
+def test_stripe_mma_shapes(m, n, k):
+    x, q, s, z = oracle.synthetic(m, n, k, 128, seed=13 * m + n + k)
+    args = cuda(x, q, s, z)
+    assert ops.w4a16_kernel(*args, 128) == "stripe_mma"
+    y = ops.w4a16_with(*args, 128, "stripe_mma")
+    torch.cuda.synchronize()
+    assert_close(y, oracle.reference(x, q, s, z, 128), f"stripe_mma {m}x{n}x{k}")
+
+
+def test_stripe_mma_rejects():
+    """Shapes stripe_mma does not take raise a clear error when it is asked for by name."""
+    for m, k, why in ((3, 2048, "M must be 1 or 2"), (1, 3072, "K must be a multiple of 2048")):
+        args = cuda(*oracle.synthetic(m, 64, k, 128))
+        with pytest.raises(RuntimeError, match=why):
+            ops.w4a16_with(*args, 128, "stripe_mma")
+
+
+@pytest.mark.parametrize("kern,m", [("stripe_mma", 1), ("stripe_mma", 2), ("stream_mma", 1),
+                                    ("stream_mma", 2), ("stream_mma", 8), ("stream_mma", 16),
+                                    ("tcgen05", 1)])
+def test_repeated_calls_weights_in_l2(kern, m):
+    """The same weights (34 MB, resident in the 126 MB L2 after the first call) in eight calls in a
+    row: every ring refill then lands within a few hundred nanoseconds, so a stage released before
+    its shared-memory loads have returned would be overwritten under them. Each call is checked."""
+    x, q, s, z = oracle.synthetic(m, 8192, 8192, 128, seed=41 + m)
+    args = cuda(x, q, s, z)
+    ref = oracle.reference(x, q, s, z, 128)
+    for rep in range(8):
+        y = ops.w4a16_with(*args, 128, kern)
+        torch.cuda.synchronize()
+        assert_close(y, ref, f"{kern} M={m} call {rep}")
+
+
+def test_strict_weights_after_in_place_requantise():
+    """Weights written by the kernel right before the GEMV in the same stream (device quantize in
+    place) with int4gemv_set_strict_weights(1): the GEMV waits for them, on every fast kernel; the
+    strict and default orderings give bit-identical results when nothing writes the weights."""
+    from int4gemv import capi
+
+    lib = capi.lib()
+    for m, k, kern in ((1, 4096, "stripe_mma"), (2, 4096, "stripe_mma"), (3, 4096, "stream_mma"),
+                       (12, 2048, "stream_mma"), (1, 1024, "tcgen05")):
+        n = 2048
+        gen = torch.Generator(device="cuda").manual_seed(m * k)
+        w0 = torch.randn(n, k, generator=gen, device="cuda") * 0.02
+        w1 = torch.randn(n, k, generator=gen, device="cuda") * 0.02
+        x = torch.randn(m, k, generator=gen, device="cuda").half()
+        q, s, z = ops.quantize(w0, 128)
+        y_default = ops.w4a16_with(x, q, s, z, 128, kern)
+        capi.check(lib.int4gemv_set_strict_weights(1))
+        try:
+            y_strict = ops.w4a16_with(x, q, s, z, 128, kern)
+            assert torch.equal(y_default.view(torch.int16), y_strict.view(torch.int16)), kern
+            for _ in range(3):  # re-quantise in place, then multiply right after it
+                q1, s1, z1 = ops.quantize(w1, 128)
+                q.copy_(q1)
+                s.copy_(s1)
+                z.copy_(z1)
+                y = ops.w4a16_with(x, q, s, z, 128, kern)
+                torch.cuda.synchronize()
+                want = oracle.reference(x.cpu().numpy(), q1.cpu().numpy(), s1.cpu().numpy(),
+                                        z1.cpu().numpy(), 128)
+                assert_close(y, want, f"strict {kern} M={m}")
+                w0, w1 = w1, w0
+        finally:
+            capi.check(lib.int4gemv_set_strict_weights(0))
 
 
 def test_stream_mma_chained_calls():
@@ -230,8 +324,9 @@ def test_misaligned_inputs():
         run("vectorized", {}, args, 128)
 
 
-def test_deterministic():
-    x, q, s, z = oracle.synthetic(4, 8192, 8192, 128, seed=11)
+@pytest.mark.parametrize("m", [1, 4])
+def test_deterministic(m):
+    x, q, s, z = oracle.synthetic(m, 8192, 8192, 128, seed=11)
     args = cuda(x, q, s, z)
     a = ops.w4a16(*args, 128)
     b = ops.w4a16(*args, 128)
@@ -341,9 +436,10 @@ def test_silu_mul_rejects():
 
 
 # Fused bias / residual epilogue: y = x @ W^T + bias + residual, rounded to fp16 once, on every
-# kernel the dispatcher can pick (the shapes below reach stream_mma, mma_pipeline, vectorized and
-# coalesced).
-BIAS = [(1, 8192, 8192, 128, "stream_mma"), (5, 300, 1024, 128, "stream_mma"),
+# kernel the dispatcher can pick (the shapes below reach stripe_mma, stream_mma, mma_pipeline,
+# vectorized and coalesced).
+BIAS = [(1, 8192, 8192, 128, "stripe_mma"), (2, 1000, 4096, 128, "stripe_mma"),
+        (5, 300, 1024, 128, "stream_mma"),
         (3, 257, 768, 64, "mma_pipeline"), (2, 100, 640, 128, "vectorized"),
         (4, 77, 96, 16, "coalesced")]
 

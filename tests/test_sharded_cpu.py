@@ -28,6 +28,11 @@ def oracle_gemv(x, q, s, z, g):
     return torch.from_numpy(y.astype(np.float16))
 
 
+def oracle_partial(x, q, s, z, g):
+    y = oracle.reference(x.numpy(), q.numpy(), s.numpy(), z.numpy(), g)
+    return torch.from_numpy(y.astype(np.float32))
+
+
 def _free_port() -> int:
     with socket.socket() as sock:
         sock.bind(("127.0.0.1", 0))
@@ -43,7 +48,8 @@ def _worker(rank, world, port, cases, results):
         for mode, m, n, k, g in cases:
             x, q, s, z = oracle.synthetic(m, n, k, g, seed=n + k)
             t = [torch.from_numpy(a) for a in (x, q, s, z)]
-            layer = ShardedW4A16(t[1], t[2], t[3], g, mode, local_gemv=oracle_gemv)
+            layer = ShardedW4A16(t[1], t[2], t[3], g, mode, local_gemv=oracle_gemv,
+                                 local_partial=oracle_partial)
             out.append(layer(t[0]).float().numpy())
         results[rank] = out
     finally:
@@ -122,3 +128,49 @@ def test_fused_layer_shape_checks():
         assert "multiple of the world size" in n_msg
         assert "multiple of 1024 and at least 1024 x world" in k_msg
         assert "mode must be" in mode_msg
+
+
+def _ksplit_rounding_worker(rank, world, port, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        m, n, k, g = 2, 64, 1024, 128
+        x, q, s, z = oracle.synthetic(m, n, k, g, seed=77)
+        t = [torch.from_numpy(a) for a in (x, q, s, z)]
+        layer = ShardedW4A16(t[1], t[2], t[3], g, "k", local_gemv=oracle_gemv,
+                             local_partial=oracle_partial)
+        results[rank] = layer(t[0]).numpy()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_k_split_rounds_once():
+    """The K-split layer adds the ranks' fp32 partial sums and rounds to fp16 once: its output is
+    bit-identical to fp16(p0 + p1), and differs from the twice-rounded fp16(fp16(p0) + fp16(p1))
+    on this case (so the test would catch a partial rounded to fp16 before the all-reduce)."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    results = ctx.Manager().dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_ksplit_rounding_worker, args=(r, world, port, results))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0, f"rank exited with {p.exitcode}"
+    m, n, k, g = 2, 64, 1024, 128
+    x, q, s, z = oracle.synthetic(m, n, k, g, seed=77)
+    partials = []
+    for r in range(world):
+        k0, k1 = split_range(k, world, r, g)
+        partials.append(oracle.reference(x[:, k0:k1], q[:, k0 // 8:k1 // 8],
+                                         s[:, k0 // g:k1 // g], z[:, k0 // g:k1 // g],
+                                         g).astype(np.float32))
+    once = (partials[0] + partials[1]).astype(np.float16)
+    twice = (partials[0].astype(np.float16).astype(np.float32)
+             + partials[1].astype(np.float16).astype(np.float32)).astype(np.float16)
+    for r in range(world):
+        np.testing.assert_array_equal(results[r].view(np.uint16), once.view(np.uint16))
+    assert not np.array_equal(once.view(np.uint16), twice.view(np.uint16))

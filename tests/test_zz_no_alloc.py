@@ -58,3 +58,34 @@ def test_static_rejects_oversize():
     with pytest.raises(capi.CapiError, match="static buffer holds"):
         capi.call("int4gemv_w4a16_exchange_static", x.data_ptr(), x.data_ptr(), x.data_ptr(),
                   x.data_ptr(), x.data_ptr(), 32, 16384, 1024, 128, capi.SHARD_K, None)
+
+
+def test_static_alternating_shapes_share_one_buffer():
+    """Calls of different shapes and modes in a row on the one static buffer, with a rejected
+    oversize call in between: each result is bit-identical to the same kernel (stream_mma) run
+    through the named-kernel entry point, and the device status stays clean."""
+    k = 4096
+    _, q, s, z = oracle.synthetic(1, 8192, k, 128, seed=23)
+    tq, ts, tz = (torch.from_numpy(a).cuda() for a in (q, s, z))
+    stream = torch.cuda.current_stream().cuda_stream
+    sequence = [(capi.SHARD_ROWS, 1, 8192), (capi.SHARD_K, 4, 4096), (None, 32, 16384),
+                (capi.SHARD_ROWS, 2, 4096), (capi.SHARD_K, 1, 8192)]
+    for i, (mode, m, n) in enumerate(sequence):
+        x = np.random.default_rng(100 + i).standard_normal((m, k)).astype(np.float16)
+        tx = torch.from_numpy(x).cuda()
+        y_static = torch.empty(m, n, dtype=torch.float16, device="cuda")
+        if mode is None:  # larger than the static buffer: rejected, nothing launched
+            with pytest.raises(capi.CapiError, match="static buffer holds"):
+                capi.call("int4gemv_w4a16_exchange_static", y_static.data_ptr(), tx.data_ptr(),
+                          tq.data_ptr(), ts.data_ptr(), tz.data_ptr(), m, n, k, 128,
+                          capi.SHARD_K, stream)
+            continue
+        y_plain = torch.empty(m, n, dtype=torch.float16, device="cuda")
+        capi.call("int4gemv_w4a16_exchange_static", y_static.data_ptr(), tx.data_ptr(),
+                  tq.data_ptr(), ts.data_ptr(), tz.data_ptr(), m, n, k, 128, mode, stream)
+        capi.call("int4gemv_w4a16_kernel", b"stream_mma", y_plain.data_ptr(), tx.data_ptr(),
+                  tq.data_ptr(), ts.data_ptr(), tz.data_ptr(), m, n, k, 128, stream)
+        torch.cuda.synchronize()
+        assert torch.equal(y_static.view(torch.int16), y_plain.view(torch.int16)), (mode, m, n)
+    assert capi.device_status() == 0
+
