@@ -7,11 +7,10 @@
 // one 2-D TMA tile of the packed weights (32 rows x 1 KB, no swizzle) plus two tiles of its scales
 // and zeros (32 rows x 16 groups), 34 KB in all; blocks of fewer rows use boxes of 16 / 8 / 4 rows,
 // so a CTA never fetches a row it does not own. On B200 these 1 KB-wide tiles stream a W4A16
-// matrix about 20 % faster than 128-byte-wide ones (measured). The ring takes nearly all of shared
-// memory (five stripes at K = 8192, three quarters of a CTA's bytes), and unless the caller asks
-// for strict ordering the producer warp issues the whole ring before griddepcontrol.wait: while
-// the previous kernel in the stream finishes, the weights of this call are already on their way,
-// so HBM does not idle between back-to-back calls.
+// matrix about 20 % faster than 128-byte-wide ones (measured). The ring holds three stripes
+// (about 100 KB per SM), and unless the caller asks for strict ordering the producer warp issues
+// the whole ring before griddepcontrol.wait: while the previous kernel in the stream finishes, the
+// weights of this call are already on their way.
 //
 // x. Right after the dependency wait every consumer thread loads its share of x with 16-byte loads
 // (one round trip), permutes each 8-weight block to the order of the unpacked A halves,
@@ -59,7 +58,10 @@ constexpr int kSxZOff = kSxQBytes + kSxRows * kSxMetaRow;
 constexpr int kSxStageBytes = kSxQBytes + 2 * kSxRows * kSxMetaRow;  // 34816
 constexpr int kSxTxPerRow = kSxRowBytes + 2 * kSxMetaRow;           // 1088 bytes land per row
 constexpr int kSxItemBytes = 272;   // one item of permuted x for one row of x (256 + 16 pad)
-constexpr int kSxMaxStages = 8;
+// Ring depth. Deeper rings keep more bytes in flight across all SMs, which lengthens every
+// request's queueing in the memory system, x's included; three 34 KB stripes per SM measured
+// fastest back to back (five: +4 %).
+constexpr int kSxMaxStages = 3;
 constexpr int kSxMaxConsumers = 16 * kWarp;  // the most consumer threads of any instance
 constexpr int kSxSmemLimit = 227 * 1024;
 constexpr int kSxMinStages = 3;
@@ -255,13 +257,12 @@ struct StripeX {
   float2 cinit, xsm;
 };
 
-template <int GPW>
+template <int GPW, int NT>
 __device__ __forceinline__ void stripe_load(const unsigned char* st, const int (&a_off)[GPW],
-                                            int s_off, int z_off, bool zero_term, bool two_tiles,
+                                            int s_off, int z_off, bool zero_term,
                                             StripeRegs<GPW>& r) {
 #pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    if (t == 1 && !two_tiles) break;
+  for (int t = 0; t < NT; ++t) {
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int row = 16 * t + 8 * h;
@@ -299,9 +300,9 @@ __device__ __forceinline__ void stripe_load_x(const unsigned char* const (&b_bas
 // granule's four words (the first low-half chain started from C = cinit, the others from zero),
 // added at the end: d[t] = sum_k q_k x_k for the lane's (rows, item) as the MMA D fragment (rows
 // g, g + 8 x columns 2c, 2c + 1).
-template <int GPW>
+template <int GPW, int NT>
 __device__ __forceinline__ void stripe_mma(const StripeRegs<GPW>& r, const StripeX<GPW>& x,
-                                           bool two_tiles, float (&d)[2][4]) {
+                                           float (&d)[2][4]) {
   float ch[2][2 * GPW - 1][4];  // the chains other than the first low-half one
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
@@ -313,8 +314,7 @@ __device__ __forceinline__ void stripe_mma(const StripeRegs<GPW>& r, const Strip
 #pragma unroll
     for (int q = 0; q < GPW; ++q) {
 #pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        if (t == 1 && !two_tiles) break;
+      for (int t = 0; t < NT; ++t) {
         uint32_t hg[4], h8[4];
         unpack_x16(word_of4(r.aw[q][t][0], u), hg);
         unpack_x16(word_of4(r.aw[q][t][1], u), h8);
@@ -336,8 +336,7 @@ __device__ __forceinline__ void stripe_mma(const StripeRegs<GPW>& r, const Strip
     }
   }
 #pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    if (t == 1 && !two_tiles) break;
+  for (int t = 0; t < NT; ++t) {
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
 #pragma unroll
@@ -347,13 +346,12 @@ __device__ __forceinline__ void stripe_mma(const StripeRegs<GPW>& r, const Strip
 }
 
 // One scale per (row, item) into the row accumulators; the granule-0 warps add the zero term.
-template <int MC, int GPW>
+template <int MC, int GPW, int NT>
 __device__ __forceinline__ void stripe_epilogue(const StripeRegs<GPW>& r, const float (&d)[2][4],
-                                                float2 xsm, bool zero_term, bool two_tiles,
+                                                float2 xsm, bool zero_term,
                                                 float (&acc)[2][2][MC]) {
 #pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    if (t == 1 && !two_tiles) break;
+  for (int t = 0; t < NT; ++t) {
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const float s = __half2float(__ushort_as_half(static_cast<uint16_t>(r.sb[t][h])));
@@ -441,10 +439,10 @@ __global__ void __launch_bounds__((CW + 1) * kWarp, 1)
   // epilogue, release the stage. (Loading the next stage's operands during this stage's MMAs was
   // measured slower on B200.)
   StageRingSx ring{full, p.stages, p.status, true, 0, 0u};
-  for (int blk = 0; blk < blocks; ++blk) {
-    const int rows_b = min(kSxRows, rows - blk * kSxRows);
-    const bool two_tiles = rows_b > 16;  // uniform over the CTA
-    float acc[2][2][MC];                 // [tile][row g / g + 8][m]
+  // One block of rows: NT 16-row tiles (2, or 1 when the block has at most 16 rows), a
+  // compile-time count so the two tiles' MMAs interleave freely.
+  auto run_block = [&]<int NT>(int blk, int rows_b) {
+    float acc[2][2][MC];  // [tile][row g / g + 8][m]
 #pragma unroll
     for (int t = 0; t < 2; ++t)
 #pragma unroll
@@ -454,13 +452,12 @@ __global__ void __launch_bounds__((CW + 1) * kWarp, 1)
     for (int j = 0; j < p.stripes; ++j) {
       const int slot = ring.next();
       StripeRegs<kGPW> r;
-      stripe_load<kGPW>(stages + slot * kSxStageBytes, a_off, s_off, z_off, zero_term,
-                        two_tiles, r);
+      stripe_load<kGPW, NT>(stages + slot * kSxStageBytes, a_off, s_off, z_off, zero_term, r);
       StripeX<kGPW> xr;
       stripe_load_x<kGPW>(b_base, b_step, bq, xsum, j, item, gran, zero_term, xr);
       float d[2][4];
-      stripe_mma<kGPW>(r, xr, two_tiles, d);
-      stripe_epilogue<MC, kGPW>(r, d, xr.xsm, zero_term, two_tiles, acc);
+      stripe_mma<kGPW, NT>(r, xr, d);
+      stripe_epilogue<MC, kGPW, NT>(r, d, xr.xsm, zero_term, acc);
       // Release the stage only after its values have been used: mbarrier.arrive does not wait
       // for shared-memory loads still in flight, and a refill served from L2 can land within a
       // few hundred nanoseconds. (Releasing here measured as fast as releasing right after the
@@ -470,7 +467,7 @@ __global__ void __launch_bounds__((CW + 1) * kWarp, 1)
     }
     // the four items of this warp's quad, then one partial per (row, m) and warp
 #pragma unroll
-    for (int t = 0; t < 2; ++t)
+    for (int t = 0; t < NT; ++t)
 #pragma unroll
       for (int h = 0; h < 2; ++h)
 #pragma unroll
@@ -482,6 +479,14 @@ __global__ void __launch_bounds__((CW + 1) * kWarp, 1)
             red[(warp * p.rows_cap + blk * kSxRows + 16 * t + 8 * h + g) * MC + m] = v;
           }
         }
+  };
+  for (int blk = 0; blk < blocks; ++blk) {
+    const int rows_b = min(kSxRows, rows - blk * kSxRows);
+    if (rows_b > 16) {  // uniform over the CTA
+      run_block.template operator()<2>(blk, rows_b);
+    } else {
+      run_block.template operator()<1>(blk, rows_b);
+    }
   }
 
   // ---- add the CW partials of every output in a fixed order; store fp16 ---------------------
