@@ -83,8 +83,9 @@ int int4gemv_sequential(void* y, const void* x, const void* qweight, const void*
 
 /* ---- The B200 fast path (new; no counterpart in the reference) ------------------------------- */
 
-/* Bytes of device workspace int4gemv_w4a16 can use for this shape (0 if none): for M >= 5 on the
- * fast path's shapes, room for x permuted once per call by a pre-kernel instead of in every CTA. */
+/* Bytes of device workspace int4gemv_w4a16 can use for this shape (0 if none): for 5 <= M <= 8 on
+ * the fast path's shapes, room for x permuted once per call by a pre-kernel instead of in every
+ * CTA. */
 int64_t int4gemv_w4a16_workspace_size(int64_t m, int64_t n, int64_t k, int64_t group_size);
 
 /* y = x @ dequant(W)^T through the fastest kernel for the shape: a persistent, TMA-bulk-fed,
@@ -97,16 +98,24 @@ int int4gemv_w4a16(void* y, const void* x, const void* qweight, const void* scal
                    const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
                    void* workspace, int64_t workspace_bytes, void* stream);
 
-/* Name of the kernel int4gemv_w4a16 picks for this shape and these pointers ("stripe_mma",
- * "stream_mma", "mma_pipeline", "vectorized", "coalesced"); for tests and the benchmark. Static
- * storage. */
+/* Name of the kernel int4gemv_w4a16 picks for this shape and these pointers ("stripe_mma" for
+ * M <= 2, "tc_dequant" for 9 <= M <= 64, "stream_mma" otherwise up to M = 32 when group_size is 128
+ * and K a multiple of 1024; "mma_pipeline", "vectorized", "coalesced" for the other shapes); for
+ * tests and the benchmark. Static storage.
+ *
+ * tc_dequant keeps split-K partial sums and per-tile counters in static device memory, so two of
+ * its calls must not run at the same time on one device: calls in one stream are ordered, and
+ * before a call in a different stream than the previous one that stream waits for an event
+ * recorded after the previous call (host-side, nothing to do for the caller). Calls captured into
+ * CUDA graphs are ordered only by the graphs' own streams: replays of such graphs must not
+ * overlap on one device. */
 const char* int4gemv_w4a16_kernel_name(const void* x, const void* qweight, const void* scales,
                                        const void* zeros, int64_t m, int64_t n, int64_t k,
                                        int64_t group_size);
 
-/* Runs one named kernel instead of the automatic choice: "stripe_mma", "stream_mma", "tcgen05",
- * "mma_pipeline", "vectorized" (128 threads, 2 rows per warp), "coalesced" or "naive". For tests
- * and benchmarks.
+/* Runs one named kernel instead of the automatic choice: "stripe_mma", "tc_dequant",
+ * "stream_mma", "tcgen05", "mma_pipeline", "vectorized" (128 threads, 2 rows per warp),
+ * "coalesced" or "naive". For tests and benchmarks.
  * Fails with
  * INT4GEMV_ERR_INVALID if that kernel does not support the shape or the pointers' alignment. */
 int int4gemv_w4a16_kernel(const char* kernel, void* y, const void* x, const void* qweight,
@@ -148,8 +157,9 @@ int int4gemv_w4a16_grouped(int count, void* const* ys, const int64_t* ns, const 
 /* y [M, N] fp32 = x @ W^T, the fp32 row sums themselves with no rounding to fp16: the local partial
  * sums of a layer split along K over several GPUs, which are added across ranks and rounded to
  * fp16 once (int4gemv/sharded.py). Same inputs and checks as int4gemv_w4a16; needs the fast path's
- * shapes (group_size 128, K a multiple of 1024, M <= 32, 16-byte aligned x, qweight, scales,
- * zeros), INT4GEMV_ERR_INVALID with the reason otherwise. New: the reference returns fp16 only. */
+ * shapes (group_size 128, K a multiple of 1024, M <= 64 (stream_mma below M = 9, tc_dequant from
+ * there), 16-byte aligned x, qweight, scales, zeros), INT4GEMV_ERR_INVALID with the reason
+ * otherwise. New: the reference returns fp16 only. */
 int int4gemv_w4a16_f32(void* y, const void* x, const void* qweight, const void* scales,
                        const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
                        void* stream);
@@ -274,18 +284,19 @@ int int4gemv_w4a16_exchange_static(void* y, const void* x, const void* qweight,
 
 /* ---- Stream ordering of the weights ---------------------------------------------------------- */
 
-/* The pipelined kernels (stripe_mma, stream_mma, tcgen05, and the fused epilogues and exchange on
- * them) are launched with programmatic dependent launch: a call may start while the previous
- * kernel in the stream is still running, and by default it already streams its qweight, scales
- * and zeros then; x is read, and y written, only after that kernel has completed. This is what
- * lets back-to-back GEMVs keep HBM busy, and it is safe whenever the weights were not written by
- * the kernel right before the call in the same stream (weights loaded or repacked earlier, or
+/* The pipelined kernels (stripe_mma, tc_dequant, stream_mma, tcgen05, and the fused epilogues and
+ * exchange on them) are launched with programmatic dependent launch: a call may start while the
+ * previous kernel in the stream is still running, and by default it already streams its qweight,
+ * scales and zeros then; x is read, and y written, only after that kernel has completed. This is
+ * what lets back-to-back GEMVs keep HBM busy, and it is safe whenever the weights were not written
+ * by the kernel right before the call in the same stream (weights loaded or repacked earlier, or
  * written by work that was followed by another kernel, an event or a copy, are fine). A caller
- * that does write the weights in the immediately preceding kernel (e.g. re-quantising in place
- * and then multiplying) calls int4gemv_set_strict_weights(1): every pipelined kernel then reads
- * its weights only after the previous kernel has completed, at some cost in overlap. Process-wide;
- * 0 restores the default. INT4GEMV_ERR_INVALID for other values. No counterpart in the reference
- * (its kernels use plain stream order). */
+ * that does write the weights in the immediately preceding kernel (e.g. re-quantising in place and
+ * then multiplying) calls int4gemv_set_strict_weights(1): every pipelined kernel then reads its
+ * weights only after the previous kernel has completed, at some cost in overlap. Process-wide; 0
+ * restores the default. INT4GEMV_ERR_INVALID for other values. No counterpart in the reference
+ * (its kernels use plain stream order).
+ */
 int int4gemv_set_strict_weights(int strict);
 
 /* ---- Device-side status --------------------------------------------------------------------- */

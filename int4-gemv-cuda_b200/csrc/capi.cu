@@ -153,10 +153,19 @@ int empty_cases(const char* name, void* y, int64_t m, int64_t n, int64_t k, cuda
 
 int launched(const char* name, cudaError_t err) { return err == cudaSuccess ? ok() : cuda_fail(name, err); }
 
-enum class Pick { kStripeMma, kStreamMma, kTcgen05, kMmaPipeline, kVectorized, kCoalesced };
+enum class Pick {
+  kStripeMma, kTcDequant, kStreamMma, kTcgen05, kMmaPipeline, kVectorized, kCoalesced
+};
+
+// From this many rows of x the tcgen05 kernel (one MMA instruction per 2048 weights, whatever the
+// row count up to 64) is faster than the warp-MMA stream, whose MMA count grows with M (measured on
+// B200 at 8192 x 8192, 4096 x 14336 and 14336 x 4096: stream_mma ahead at M = 8, tc_dequant from
+// M = 10 on).
+constexpr int kTcDequantMinM = 9;
 
 Pick pick_kernel(const i4::GemvArgs& a) {
   if (i4::stripe_mma_supported(a, nullptr)) return Pick::kStripeMma;
+  if (a.m >= kTcDequantMinM && i4::tc_dequant_supported(a, nullptr)) return Pick::kTcDequant;
   if (i4::stream_mma_supported(a, nullptr)) return Pick::kStreamMma;
   if (i4::mma_pipeline_supported(a, nullptr)) return Pick::kMmaPipeline;
   if (a.group % 32 == 0 && reinterpret_cast<uintptr_t>(a.x) % 16 == 0 &&
@@ -171,6 +180,8 @@ int run_picked(const char* name, const i4::GemvArgs& a, cudaStream_t st) {
   switch (pick_kernel(a)) {
     case Pick::kStripeMma:
       return launched(name, i4::launch_stripe_mma(a, st, strict_weights()));
+    case Pick::kTcDequant:
+      return launched(name, i4::launch_tc_dequant(a, st, strict_weights()));
     case Pick::kStreamMma:
       return launched(name, i4::launch_stream_mma(a, st, strict_weights()));
     case Pick::kTcgen05:
@@ -321,9 +332,10 @@ int int4gemv_kernel_info(const char* kernel, int64_t m, int64_t threads_per_bloc
   } else if (std::strcmp(kernel, "naive") == 0 || std::strcmp(kernel, "coalesced") == 0) {
     err = i4::simt_attrs(kernel, static_cast<int>(m), 0, 1, &at);
   } else if (std::strcmp(kernel, "w4a16") == 0) {
-    err = m <= 2    ? i4::stripe_mma_attrs(static_cast<int>(m), &at)
-          : m <= 32 ? i4::stream_mma_attrs(static_cast<int>(m), &at)
-                    : i4::mma_pipeline_attrs(16, &at);
+    err = m <= 2                ? i4::stripe_mma_attrs(static_cast<int>(m), &at)
+          : m < kTcDequantMinM  ? i4::stream_mma_attrs(static_cast<int>(m), &at)
+          : m <= 64             ? i4::tc_dequant_attrs(static_cast<int>(m), &at)
+                                : i4::mma_pipeline_attrs(16, &at);
   } else {
     return fail(INT4GEMV_ERR_INVALID, "kernel_info: unknown kernel '%s'", kernel);
   }
@@ -362,7 +374,7 @@ int64_t int4gemv_w4a16_workspace_size(int64_t m, int64_t n, int64_t k, int64_t g
   // The size depends on the shape only; aligned stand-in pointers pass the alignment checks.
   const void* aligned = reinterpret_cast<const void*>(static_cast<uintptr_t>(256));
   const i4::GemvArgs a = make_args(nullptr, aligned, aligned, aligned, aligned, m, n, k, group_size);
-  return i4::stream_mma_workspace_bytes(a);
+  return pick_kernel(a) == Pick::kStreamMma ? i4::stream_mma_workspace_bytes(a) : 0;
 }
 
 int int4gemv_w4a16(void* y, const void* x, const void* qweight, const void* scales,
@@ -456,6 +468,8 @@ const char* int4gemv_w4a16_kernel_name(const void* x, const void* qweight, const
   switch (pick_kernel(a)) {
     case Pick::kStripeMma:
       return "stripe_mma";
+    case Pick::kTcDequant:
+      return "tc_dequant";
     case Pick::kStreamMma:
       return "stream_mma";
     case Pick::kTcgen05:
@@ -489,6 +503,10 @@ int int4gemv_w4a16_kernel(const char* kernel, void* y, const void* x, const void
   if (std::strcmp(kernel, "stripe_mma") == 0) {
     if (!i4::stripe_mma_supported(a, &why)) return fail(INT4GEMV_ERR_INVALID, "stripe_mma: %s", why);
     return launched(name, i4::launch_stripe_mma(a, st, strict_weights()));
+  }
+  if (std::strcmp(kernel, "tc_dequant") == 0) {
+    if (!i4::tc_dequant_supported(a, &why)) return fail(INT4GEMV_ERR_INVALID, "tc_dequant: %s", why);
+    return launched(name, i4::launch_tc_dequant(a, st, strict_weights()));
   }
   if (std::strcmp(kernel, "tcgen05") == 0) {
     if (!i4::tc_gemv_supported(a, &why)) return fail(INT4GEMV_ERR_INVALID, "tcgen05: %s", why);
@@ -545,6 +563,9 @@ int int4gemv_w4a16_f32(void* y, const void* x, const void* qweight, const void* 
   i4::GemvArgs a = make_args(y, x, qweight, scales, zeros, m, n, k, group_size);
   a.epilogue = i4::kStoreF32;
   const char* why = "unsupported shape";
+  if (a.m >= kTcDequantMinM && i4::tc_dequant_supported(a, nullptr)) {
+    return launched(name, i4::launch_tc_dequant(a, st, strict_weights()));
+  }
   if (!i4::stream_mma_supported(a, &why)) return fail(INT4GEMV_ERR_INVALID, "%s: %s", name, why);
   return launched(name, i4::launch_stream_mma(a, st, strict_weights()));
 }

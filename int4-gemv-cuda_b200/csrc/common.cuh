@@ -97,6 +97,20 @@ __device__ __forceinline__ uint4 permute_x_block(const uint4& v, float& bsum, fl
   return o;
 }
 
+// permute_x_block without the sums.
+__device__ __forceinline__ uint4 permute_x8(const uint4& v) {
+  uint4 o;
+  uint32_t hi02, hi13;
+  asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(o.x) : "r"(v.x), "r"(v.z));  // (x0, x4)
+  asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(hi02) : "r"(v.x), "r"(v.z));  // (x1, x5)
+  asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(o.z) : "r"(v.y), "r"(v.w));  // (x2, x6)
+  asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(hi13) : "r"(v.y), "r"(v.w));  // (x3, x7)
+  const uint32_t sixteenth = 0x2C002C00u;                                // (1/16, 1/16)
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o.y) : "r"(hi02), "r"(sixteenth));
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o.w) : "r"(hi13), "r"(sixteenth));
+  return o;
+}
+
 __device__ __forceinline__ float2 half2_bits_to_float2(uint32_t bits) {
   __half2 h;
   memcpy(&h, &bits, sizeof(h));

@@ -128,6 +128,14 @@ bool stripe_mma_supported(const GemvArgs& a, const char** why);
 cudaError_t launch_stripe_mma(const GemvArgs& a, cudaStream_t stream, bool strict);
 cudaError_t stripe_mma_attrs(int m, KernelAttrs* out);
 
+// tcgen05 GEMV for M <= 64, group 128, K % 1024 == 0 (tc_dequant.cu): weights dequantized into
+// TMEM, one accumulator per 128-row tile, stream-K split over the SMs with a fixed-order reduction
+// of shared tiles through static device memory (calls in different streams are ordered by an
+// event). Plain stores only (kStoreY with bias / residual, or kStoreF32).
+bool tc_dequant_supported(const GemvArgs& a, const char** why);
+cudaError_t launch_tc_dequant(const GemvArgs& a, cudaStream_t stream, bool strict);
+cudaError_t tc_dequant_attrs(int m, KernelAttrs* out);
+
 // TMA-bulk-fed mma.sync pipeline (mma_pipeline.cu). `why` gets a reason when unsupported.
 bool mma_pipeline_supported(const GemvArgs& a, const char** why);
 cudaError_t launch_mma_pipeline(const GemvArgs& a, cudaStream_t stream);

@@ -40,6 +40,7 @@
 #include <algorithm>
 #include <mutex>
 
+#include "tcgen05.cuh"
 #include "weight_stream.cuh"
 
 namespace i4 {
@@ -93,76 +94,6 @@ __device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, __half2 f) {
   return r;
 }
 
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-      "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
-      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
-      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-      : "memory");
-}
-
-template <int MT>
-__device__ __forceinline__ void tmem_ld(uint32_t taddr, float (&v)[MT]) {
-  uint32_t r[MT];
-  if constexpr (MT == 1) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r[0]) : "r"(taddr));
-  } else if constexpr (MT == 2) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];"
-                 : "=r"(r[0]), "=r"(r[1])
-                 : "r"(taddr));
-  } else if constexpr (MT == 4) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(taddr));
-  } else {
-    static_assert(MT == 8, "MT must be 1, 2, 4 or 8");
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-          "=r"(r[7])
-        : "r"(taddr));
-  }
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < MT; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                        uint32_t idesc, bool accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
-      : "memory");
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          smem_addr(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_relaxed(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar))
-               : "memory");
-}
-
-// Shared-memory matrix descriptor, no swizzle, K-major (sm_100 format, version 1).
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
-  return static_cast<uint64_t>((addr >> 4) & 0x3FFF) |
-         (static_cast<uint64_t>((lbo >> 4) & 0x3FFF) << 16) |
-         (static_cast<uint64_t>((sbo >> 4) & 0x3FFF) << 32) | (static_cast<uint64_t>(1) << 46);
-}
-
 template <int MT>
 __global__ void __launch_bounds__(kThreads, 2)
     tc_gemv_kernel(GemvArgs a, TcPlan p, const __grid_constant__ WeightMaps maps) {
@@ -199,12 +130,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
   if (warp == 0) {
     // TMEM before the dependents trigger: a next-kernel CTA must never hold TMEM this CTA needs.
-    asm volatile(
-        "tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-            smem_addr(tmem_slot)),
-        "r"(kTmemCols)
-        : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    tmem_alloc(tmem_slot, kTmemCols);
   }
   tc_fence_before();
   __syncthreads();
@@ -392,7 +318,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           }
           tmem_st16(a_addr + 16 * c4, v);
         }
-        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tmem_wait_st();
         tc_fence_before();
         mbar_arrive_relaxed(&bars[kBarA + buf]);
         if (issuer && ok && !mbar_wait_bounded(&bars[kBarA + buf], (it >> 1) & 1)) {
@@ -437,9 +363,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
   if (warp == 0) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(kTmemCols)
-                 : "memory");
+    tmem_dealloc(tmem, kTmemCols);
   }
 }
 

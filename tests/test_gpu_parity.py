@@ -24,13 +24,16 @@ KERNELS = [
     ("vectorized", {"threads_per_block": 64, "rows_per_warp": 4}),
     ("w4a16", {}),
 ]
-FAST = ["stripe_mma", "stream_mma", "tcgen05", "mma_pipeline"]
+FAST = ["stripe_mma", "tc_dequant", "stream_mma", "tcgen05", "mma_pipeline"]
 
 
 def expected_kernel(m, k, g=128, n=8192):
     """The kernel int4gemv_w4a16 picks on the fast path's shapes: stripe_mma for M <= 2 and K a
     multiple of 2048 when x (permuted, per-item padded), its tables and three 34 KB stripes fit in
-    227 KB of shared memory; stream_mma for the rest (M <= 32, K a multiple of 1024)."""
+    227 KB of shared memory; tc_dequant for 9 <= M <= 64; stream_mma for the rest (M <= 32, K a
+    multiple of 1024)."""
+    if 9 <= m <= 64 and g == 128 and k % 1024 == 0:
+        return "tc_dequant"
     if m > 2 or k % 2048 or g != 128:
         return "stream_mma"
     units = (n + 3) // 4
@@ -152,8 +155,8 @@ def test_each_fast_kernel(m, n, k, g):
 
 
 def test_fast_kernel_coverage():
-    """stream_mma takes every BASELINE shape (stripe_mma those with M <= 2); mma_pipeline takes
-    group 32 / 64."""
+    """stream_mma and tc_dequant take every BASELINE shape (stripe_mma those with M <= 2);
+    mma_pipeline takes group 32 / 64."""
     x, q, s, z = cuda(*oracle.synthetic(1, 256, 8192, 128))
     assert [k for k, _ in fast_kernels_for([x, q, s, z], 128)] == FAST
     x, q, s, z = cuda(*oracle.synthetic(2, 256, 1024, 32))
@@ -208,9 +211,73 @@ def test_stripe_mma_rejects():
             ops.w4a16_with(*args, 128, "stripe_mma")
 
 
+# tc_dequant edge cases: N not a multiple of the 128-row tile (rows past N read as zeros), a single
+# tile shared by many CTAs (K large, N small: up to 112 contributors per tile), ranges that cover
+# whole tiles, every accumulator width (M rounded up to 16, 32, 48, 64) with partly filled rows of
+# x, K from one 1024-weight block to 28672, and N beyond 148 tiles.
+TD = [
+    (1, 1, 1024), (9, 37, 1024), (16, 100, 28672), (17, 128, 1024), (24, 129, 2048),
+    (32, 148 * 128 + 3, 1024), (33, 1000, 4096), (48, 300, 3072), (64, 4096, 2048),
+    (64, 129, 8192), (40, 8192, 8192), (12, 28672, 8192), (20, 4096, 14336), (10, 14336, 4096),
+    (2, 148 * 128 * 2 + 77, 2048), (63, 3000, 5120),
+]
+
+
+@pytest.mark.parametrize("m,n,k", TD, ids=[f"m{m}_n{n}_k{k}" for m, n, k in TD])
+def test_tc_dequant_shapes(m, n, k):
+    x, q, s, z = oracle.synthetic(m, n, k, 128, seed=17 * m + n + k)
+    args = cuda(x, q, s, z)
+    assert ops.w4a16_kernel(*args, 128) == expected_kernel(m, k, n=n)
+    y = ops.w4a16_with(*args, 128, "tc_dequant")
+    torch.cuda.synchronize()
+    assert_close(y, oracle.reference(x, q, s, z, 128), f"tc_dequant {m}x{n}x{k}")
+    y2 = ops.w4a16_with(*args, 128, "tc_dequant")
+    torch.cuda.synchronize()
+    assert torch.equal(y, y2), "tc_dequant must be deterministic (fixed-order split-K sums)"
+
+
+def test_tc_dequant_rejects():
+    """Shapes tc_dequant does not take raise a clear error when it is asked for by name."""
+    for m, k, g, why in ((65, 1024, 128, r"M must be in \[1, 64\]"),
+                         (4, 1536, 128, "K must be a positive multiple of 1024"),
+                         (4, 1024, 64, "group_size must be 128")):
+        args = cuda(*oracle.synthetic(m, 64, k, g))
+        with pytest.raises(RuntimeError, match=why):
+            ops.w4a16_with(*args, g, "tc_dequant")
+
+
+def test_tc_dequant_two_streams():
+    """tc_dequant's split-K partial sums and tile counters live in static device memory; calls
+    issued on two streams without any synchronisation between them are ordered by the library
+    (an event between the streams), so every result stays correct."""
+    m, n, k = 16, 4096, 4096
+    sets = [oracle.synthetic(m, n, k, 128, seed=300 + i) for i in range(6)]
+    dev = [cuda(*st) for st in sets]
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    torch.cuda.synchronize()
+    outs = []
+    for i, args in enumerate(dev):
+        with torch.cuda.stream(streams[i % 2]):
+            outs.append(ops.w4a16_with(*args, 128, "tc_dequant"))
+    torch.cuda.synchronize()
+    for i, (x, q, s, z) in enumerate(sets):
+        assert_close(outs[i], oracle.reference(x, q, s, z, 128), f"call {i}")
+
+
+@pytest.mark.parametrize("m,n,k", [(9, 1000, 2048), (16, 4096, 8192), (64, 300, 1024)])
+def test_w4a16_f32_tc_dequant(m, n, k):
+    """The fp32 row sums (the K-split partials of a sharded layer) through tc_dequant."""
+    x, q, s, z = oracle.synthetic(m, n, k, 128, seed=5 + m)
+    y = ops.w4a16_f32(*cuda(x, q, s, z), 128)
+    torch.cuda.synchronize()
+    assert y.dtype == torch.float32
+    assert_close(y.cpu().numpy(), oracle.reference(x, q, s, z, 128), f"w4a16_f32 M={m}")
+
+
 @pytest.mark.parametrize("kern,m", [("stripe_mma", 1), ("stripe_mma", 2), ("stream_mma", 1),
                                     ("stream_mma", 2), ("stream_mma", 8), ("stream_mma", 16),
-                                    ("tcgen05", 1)])
+                                    ("tcgen05", 1), ("tc_dequant", 1), ("tc_dequant", 16),
+                                    ("tc_dequant", 40)])
 def test_repeated_calls_weights_in_l2(kern, m):
     """The same weights (34 MB, resident in the 126 MB L2 after the first call) in eight calls in a
     row: every ring refill then lands within a few hundred nanoseconds, so a stage released before
@@ -232,7 +299,8 @@ def test_strict_weights_after_in_place_requantise():
 
     lib = capi.lib()
     for m, k, kern in ((1, 4096, "stripe_mma"), (2, 4096, "stripe_mma"), (3, 4096, "stream_mma"),
-                       (12, 2048, "stream_mma"), (1, 1024, "tcgen05")):
+                       (12, 2048, "stream_mma"), (1, 1024, "tcgen05"), (16, 2048, "tc_dequant"),
+                       (33, 1024, "tc_dequant")):
         n = 2048
         gen = torch.Generator(device="cuda").manual_seed(m * k)
         w0 = torch.randn(n, k, generator=gen, device="cuda") * 0.02
@@ -324,7 +392,7 @@ def test_misaligned_inputs():
         run("vectorized", {}, args, 128)
 
 
-@pytest.mark.parametrize("m", [1, 4])
+@pytest.mark.parametrize("m", [1, 4, 16, 40])
 def test_deterministic(m):
     x, q, s, z = oracle.synthetic(m, 8192, 8192, 128, seed=11)
     args = cuda(x, q, s, z)
@@ -436,10 +504,11 @@ def test_silu_mul_rejects():
 
 
 # Fused bias / residual epilogue: y = x @ W^T + bias + residual, rounded to fp16 once, on every
-# kernel the dispatcher can pick (the shapes below reach stripe_mma, stream_mma, mma_pipeline,
-# vectorized and coalesced).
+# kernel the dispatcher can pick (the shapes below reach stripe_mma, tc_dequant, stream_mma,
+# mma_pipeline, vectorized and coalesced).
 BIAS = [(1, 8192, 8192, 128, "stripe_mma"), (2, 1000, 4096, 128, "stripe_mma"),
-        (5, 300, 1024, 128, "stream_mma"),
+        (5, 300, 1024, 128, "stream_mma"), (16, 1000, 2048, 128, "tc_dequant"),
+        (40, 300, 1024, 128, "tc_dequant"),
         (3, 257, 768, 64, "mma_pipeline"), (2, 100, 640, 128, "vectorized"),
         (4, 77, 96, 16, "coalesced")]
 
