@@ -714,15 +714,17 @@ def run_ours(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
-SWEEP = ([(m, 8192, 8192) for m in (1, 2, 4, 8, 16, 32)]
-         + [(1, 4096, 4096), (1, 14336, 4096), (1, 4096, 14336), (1, 28672, 8192),
-            (1, 8192, 28672), (8, 28672, 8192), (8, 8192, 28672)])
+SWEEP = ([(m, 8192, 8192) for m in (1, 2, 4, 8, 16, 32, 64)]
+         + [(1, 4096, 4096), (1, 14336, 4096), (1, 4096, 14336), (16, 14336, 4096),
+            (16, 4096, 14336), (1, 28672, 8192), (1, 8192, 28672), (8, 28672, 8192),
+            (8, 8192, 28672), (16, 28672, 8192)])
 
 
-# The shapes of the default line's "sweep" key: BASELINE's M sweep at 8192 x 8192 and the M = 1
-# shapes of the other single-GPU configs.
-SWEEP_DEFAULT = ([(m, 8192, 8192) for m in (1, 2, 4, 8, 16, 32)]
-                 + [(1, 4096, 4096), (1, 14336, 4096), (1, 4096, 14336)])
+# The shapes of the default line's "sweep" key: BASELINE's M sweep at 8192 x 8192 (plus M = 64),
+# the M = 1 shapes of the other single-GPU configs and M = 16 at the two MLP shapes.
+SWEEP_DEFAULT = ([(m, 8192, 8192) for m in (1, 2, 4, 8, 16, 32, 64)]
+                 + [(1, 4096, 4096), (1, 14336, 4096), (1, 4096, 14336), (16, 14336, 4096),
+                    (16, 4096, 14336)])
 
 
 def sweep_one(m: int, n: int, k: int, peak: float, calls_timed: int = 1000) -> dict:
