@@ -558,6 +558,28 @@ def run_reference_arm(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def time_stream_ceiling(sets, n_sets: int, bytes_call: int) -> dict:
+    """int4gemv_stripe_load_only back to back over the weight rotation: how fast the stripe stream
+    alone moves the call's bytes (what the GEMV on top of it could reach)."""
+    from int4gemv import capi
+
+    lib = capi.lib()
+    out = torch.empty(N, dtype=torch.int32, device="cuda")
+
+    def lo(i):
+        q, s, z = sets[i]
+        return lambda: capi.check(lib.int4gemv_stripe_load_only(
+            out.data_ptr(), q.data_ptr(), s.data_ptr(), z.data_ptr(), N, K, GROUP,
+            torch.cuda.current_stream().cuda_stream))
+
+    fns = [lo(i) for i in range(n_sets)]
+    t = time_graph_calls(fns * max(1, 32 // n_sets), 2000, 100)
+    peak = measured_peak()[0]
+    return {"kernel": "stripe_mma loads only (int4gemv_stripe_load_only)",
+            "us": round(t * 1e6, 3), "gb_s": round(bytes_call / t / 1e9, 1),
+            "frac_of_hbm": round(bytes_call / t / 1e9 / peak, 4)}
+
+
 def run_ours(args, world, rank, local):
     from int4gemv import ops
     import torch.nn.functional as F
@@ -627,6 +649,10 @@ def run_ours(args, world, rank, local):
         # ---- our vectorized (the reference-shaped API kernel)
         vv = [(lambda i=i: ops.vectorized(x, *sets[i], GROUP)) for i in range(n_sets)]
         extra["vectorized_us"] = round(time_graph_calls(vv * max(1, 64 // n_sets), 5000, 100) * 1e6, 3)
+        # ---- the loads-only ceiling of the fast path's stream (same tiles, ring, grid and
+        # launch; the arithmetic replaced by an XOR fold, no x), same rotation
+        if kernel == "stripe_mma":
+            extra["stream_ceiling"] = time_stream_ceiling(sets, n_sets, bytes_call)
         extra["quantize"] = time_quantize()
         extra["grouped_qkv"] = time_grouped()
         if not args.no_sweep:

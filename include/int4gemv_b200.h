@@ -99,8 +99,9 @@ int int4gemv_w4a16(void* y, const void* x, const void* qweight, const void* scal
                    void* workspace, int64_t workspace_bytes, void* stream);
 
 /* Name of the kernel int4gemv_w4a16 picks for this shape and these pointers ("stripe_mma" for
- * M <= 2, "tc_dequant" for 9 <= M <= 64, "stream_mma" otherwise up to M = 32 when group_size is 128
- * and K a multiple of 1024; "mma_pipeline", "vectorized", "coalesced" for the other shapes); for
+ * M <= 4 when K is a multiple of 2048 and x fits in its shared memory, "tc_dequant" for
+ * 9 <= M <= 64, "stream_mma" otherwise up to M = 32 when group_size is 128 and K a multiple of
+ * 1024; "mma_pipeline", "vectorized", "coalesced" for the other shapes); for
  * tests and the benchmark. Static storage.
  *
  * tc_dequant keeps split-K partial sums and per-tile counters in static device memory, so two of
@@ -112,6 +113,17 @@ int int4gemv_w4a16(void* y, const void* x, const void* qweight, const void* scal
 const char* int4gemv_w4a16_kernel_name(const void* x, const void* qweight, const void* scales,
                                        const void* zeros, int64_t m, int64_t n, int64_t k,
                                        int64_t group_size);
+
+/* The loads-only ceiling of the M <= 4 fast path (new; the reference's load_only above is the
+ * same idea for its SIMT kernel, csrc/w4a16.h:45-47): the stripe_mma weight stream (2-D TMA tiles,
+ * the same ring, grid and launch) with the arithmetic replaced by a fold, no x. out is uint32 [N];
+ * out[r] is the XOR of every 32-bit word of qweight row r and, for each group of the row, of
+ * (scale bits | zero bits << 16). Needs group_size 128, K a multiple of 2048, 16-byte aligned
+ * qweight, scales and zeros; INT4GEMV_ERR_INVALID with the reason otherwise. For measuring how
+ * close the GEMV comes to the stream it rides on. */
+int int4gemv_stripe_load_only(void* out, const void* qweight, const void* scales,
+                              const void* zeros, int64_t n, int64_t k, int64_t group_size,
+                              void* stream);
 
 /* Runs one named kernel instead of the automatic choice: "stripe_mma", "tc_dequant",
  * "stream_mma", "tcgen05", "mma_pipeline", "vectorized" (128 threads, 2 rows per warp),
@@ -156,10 +168,10 @@ int int4gemv_w4a16_grouped(int count, void* const* ys, const int64_t* ns, const 
 
 /* y [M, N] fp32 = x @ W^T, the fp32 row sums themselves with no rounding to fp16: the local partial
  * sums of a layer split along K over several GPUs, which are added across ranks and rounded to
- * fp16 once (int4gemv/sharded.py). Same inputs and checks as int4gemv_w4a16; needs the fast path's
- * shapes (group_size 128, K a multiple of 1024, M <= 64 (stream_mma below M = 9, tc_dequant from
- * there), 16-byte aligned x, qweight, scales, zeros), INT4GEMV_ERR_INVALID with the reason
- * otherwise. New: the reference returns fp16 only. */
+ * fp16 once (int4gemv/sharded.py). Same inputs and checks as int4gemv_w4a16, any shape they
+ * accept: on the fast path's shapes (group_size 128, K a multiple of 1024, M <= 64) stream_mma or
+ * tc_dequant, otherwise the SIMT kernels (vectorized when group_size % 32 == 0 and x, qweight are
+ * 16-byte aligned, else coalesced). New: the reference returns fp16 only. */
 int int4gemv_w4a16_f32(void* y, const void* x, const void* qweight, const void* scales,
                        const void* zeros, int64_t m, int64_t n, int64_t k, int64_t group_size,
                        void* stream);

@@ -318,6 +318,26 @@ int int4gemv_load_only(void* out, const void* x, const void* qweight, const void
                                              static_cast<int>(rows_per_warp), st));
 }
 
+int int4gemv_stripe_load_only(void* out, const void* qweight, const void* scales,
+                              const void* zeros, int64_t n, int64_t k, int64_t group_size,
+                              void* stream) {
+  const char* name = "stripe_load_only";
+  if (int e = check_sizes(name, 1, n, k, group_size)) return e;
+  if (n > 0 && k > 0 && (!out || !qweight || !scales || !zeros)) {
+    return fail(INT4GEMV_ERR_INVALID, "%s: null pointer", name);
+  }
+  const auto st = static_cast<cudaStream_t>(stream);
+  if (n == 0) return ok();
+  if (k == 0) {
+    const cudaError_t err = cudaMemsetAsync(out, 0, static_cast<size_t>(n * 4), st);
+    return err == cudaSuccess ? ok() : cuda_fail(name, err);
+  }
+  const i4::GemvArgs a = make_args(nullptr, nullptr, qweight, scales, zeros, 1, n, k, group_size);
+  const char* why = "unsupported shape";
+  if (!i4::stripe_mma_supported(a, &why)) return fail(INT4GEMV_ERR_INVALID, "%s: %s", name, why);
+  return launched(name, i4::launch_stripe_load_only(static_cast<uint32_t*>(out), a, st));
+}
+
 int int4gemv_kernel_info(const char* kernel, int64_t m, int64_t threads_per_block,
                          int64_t rows_per_warp, int64_t* info) {
   if (!kernel || !info) return fail(INT4GEMV_ERR_INVALID, "kernel_info: null argument");
@@ -332,7 +352,7 @@ int int4gemv_kernel_info(const char* kernel, int64_t m, int64_t threads_per_bloc
   } else if (std::strcmp(kernel, "naive") == 0 || std::strcmp(kernel, "coalesced") == 0) {
     err = i4::simt_attrs(kernel, static_cast<int>(m), 0, 1, &at);
   } else if (std::strcmp(kernel, "w4a16") == 0) {
-    err = m <= 2                ? i4::stripe_mma_attrs(static_cast<int>(m), &at)
+    err = m <= 4                ? i4::stripe_mma_attrs(static_cast<int>(m), &at)
           : m < kTcDequantMinM  ? i4::stream_mma_attrs(static_cast<int>(m), &at)
           : m <= 64             ? i4::tc_dequant_attrs(static_cast<int>(m), &at)
                                 : i4::mma_pipeline_attrs(16, &at);
@@ -562,12 +582,18 @@ int int4gemv_w4a16_f32(void* y, const void* x, const void* qweight, const void* 
   }
   i4::GemvArgs a = make_args(y, x, qweight, scales, zeros, m, n, k, group_size);
   a.epilogue = i4::kStoreF32;
-  const char* why = "unsupported shape";
   if (a.m >= kTcDequantMinM && i4::tc_dequant_supported(a, nullptr)) {
     return launched(name, i4::launch_tc_dequant(a, st, strict_weights()));
   }
-  if (!i4::stream_mma_supported(a, &why)) return fail(INT4GEMV_ERR_INVALID, "%s: %s", name, why);
-  return launched(name, i4::launch_stream_mma(a, st, strict_weights()));
+  if (i4::stream_mma_supported(a, nullptr)) {
+    return launched(name, i4::launch_stream_mma(a, st, strict_weights()));
+  }
+  // any other shape (e.g. a K shard that is not a multiple of 1024): the SIMT kernels
+  if (a.group % 32 == 0 && reinterpret_cast<uintptr_t>(a.x) % 16 == 0 &&
+      reinterpret_cast<uintptr_t>(a.q) % 16 == 0) {
+    return launched(name, i4::launch_vectorized(a, 128, 2, st));
+  }
+  return launched(name, i4::launch_coalesced(a, st));
 }
 
 int int4gemv_unpack(void* q, const void* qweight, int64_t n, int64_t k, void* stream) {

@@ -66,7 +66,7 @@ struct GemvArgs {
   const half* s;       // [n, k / group]
   const half* z;       // [n, k / group]
   int m, n, k, group;
-  int epilogue = kStoreY;  // only stream_mma implements kSiluMul
+  int epilogue = kStoreY;  // kSiluMul etc.: stream_mma; kStoreF32: stream_mma, tc_dequant, SIMT
   // kStoreY only, each optional: y[m, r] = sum + bias[r] + residual[m, r], rounded to fp16 once.
   // residual may be y itself (each output is read and written by the same thread).
   const half* bias = nullptr;      // [n]
@@ -122,11 +122,15 @@ cudaError_t launch_stream_mma(const GemvArgs& a, cudaStream_t stream, bool stric
 int64_t stream_mma_workspace_bytes(const GemvArgs& a);
 cudaError_t stream_mma_attrs(int m, KernelAttrs* out);
 
-// Stripe-fed mma.sync GEMV for M <= 2, group 128, K % 2048 == 0 (stripe_mma.cu): 2-D TMA tiles of
+// Stripe-fed mma.sync GEMV for M <= 4, group 128, K % 2048 == 0 (stripe_mma.cu): 2-D TMA tiles of
 // 32 rows x 2048 weights, the whole ring issued before the dependency wait unless strict.
 bool stripe_mma_supported(const GemvArgs& a, const char** why);
 cudaError_t launch_stripe_mma(const GemvArgs& a, cudaStream_t stream, bool strict);
 cudaError_t stripe_mma_attrs(int m, KernelAttrs* out);
+// The loads-only ceiling of the stripe stream (M = 1 plan, no x, no MMA): out[row] = XOR of the
+// row's packed words and of (scale bits | zero bits << 16) of each of its groups. a.y, a.x and
+// a.m are ignored.
+cudaError_t launch_stripe_load_only(uint32_t* out, const GemvArgs& a, cudaStream_t stream);
 
 // tcgen05 GEMV for M <= 64, group 128, K % 1024 == 0 (tc_dequant.cu): weights dequantized into
 // TMEM, one accumulator per 128-row tile, stream-K split over the SMs with a fixed-order reduction

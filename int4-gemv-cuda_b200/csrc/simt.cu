@@ -36,7 +36,11 @@ __device__ __forceinline__ void store_tile(const GemvArgs& a, const float (&acc)
 #pragma unroll
   for (int i = 0; i < TM; ++i) {
     if (m0 + i < a.m) {
-      a.y[static_cast<int64_t>(m0 + i) * a.n + row] = store_value(a, m0 + i, row, acc[i]);
+      if (a.epilogue == kStoreF32) {  // the fp32 row sums (int4gemv_w4a16_f32)
+        reinterpret_cast<float*>(a.y)[static_cast<int64_t>(m0 + i) * a.n + row] = acc[i];
+      } else {
+        a.y[static_cast<int64_t>(m0 + i) * a.n + row] = store_value(a, m0 + i, row, acc[i]);
+      }
     }
   }
 }

@@ -1,4 +1,4 @@
-// The B200 fast path for M <= 2: stripes of 32 rows x 2048 weights streamed by TMA into a ring of
+// The B200 fast path for M <= 4: stripes of 32 rows x 2048 weights streamed by TMA into a ring of
 // shared-memory stages, and warp-level tensor-core MMAs (mma.sync m16n8k16, f16 x f16 -> f32) on
 // the nibbles unpacked in registers.
 //
@@ -19,12 +19,14 @@
 // bq[item][granule][m] = the sum of the B values of each 4-word granule, and xs[item][m] = the sum
 // of the item's x.
 //
-// Math side. Sixteen consumer warps. Warp w takes items 4 (w % 4) .. + 3 of every stripe and one
-// word granule (4 words) of each; lane (g, c) takes item 4 (w % 4) + c ("narrow" layout: the eight
-// MMA columns are four items x two rows of x, and lane c's k-slots hold its own item's words, so
-// one MMA covers 256 weights of four different groups), granule (w / 4 + c / 2) % 4 (rotated so
-// the 16-byte loads of one shared-memory phase hit distinct banks), and rows g, g + 8, 16 + g,
-// 24 + g of the block. Per packed word one shift and four LOP3s give the fp16 A halves 1024 + q
+// Math side. Sixteen consumer warps. For M <= 2 warp w takes items 4 (w % 4) .. + 3 of every
+// stripe and one word granule (4 words) of each; lane (g, c) takes item 4 (w % 4) + c ("narrow"
+// layout: the eight MMA columns are four items x two rows of x, and lane c's k-slots hold its own
+// item's words, so one MMA covers 256 weights of four different groups), granule (w / 4 + c / 2)
+// % 4 (rotated so the 16-byte loads of one shared-memory phase hit distinct banks), and rows g,
+// g + 8, 16 + g, 24 + g of the block. For M = 3 or 4 the eight columns are two items x four rows
+// of x: lanes c and c ^ 1 share item 2 (w % 8) + c / 2, each with its own granule 2 (w / 8) + c % 2,
+// and an MMA still covers 256 weights (so M = 4 costs the MMAs of M = 1). Per packed word one shift and four LOP3s give the fp16 A halves 1024 + q
 // and 1024 + 16 q exactly; the B registers of a word are reused for both 16-row tiles. Each tile's
 // low-half MMA chain starts from C = -1024 * (sum of the B values of the granule), which removes
 // the magic-number offset inside the tensor core, so after the stripe the accumulators hold
@@ -184,14 +186,14 @@ __device__ __forceinline__ void stripe_produce(const StripePlan& p, const Stripe
 // x -> the permuted B layout and the two tables (see the file comment). Thread t handles blocks
 // (8 weights of one row of x) 2 t and 2 t + 1 of each 2 x NT-block step; a thread pair
 // covers one 4-word granule, eight threads one item.
-template <int NT>
+template <int NT, int TS>
 __device__ __forceinline__ void stripe_prepare_x(const GemvArgs& a, const StripePlan& p,
                                                  unsigned char* smem, int tid) {
   const int kw_per_m = a.k / 8;
   const int total = a.m * kw_per_m;
   unsigned char* xs = smem + p.off_xs;
-  float* bq = reinterpret_cast<float*>(smem + p.off_bq);    // [items][4][2]
-  float* xsum = reinterpret_cast<float*>(smem + p.off_xsum);  // [items][2]
+  float* bq = reinterpret_cast<float*>(smem + p.off_bq);    // [items][4][TS]
+  float* xsum = reinterpret_cast<float*>(smem + p.off_xsum);  // [items][TS]
   for (int base = 0; base < total; base += 4 * NT) {
     // Two steps per round: all four 16-byte loads are in flight together.
     uint4 v[4];
@@ -227,13 +229,16 @@ __device__ __forceinline__ void stripe_prepare_x(const GemvArgs& a, const Stripe
       xsm += __shfl_xor_sync(0xffffffffu, xsm, 4);  // the item (16 words) of eight threads
       if (valid) {
         const int item = kw >> 4, gran = (kw >> 2) & 3;
+        // the columns of rows a.m .. TS - 1 of x (absent) hold zeros
         if ((tid & 1) == 0) {
-          bq[(item * 4 + gran) * 2 + m] = -1024.0f * bsum;
-          if (a.m == 1) bq[(item * 4 + gran) * 2 + 1] = 0.0f;
+          bq[(item * 4 + gran) * TS + m] = -1024.0f * bsum;
+          if (m == 0)
+            for (int mm = a.m; mm < TS; ++mm) bq[(item * 4 + gran) * TS + mm] = 0.0f;
         }
         if ((tid & 7) == 0) {
-          xsum[item * 2 + m] = xsm;
-          if (a.m == 1) xsum[item * 2 + 1] = 0.0f;
+          xsum[item * TS + m] = xsm;
+          if (m == 0)
+            for (int mm = a.m; mm < TS; ++mm) xsum[item * TS + mm] = 0.0f;
         }
       }
     }
@@ -276,10 +281,13 @@ __device__ __forceinline__ void stripe_load(const unsigned char* st, const int (
   }
 }
 
-template <int GPW>
+// TS: columns of the tables. With TS = 4 (the MC = 4 layout, one granule per lane) the lane's D
+// columns also take the B values of its partner lane (c ^ 1), whose granule is gran ^ 1; m0 is
+// the first of the lane's two rows of x.
+template <int GPW, int TS>
 __device__ __forceinline__ void stripe_load_x(const unsigned char* const (&b_base)[GPW], int b_step,
                                               const float* bq, const float* xsum, int j, int item,
-                                              const int (&gran)[GPW], bool zero_term,
+                                              const int (&gran)[GPW], int m0, bool zero_term,
                                               StripeX<GPW>& x) {
   const int tab = j * kSxItems + item;
   float2 ci = make_float2(0.0f, 0.0f);
@@ -288,12 +296,18 @@ __device__ __forceinline__ void stripe_load_x(const unsigned char* const (&b_bas
     const unsigned char* bsrc = b_base[q] + j * b_step;
 #pragma unroll
     for (int u = 0; u < 4; ++u) x.bx[q][u] = *reinterpret_cast<const uint4*>(bsrc + u * 16);
-    const float2 v = *reinterpret_cast<const float2*>(bq + (tab * 4 + gran[q]) * 2);
+    const float2 v = *reinterpret_cast<const float2*>(bq + (tab * 4 + gran[q]) * TS + m0);
     ci.x += v.x;
     ci.y += v.y;
+    if constexpr (TS == 4) {
+      const float2 w = *reinterpret_cast<const float2*>(bq + (tab * 4 + (gran[q] ^ 1)) * TS + m0);
+      ci.x += w.x;
+      ci.y += w.y;
+    }
   }
   x.cinit = ci;
-  x.xsm = zero_term ? *reinterpret_cast<const float2*>(xsum + tab * 2) : make_float2(0.0f, 0.0f);
+  x.xsm = zero_term ? *reinterpret_cast<const float2*>(xsum + tab * TS + m0)
+                    : make_float2(0.0f, 0.0f);
 }
 
 // The stage's 16 GPW MMAs: per tile and granule a low-half and a high-half chain over the
@@ -346,10 +360,11 @@ __device__ __forceinline__ void stripe_mma(const StripeRegs<GPW>& r, const Strip
 }
 
 // One scale per (row, item) into the row accumulators; the granule-0 warps add the zero term.
-template <int MC, int GPW, int NT>
+// E: the lane's D columns that hold rows of x (1 for M = 1, else 2).
+template <int E, int GPW, int NT>
 __device__ __forceinline__ void stripe_epilogue(const StripeRegs<GPW>& r, const float (&d)[2][4],
                                                 float2 xsm, bool zero_term,
-                                                float (&acc)[2][2][MC]) {
+                                                float (&acc)[2][2][E]) {
 #pragma unroll
   for (int t = 0; t < NT; ++t) {
 #pragma unroll
@@ -358,7 +373,7 @@ __device__ __forceinline__ void stripe_epilogue(const StripeRegs<GPW>& r, const 
       const float z =
           zero_term ? __half2float(__ushort_as_half(static_cast<uint16_t>(r.zb[t][h]))) : 0.0f;
 #pragma unroll
-      for (int m = 0; m < MC; ++m) {
+      for (int m = 0; m < E; ++m) {
         const float xz = m == 0 ? xsm.x : xsm.y;
         acc[t][h][m] = fmaf(s, fmaf(-z, xz, d[t][2 * h + m]), acc[t][h][m]);
       }
@@ -366,13 +381,19 @@ __device__ __forceinline__ void stripe_epilogue(const StripeRegs<GPW>& r, const 
   }
 }
 
-// MC: rows of x (1 or 2). CW: consumer warps, 16 (one 4-word granule per lane and stage) or 8
-// (two); plus one producer warp.
-template <int MC, int CW>
+// MC: columns per group in the MMA's eight (1 or 2: four groups per MMA; 4 for M = 3 or 4: two
+// groups, each over the k-slots of a lane pair). CW: consumer warps, 16 (one 4-word granule per
+// lane and stage) or 8 (two; MC <= 2 only); plus one producer warp. LO: the loads-only ceiling of the same stream (no x, no MMA):
+// every packed word and, once per (row, group), the scale and zero bits are XOR-folded into one
+// 32-bit word per row, written to ((uint32_t*) a.y)[row].
+template <int MC, int CW, bool LO = false>
 __global__ void __launch_bounds__((CW + 1) * kWarp, 1)
     stripe_mma_kernel(GemvArgs a, StripePlan p, const __grid_constant__ StripeMaps maps) {
   constexpr int kGPW = 16 / CW;            // granules per lane and stage
   constexpr int kConsumers = CW * kWarp;
+  constexpr int kTS = MC <= 2 ? 2 : 4;     // columns of the x tables
+  constexpr int kE = MC == 1 ? 1 : 2;      // the lane's D columns that hold rows of x
+  static_assert(MC != 4 || CW == 16, "the MC = 4 layout takes one granule per lane");
   extern __shared__ __align__(1024) unsigned char smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + kSxMaxStages;
@@ -409,15 +430,25 @@ __global__ void __launch_bounds__((CW + 1) * kWarp, 1)
 
   // ---------------- consumers ----------------
   grid_dependency_wait();  // x may come from the previous kernel in the stream
-  stripe_prepare_x<kConsumers>(a, p, smem, tid);
-  named_barrier(kSxBarrier, kConsumers);
+  if constexpr (!LO) {
+    stripe_prepare_x<kConsumers, kTS>(a, p, smem, tid);
+    named_barrier(kSxBarrier, kConsumers);
+  }
 
   const int g = lane >> 2, c = lane & 3;
-  const int iq = warp & 3, wq = warp >> 2;     // item quad; granule set (kGPW granules each)
-  const int item = 4 * iq + c;                 // item of this lane within a stripe
-  const bool zero_term = wq == 0;              // these warps add the zero term of their items
-  const int xm = g - 2 * c;                    // the row of x whose B values this lane holds
-  const bool has_x = xm >= 0 && xm < MC;
+  // MC <= 2: lane c takes item 4 (w % 4) + c (column pair c), granule set w / 4 (kGPW granules);
+  //   column g is (item g / 2, row of x g % 2).
+  // MC = 4: lanes c and c ^ 1 take item 2 (w % 8) + c / 2 (columns 4 (c / 2) .. + 3), with the
+  //   granules 2 (w / 8) + c % 2; column g is (item g / 4, row of x g % 4), and the lane's D
+  //   columns 2c, 2c + 1 are rows m0 = 2 (c % 2) and m0 + 1 of its item.
+  // A k-slot's word depends on c only (never on g): B column g is supplied by the lanes of row g.
+  const int iq = MC == 4 ? (warp & 7) : (warp & 3);
+  const int wq = MC == 4 ? (warp >> 3) : (warp >> 2);
+  const int item = MC == 4 ? 2 * iq + (c >> 1) : 4 * iq + c;  // item of this lane in a stripe
+  const bool zero_term = wq == 0;  // the warps holding granule 0 of their items add the zero term
+  const int xm = MC == 4 ? (g & 3) : g - 2 * c;  // the row of x whose B values this lane holds
+  const bool has_x = MC == 4 ? ((g >> 2) == (c >> 1) && xm < a.m) : (xm >= 0 && xm < MC);
+  const int m0 = MC == 4 ? 2 * (c & 1) : 0;
   const unsigned char* xs = smem + p.off_xs;
   const float* bq = reinterpret_cast<const float*>(smem + p.off_bq);
   const float* xsum = reinterpret_cast<const float*>(smem + p.off_xsum);
@@ -425,8 +456,9 @@ __global__ void __launch_bounds__((CW + 1) * kWarp, 1)
   const unsigned char* b_base[kGPW];
 #pragma unroll
   for (int q = 0; q < kGPW; ++q) {
-    // granules rotated by c / 2 so the 16-byte loads of one shared-memory phase hit distinct banks
-    gran[q] = (kGPW * wq + q + (c >> 1)) & 3;
+    // MC <= 2: granules rotated by c / 2 so the 16-byte loads of one shared-memory phase hit
+    // distinct banks
+    gran[q] = MC == 4 ? 2 * wq + (c & 1) : (kGPW * wq + q + (c >> 1)) & 3;
     a_off[q] = g * kSxRowBytes + item * 64 + gran[q] * 16;
     b_base[q] = has_x ? xs + xm * p.xs_stride + item * kSxItemBytes + gran[q] * 64
                       : smem + kSxZeroOff;
@@ -442,22 +474,53 @@ __global__ void __launch_bounds__((CW + 1) * kWarp, 1)
   // One block of rows: NT 16-row tiles (2, or 1 when the block has at most 16 rows), a
   // compile-time count so the two tiles' MMAs interleave freely.
   auto run_block = [&]<int NT>(int blk, int rows_b) {
-    float acc[2][2][MC];  // [tile][row g / g + 8][m]
+    if constexpr (LO) {
+      uint32_t f[2][2] = {{0u, 0u}, {0u, 0u}};  // [tile][row g / g + 8]
+      for (int j = 0; j < p.stripes; ++j) {
+        const int slot = ring.next();
+        StripeRegs<kGPW> r;
+        stripe_load<kGPW, NT>(stages + slot * kSxStageBytes, a_off, s_off, z_off, zero_term, r);
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+#pragma unroll
+            for (int q = 0; q < kGPW; ++q) f[t][h] ^= fold4(r.aw[q][t][h]);
+            if (zero_term) f[t][h] ^= r.sb[t][h] | (r.zb[t][h] << 16);
+          }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);  // after the folds: every load has returned
+      }
+      uint32_t* redu = reinterpret_cast<uint32_t*>(red);
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t v = f[t][h];
+          v ^= __shfl_xor_sync(0xffffffffu, v, 1);
+          v ^= __shfl_xor_sync(0xffffffffu, v, 2);
+          if (c == 0 && 16 * t + 8 * h + g < rows_b) {
+            redu[warp * p.rows_cap + blk * kSxRows + 16 * t + 8 * h + g] = v;
+          }
+        }
+      return;
+    }
+    float acc[2][2][kE];  // [tile][row g / g + 8][row of x m0 + e]
 #pragma unroll
     for (int t = 0; t < 2; ++t)
 #pragma unroll
       for (int h = 0; h < 2; ++h)
 #pragma unroll
-        for (int m = 0; m < MC; ++m) acc[t][h][m] = 0.0f;
+        for (int e = 0; e < kE; ++e) acc[t][h][e] = 0.0f;
     for (int j = 0; j < p.stripes; ++j) {
       const int slot = ring.next();
       StripeRegs<kGPW> r;
       stripe_load<kGPW, NT>(stages + slot * kSxStageBytes, a_off, s_off, z_off, zero_term, r);
       StripeX<kGPW> xr;
-      stripe_load_x<kGPW>(b_base, b_step, bq, xsum, j, item, gran, zero_term, xr);
+      stripe_load_x<kGPW, kTS>(b_base, b_step, bq, xsum, j, item, gran, m0, zero_term, xr);
       float d[2][4];
       stripe_mma<kGPW, NT>(r, xr, d);
-      stripe_epilogue<MC, kGPW, NT>(r, d, xr.xsm, zero_term, acc);
+      stripe_epilogue<kE, kGPW, NT>(r, d, xr.xsm, zero_term, acc);
       // Release the stage only after its values have been used: mbarrier.arrive does not wait
       // for shared-memory loads still in flight, and a refill served from L2 can land within a
       // few hundred nanoseconds. (Releasing here measured as fast as releasing right after the
@@ -465,18 +528,19 @@ __global__ void __launch_bounds__((CW + 1) * kWarp, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);  // the stage may be refilled
     }
-    // the four items of this warp's quad, then one partial per (row, m) and warp
+    // the items of this warp (four, or two for MC = 4), then one partial per (row, m) and warp
 #pragma unroll
     for (int t = 0; t < NT; ++t)
 #pragma unroll
       for (int h = 0; h < 2; ++h)
 #pragma unroll
-        for (int m = 0; m < MC; ++m) {
-          float v = acc[t][h][m];
-          v += __shfl_xor_sync(0xffffffffu, v, 1);
+        for (int e = 0; e < kE; ++e) {
+          float v = acc[t][h][e];
+          if constexpr (MC != 4) v += __shfl_xor_sync(0xffffffffu, v, 1);
           v += __shfl_xor_sync(0xffffffffu, v, 2);
-          if (c == 0 && 16 * t + 8 * h + g < rows_b) {
-            red[(warp * p.rows_cap + blk * kSxRows + 16 * t + 8 * h + g) * MC + m] = v;
+          const bool writer = MC == 4 ? c < 2 : c == 0;
+          if (writer && 16 * t + 8 * h + g < rows_b) {
+            red[(warp * p.rows_cap + blk * kSxRows + 16 * t + 8 * h + g) * MC + m0 + e] = v;
           }
         }
   };
@@ -491,7 +555,17 @@ __global__ void __launch_bounds__((CW + 1) * kWarp, 1)
 
   // ---- add the CW partials of every output in a fixed order; store fp16 ---------------------
   named_barrier(kSxBarrier, kConsumers);
-  for (int o = tid; o < rows * MC; o += kConsumers) {
+  if constexpr (LO) {
+    const uint32_t* redu = reinterpret_cast<const uint32_t*>(red);
+    for (int r = tid; r < rows; r += kConsumers) {
+      uint32_t v = 0;
+#pragma unroll
+      for (int w = 0; w < CW; ++w) v ^= redu[w * p.rows_cap + r];
+      if (ring.ok) reinterpret_cast<uint32_t*>(a.y)[row_begin + r] = v;
+    }
+    return;
+  }
+  for (int o = tid; o < rows * a.m; o += kConsumers) {
     const int m = o / rows;
     const int r = o - m * rows;
     float sum = 0.0f;
@@ -510,7 +584,7 @@ bool stripe_plan(const GemvArgs& a, StripePlan* p, const char** why) {
     if (why) *why = reason;
     return false;
   };
-  if (a.m < 1 || a.m > 2) return fail("M must be 1 or 2");
+  if (a.m < 1 || a.m > 4) return fail("M must be in [1, 4]");
   if (a.group != kItemK) return fail("group_size must be 128");
   if (a.k % kSxK != 0) return fail("K must be a multiple of 2048");
   if (a.epilogue != kStoreY) return fail("plain stores only");
@@ -527,12 +601,14 @@ bool stripe_plan(const GemvArgs& a, StripePlan* p, const char** why) {
   int64_t off = kSxHeader;
   p->off_xs = static_cast<int>(off);
   off += static_cast<int64_t>(a.m) * p->xs_stride;
+  const int mc = a.m <= 2 ? a.m : 4;  // the kernel's MC
+  const int ts = a.m <= 2 ? 2 : 4;    // columns of the x tables
   p->off_bq = static_cast<int>(off);
-  off += static_cast<int64_t>(p->items) * 4 * 2 * 4;
+  off += static_cast<int64_t>(p->items) * 4 * ts * 4;
   p->off_xsum = static_cast<int>(off);
-  off += static_cast<int64_t>(p->items) * 2 * 4;
+  off += static_cast<int64_t>(p->items) * ts * 4;
   p->off_red = static_cast<int>(off);
-  off += static_cast<int64_t>(16) * p->rows_cap * a.m * 4;  // partials of up to 16 warps
+  off += static_cast<int64_t>(16) * p->rows_cap * mc * 4;  // partials of up to 16 warps
   off = (off + 1023) / 1024 * 1024;
   p->off_stage = static_cast<int>(off);
   if (off >= kSxSmemLimit) return fail("x does not fit in shared memory");
@@ -628,10 +704,11 @@ cudaError_t stripe_maps_for(const GemvArgs& a, StripeMaps* out) {
 template <typename F>
 cudaError_t with_stripe_m(int m, F&& f) {
   if (m <= 1) return f.template operator()<1, STRIPE_CW>();
-  return f.template operator()<2, STRIPE_CW>();
+  if (m == 2) return f.template operator()<2, STRIPE_CW>();
+  return f.template operator()<4, 16>();
 }
 
-std::once_flag g_stripe_attr_once[2][64];
+std::once_flag g_stripe_attr_once[4][64];
 
 }  // namespace
 
@@ -673,8 +750,45 @@ cudaError_t launch_stripe_mma(const GemvArgs& a, cudaStream_t stream, bool stric
   });
 }
 
+cudaError_t launch_stripe_load_only(uint32_t* out, const GemvArgs& args, cudaStream_t stream) {
+  GemvArgs a = args;
+  a.y = reinterpret_cast<half*>(out);
+  a.x = nullptr;
+  a.m = 1;
+  a.epilogue = kStoreY;
+  StripePlan p;
+  if (!stripe_plan(a, &p, nullptr)) return cudaErrorInvalidValue;
+  p.strict = 0;
+  p.status = device_status_word();
+  if (!p.status) return cudaErrorInvalidSymbol;
+  StripeMaps maps;
+  const cudaError_t merr = stripe_maps_for(a, &maps);
+  if (merr != cudaSuccess) return merr;
+  int dev = 0;
+  const cudaError_t derr = cudaGetDevice(&dev);
+  if (derr != cudaSuccess) return derr;
+  static std::once_flag attr_once[64];
+  cudaError_t result = cudaSuccess;
+  std::call_once(attr_once[dev & 63], [&] {
+    result = cudaFuncSetAttribute(stripe_mma_kernel<1, STRIPE_CW, true>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, kSxSmemLimit);
+  });
+  if (result != cudaSuccess) return result;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.ctas);
+  cfg.blockDim = dim3((STRIPE_CW + 1) * kWarp);
+  cfg.dynamicSmemBytes = p.smem_bytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, stripe_mma_kernel<1, STRIPE_CW, true>, a, p, maps);
+}
+
 cudaError_t stripe_mma_attrs(int m, KernelAttrs* out) {
-  const int mm = m < 1 ? 1 : m > 2 ? 2 : m;
+  const int mm = m < 1 ? 1 : m > 4 ? 4 : m;
   return with_stripe_m(mm, [&]<int MC, int CW>() {
     cudaFuncAttributes fa;
     cudaError_t err = cudaFuncGetAttributes(&fa, stripe_mma_kernel<MC, CW>);

@@ -26,6 +26,7 @@ _PROTOTYPES = {
     "int4gemv_coalesced": (ctypes.c_int, [_p] * 5 + [_i64] * 4 + [_p]),
     "int4gemv_vectorized": (ctypes.c_int, [_p] * 5 + [_i64] * 6 + [_p]),
     "int4gemv_load_only": (ctypes.c_int, [_p] * 5 + [_i64] * 6 + [_p]),
+    "int4gemv_stripe_load_only": (ctypes.c_int, [_p] * 4 + [_i64] * 3 + [_p]),
     "int4gemv_kernel_info": (ctypes.c_int, [ctypes.c_char_p, _i64, _i64, _i64,
                                             ctypes.POINTER(ctypes.c_int64)]),
     "int4gemv_sequential": (ctypes.c_int, [_p] * 5 + [_i64] * 5),

@@ -74,3 +74,34 @@ def test_kernel_info_and_status():
     with pytest.raises(capi.CapiError, match="unknown kernel"):
         capi.kernel_info("bogus", 1)
     assert capi.device_status() == 0
+
+
+def stripe_fold_oracle(q, s, z):
+    """out[r] = XOR of the row's packed words and, per group, of (scale bits | zero bits << 16)."""
+    out = np.bitwise_xor.reduce(q.view(np.uint32), axis=1)
+    sz = s.view(np.uint16).astype(np.uint32) | (z.view(np.uint16).astype(np.uint32) << 16)
+    return out ^ np.bitwise_xor.reduce(sz, axis=1)
+
+
+@pytest.mark.parametrize("n,k", [(8192, 8192), (37, 2048), (148 * 4 + 3, 4096), (1000, 28672),
+                                 (16, 6144)])
+def test_stripe_load_only(n, k):
+    """The loads-only ceiling of the M <= 2 stream folds exactly the bytes the GEMV reads."""
+    _, q, s, z = oracle.synthetic(1, n, k, 128, seed=n + k)
+    tq, ts, tz = dev(q), dev(s), dev(z)
+    out = torch.full((n,), -1, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    for _ in range(2):  # the second call reads weights the first one left in L2
+        capi.call("int4gemv_stripe_load_only", *ptrs(out, tq, ts, tz), n, k, 128, stream)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(out.cpu().numpy().view(np.uint32),
+                                      stripe_fold_oracle(q, s, z))
+    assert capi.device_status() == 0
+
+
+def test_stripe_load_only_rejects():
+    _, q, s, z = oracle.synthetic(1, 64, 3072, 128)
+    tq, ts, tz = dev(q), dev(s), dev(z)
+    out = torch.empty(64, dtype=torch.int32, device="cuda")
+    with pytest.raises(capi.CapiError, match="K must be a multiple of 2048"):
+        capi.call("int4gemv_stripe_load_only", *ptrs(out, tq, ts, tz), 64, 3072, 128, None)

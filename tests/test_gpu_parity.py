@@ -28,19 +28,21 @@ FAST = ["stripe_mma", "tc_dequant", "stream_mma", "tcgen05", "mma_pipeline"]
 
 
 def expected_kernel(m, k, g=128, n=8192):
-    """The kernel int4gemv_w4a16 picks on the fast path's shapes: stripe_mma for M <= 2 and K a
-    multiple of 2048 when x (permuted, per-item padded), its tables and three 34 KB stripes fit in
-    227 KB of shared memory; tc_dequant for 9 <= M <= 64; stream_mma for the rest (M <= 32, K a
-    multiple of 1024)."""
+    """The kernel int4gemv_w4a16 picks on the fast path's shapes: stripe_mma for M <= 4 and K a
+    multiple of 2048 when x (permuted, per-item padded), its tables, the warps' partials and three
+    34 KB stripes fit in 227 KB of shared memory; tc_dequant for 9 <= M <= 64; stream_mma for the
+    rest (M <= 32, K a multiple of 1024)."""
     if 9 <= m <= 64 and g == 128 and k % 1024 == 0:
         return "tc_dequant"
-    if m > 2 or k % 2048 or g != 128:
+    if m > 4 or k % 2048 or g != 128:
         return "stream_mma"
     units = (n + 3) // 4
     rows_cap = 4 * (-(-units // min(torch.cuda.get_device_properties(0).multi_processor_count,
                                     units)))
     items = k // 128
-    off = 1536 + m * items * 272 + items * 40 + 16 * rows_cap * m * 4
+    ts = 2 if m <= 2 else 4  # columns of the x tables
+    mc = m if m <= 2 else 4  # columns of the partials
+    off = 1536 + m * items * 272 + items * 20 * ts + 16 * rows_cap * mc * 4
     off = -(-off // 1024) * 1024
     return "stripe_mma" if (227 * 1024 - off) // 34816 >= 3 else "stream_mma"
 
@@ -185,11 +187,13 @@ def test_stream_mma_shapes(m, n, k):
 
 
 # stripe_mma edge cases: rows per CTA below one 16-row tile, between one and two tiles, several
-# 32-row blocks, N not a multiple of 4, M = 1 and 2, K from one stripe (2048) to 28672.
+# 32-row blocks, N not a multiple of 4, M = 1 to 4 (M = 3 and 4: two groups x four rows of x per
+# MMA, M = 3 with an empty column), K from one stripe (2048) to 28672.
 STRIPE = [
     (1, 1, 2048), (2, 5, 2048), (1, 37, 8192), (2, 148 * 4 + 3, 4096), (1, 148 * 20 + 1, 6144),
     (2, 148 * 24, 2048), (1, 148 * 36 + 2, 10240), (2, 4099, 8192), (1, 1000, 28672),
-    (2, 300, 14336), (1, 28672, 2048),
+    (2, 300, 14336), (1, 28672, 2048), (3, 1, 2048), (4, 37, 8192), (3, 148 * 4 + 3, 4096),
+    (4, 4099, 8192), (3, 8192, 8192), (4, 14336, 4096), (4, 148 * 36 + 2, 6144),
 ]
 
 
@@ -197,7 +201,7 @@ STRIPE = [
 def test_stripe_mma_shapes(m, n, k):
     x, q, s, z = oracle.synthetic(m, n, k, 128, seed=13 * m + n + k)
     args = cuda(x, q, s, z)
-    assert ops.w4a16_kernel(*args, 128) == "stripe_mma"
+    assert ops.w4a16_kernel(*args, 128) == expected_kernel(m, k, n=n)
     y = ops.w4a16_with(*args, 128, "stripe_mma")
     torch.cuda.synchronize()
     assert_close(y, oracle.reference(x, q, s, z, 128), f"stripe_mma {m}x{n}x{k}")
@@ -205,7 +209,7 @@ def test_stripe_mma_shapes(m, n, k):
 
 def test_stripe_mma_rejects():
     """Shapes stripe_mma does not take raise a clear error when it is asked for by name."""
-    for m, k, why in ((3, 2048, "M must be 1 or 2"), (1, 3072, "K must be a multiple of 2048")):
+    for m, k, why in ((5, 2048, r"M must be in \[1, 4\]"), (1, 3072, "K must be a multiple of 2048")):
         args = cuda(*oracle.synthetic(m, 64, k, 128))
         with pytest.raises(RuntimeError, match=why):
             ops.w4a16_with(*args, 128, "stripe_mma")
@@ -264,6 +268,18 @@ def test_tc_dequant_two_streams():
         assert_close(outs[i], oracle.reference(x, q, s, z, 128), f"call {i}")
 
 
+@pytest.mark.parametrize("m,n,k,g", [(1, 2048, 3584, 128), (3, 300, 768, 64), (2, 100, 96, 16),
+                                     (12, 257, 1536, 128)])
+def test_w4a16_f32_any_shape(m, n, k, g):
+    """The fp32 row sums off the fast path's shapes (a K shard of a split layer need not be a
+    multiple of 1024): the SIMT kernels store fp32."""
+    x, q, s, z = oracle.synthetic(m, n, k, g, seed=7 + m + k)
+    y = ops.w4a16_f32(*cuda(x, q, s, z), g)
+    torch.cuda.synchronize()
+    assert y.dtype == torch.float32
+    assert_close(y.cpu().numpy(), oracle.reference(x, q, s, z, g), f"w4a16_f32 {m}x{n}x{k} g{g}")
+
+
 @pytest.mark.parametrize("m,n,k", [(9, 1000, 2048), (16, 4096, 8192), (64, 300, 1024)])
 def test_w4a16_f32_tc_dequant(m, n, k):
     """The fp32 row sums (the K-split partials of a sharded layer) through tc_dequant."""
@@ -274,7 +290,8 @@ def test_w4a16_f32_tc_dequant(m, n, k):
     assert_close(y.cpu().numpy(), oracle.reference(x, q, s, z, 128), f"w4a16_f32 M={m}")
 
 
-@pytest.mark.parametrize("kern,m", [("stripe_mma", 1), ("stripe_mma", 2), ("stream_mma", 1),
+@pytest.mark.parametrize("kern,m", [("stripe_mma", 1), ("stripe_mma", 2), ("stripe_mma", 3),
+                                    ("stripe_mma", 4), ("stream_mma", 1),
                                     ("stream_mma", 2), ("stream_mma", 8), ("stream_mma", 16),
                                     ("tcgen05", 1), ("tc_dequant", 1), ("tc_dequant", 16),
                                     ("tc_dequant", 40)])
@@ -298,7 +315,8 @@ def test_strict_weights_after_in_place_requantise():
     from int4gemv import capi
 
     lib = capi.lib()
-    for m, k, kern in ((1, 4096, "stripe_mma"), (2, 4096, "stripe_mma"), (3, 4096, "stream_mma"),
+    for m, k, kern in ((1, 4096, "stripe_mma"), (2, 4096, "stripe_mma"), (4, 4096, "stripe_mma"),
+                       (3, 4096, "stream_mma"),
                        (12, 2048, "stream_mma"), (1, 1024, "tcgen05"), (16, 2048, "tc_dequant"),
                        (33, 1024, "tc_dequant")):
         n = 2048
@@ -392,7 +410,7 @@ def test_misaligned_inputs():
         run("vectorized", {}, args, 128)
 
 
-@pytest.mark.parametrize("m", [1, 4, 16, 40])
+@pytest.mark.parametrize("m", [1, 3, 4, 16, 40])
 def test_deterministic(m):
     x, q, s, z = oracle.synthetic(m, 8192, 8192, 128, seed=11)
     args = cuda(x, q, s, z)
@@ -507,6 +525,7 @@ def test_silu_mul_rejects():
 # kernel the dispatcher can pick (the shapes below reach stripe_mma, tc_dequant, stream_mma,
 # mma_pipeline, vectorized and coalesced).
 BIAS = [(1, 8192, 8192, 128, "stripe_mma"), (2, 1000, 4096, 128, "stripe_mma"),
+        (4, 1000, 2048, 128, "stripe_mma"),
         (5, 300, 1024, 128, "stream_mma"), (16, 1000, 2048, 128, "tc_dequant"),
         (40, 300, 1024, 128, "tc_dequant"),
         (3, 257, 768, 64, "mma_pipeline"), (2, 100, 640, 128, "vectorized"),
