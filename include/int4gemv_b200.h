@@ -83,9 +83,9 @@ int int4gemv_sequential(void* y, const void* x, const void* qweight, const void*
 
 /* ---- The B200 fast path (new; no counterpart in the reference) ------------------------------- */
 
-/* Bytes of device workspace int4gemv_w4a16 can use for this shape (0 if none): for 5 <= M <= 8 on
- * the fast path's shapes, room for x permuted once per call by a pre-kernel instead of in every
- * CTA. */
+/* Bytes of device workspace int4gemv_w4a16 can use for this shape (0 if none): for the shapes with
+ * 5 <= M <= 8 that go to stream_mma (those stripe_mma does not take), room for x permuted once per
+ * call by a pre-kernel instead of in every CTA. */
 int64_t int4gemv_w4a16_workspace_size(int64_t m, int64_t n, int64_t k, int64_t group_size);
 
 /* y = x @ dequant(W)^T through the fastest kernel for the shape: a persistent, TMA-bulk-fed,
@@ -99,9 +99,9 @@ int int4gemv_w4a16(void* y, const void* x, const void* qweight, const void* scal
                    void* workspace, int64_t workspace_bytes, void* stream);
 
 /* Name of the kernel int4gemv_w4a16 picks for this shape and these pointers ("stripe_mma" for
- * M <= 4 when K is a multiple of 2048 and x fits in its shared memory, "tc_dequant" for
- * 9 <= M <= 64, "stream_mma" otherwise up to M = 32 when group_size is 128 and K a multiple of
- * 1024; "mma_pipeline", "vectorized", "coalesced" for the other shapes); for
+ * M <= 8 when K is a multiple of 2048 and its x panels and partials fit in shared memory,
+ * "tc_dequant" for 9 <= M <= 64, "stream_mma" otherwise up to M = 32 when group_size is 128 and K
+ * a multiple of 1024; "mma_pipeline", "vectorized", "coalesced" for the other shapes); for
  * tests and the benchmark. Static storage.
  *
  * tc_dequant keeps split-K partial sums and per-tile counters in static device memory, so two of

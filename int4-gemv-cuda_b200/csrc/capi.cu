@@ -352,7 +352,7 @@ int int4gemv_kernel_info(const char* kernel, int64_t m, int64_t threads_per_bloc
   } else if (std::strcmp(kernel, "naive") == 0 || std::strcmp(kernel, "coalesced") == 0) {
     err = i4::simt_attrs(kernel, static_cast<int>(m), 0, 1, &at);
   } else if (std::strcmp(kernel, "w4a16") == 0) {
-    err = m <= 4                ? i4::stripe_mma_attrs(static_cast<int>(m), &at)
+    err = m <= 8                ? i4::stripe_mma_attrs(static_cast<int>(m), &at)
           : m < kTcDequantMinM  ? i4::stream_mma_attrs(static_cast<int>(m), &at)
           : m <= 64             ? i4::tc_dequant_attrs(static_cast<int>(m), &at)
                                 : i4::mma_pipeline_attrs(16, &at);

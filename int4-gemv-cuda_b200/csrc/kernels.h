@@ -122,7 +122,7 @@ cudaError_t launch_stream_mma(const GemvArgs& a, cudaStream_t stream, bool stric
 int64_t stream_mma_workspace_bytes(const GemvArgs& a);
 cudaError_t stream_mma_attrs(int m, KernelAttrs* out);
 
-// Stripe-fed mma.sync GEMV for M <= 4, group 128, K % 2048 == 0 (stripe_mma.cu): 2-D TMA tiles of
+// Stripe-fed mma.sync GEMV for M <= 8, group 128, K % 2048 == 0 (stripe_mma.cu): 2-D TMA tiles of
 // 32 rows x 2048 weights, the whole ring issued before the dependency wait unless strict.
 bool stripe_mma_supported(const GemvArgs& a, const char** why);
 cudaError_t launch_stripe_mma(const GemvArgs& a, cudaStream_t stream, bool strict);

@@ -932,9 +932,10 @@ __global__ void __maxnreg__(CW == 16 ? 96 : 168)
       if (in.ok) go.y[gi][static_cast<int64_t>(m) * ng + row - base] = __float2half_rn(sum);
     }
   } else if (a.epilogue == kGatherPeers) {
-    // This rank's columns of y, each as a tagged word (fp16 bits, call number), into every rank's
-    // gather buffer. The rows this CTA then copies into y are the same row range of every rank's
-    // shard: the words its counterpart CTAs write; each is read once its tag shows this call.
+    // This rank's columns of y, each as a tagged word (fp16 bits, call number), into every other
+    // rank's gather buffer and straight into this rank's y. The rows this CTA then copies into y
+    // are the same row range of every other rank's shard: the words its counterpart CTAs write;
+    // each is read once its tag shows this call.
     const unsigned epoch = exchange_epoch(peers);
     named_barrier(kConsumerBarrier, kConsumerThreads);  // every thread has read the call number
     for (int o = tid; o < rows * a.m; o += kConsumerThreads) {
@@ -942,12 +943,19 @@ __global__ void __maxnreg__(CW == 16 ? 96 : 168)
       const int r = o - m * rows;
       const unsigned h = __half_as_ushort(__float2half_rn(row_sum(r, m)));
       const int64_t at = static_cast<int64_t>(m) * peers.n_total + peers.col0 + row_begin + r;
-      for (int q = 0; q < peers.world; ++q) st_tagged(exchange_words(peers, q, epoch) + at, h, epoch);
+      for (int q = 0; q < peers.world; ++q) {
+        if (q == peers.rank) {
+          if (in.ok) a.y[at] = __ushort_as_half(static_cast<unsigned short>(h));
+        } else {
+          st_tagged(exchange_words(peers, q, epoch) + at, h, epoch);
+        }
+      }
     }
     const unsigned long long* buf = exchange_words(peers, peers.rank, epoch);
     bool live = true;
     for (int o = tid; o < peers.world * rows * a.m; o += kConsumerThreads) {
       const int q = o / (rows * a.m);
+      if (q == peers.rank) continue;  // this rank's own rows went to y above
       const int rem = o - q * rows * a.m;
       const int m = rem / rows;
       const int r = rem - m * rows;
@@ -957,9 +965,10 @@ __global__ void __maxnreg__(CW == 16 ? 96 : 168)
     }
     exchange_done(peers, epoch, tid);
   } else if (a.epilogue == kReducePeers) {
-    // This rank's fp32 partial sums, as tagged words, into slot `rank` of every rank's receive
-    // buffer; then the sum of the ranks' partials for this CTA's rows in rank order (the same on
-    // every rank, so all ranks hold bit-identical y), each read once its tag shows this call.
+    // This rank's fp32 partial sums, as tagged words, into slot `rank` of every other rank's
+    // receive buffer; then the sum of the ranks' partials for this CTA's rows in rank order (the
+    // same on every rank, so all ranks hold bit-identical y), each other rank's read once its tag
+    // shows this call, this rank's own taken from the same fixed-order sum in shared memory.
     const unsigned epoch = exchange_epoch(peers);
     named_barrier(kConsumerBarrier, kConsumerThreads);  // every thread has read the call number
     const int64_t slot = static_cast<int64_t>(a.m) * a.n;
@@ -968,7 +977,9 @@ __global__ void __maxnreg__(CW == 16 ? 96 : 168)
       const int r = o - m * rows;
       const unsigned bits = __float_as_uint(row_sum(r, m));
       const int64_t at = peers.rank * slot + static_cast<int64_t>(m) * a.n + row_begin + r;
-      for (int q = 0; q < peers.world; ++q) st_tagged(exchange_words(peers, q, epoch) + at, bits, epoch);
+      for (int q = 0; q < peers.world; ++q) {
+        if (q != peers.rank) st_tagged(exchange_words(peers, q, epoch) + at, bits, epoch);
+      }
     }
     const unsigned long long* mine = exchange_words(peers, peers.rank, epoch);
     bool live = true;
@@ -978,7 +989,9 @@ __global__ void __maxnreg__(CW == 16 ? 96 : 168)
       const int64_t at = static_cast<int64_t>(m) * a.n + row_begin + r;
       float total = 0.0f;
       for (int q = 0; q < peers.world; ++q) {
-        total += __uint_as_float(exchange_read(mine + q * slot + at, epoch, &live, p.status));
+        total += q == peers.rank
+                     ? row_sum(r, m)
+                     : __uint_as_float(exchange_read(mine + q * slot + at, epoch, &live, p.status));
       }
       if (in.ok) a.y[at] = store_value(a, m, row_begin + r, total);
     }

@@ -1,4 +1,4 @@
-// The B200 fast path for M <= 4: stripes of 32 rows x 2048 weights streamed by TMA into a ring of
+// The B200 fast path for M <= 8: stripes of 32 rows x 2048 weights streamed by TMA into a ring of
 // shared-memory stages, and warp-level tensor-core MMAs (mma.sync m16n8k16, f16 x f16 -> f32) on
 // the nibbles unpacked in registers.
 //
@@ -25,8 +25,14 @@
 // item's words, so one MMA covers 256 weights of four different groups), granule (w / 4 + c / 2)
 // % 4 (rotated so the 16-byte loads of one shared-memory phase hit distinct banks), and rows g,
 // g + 8, 16 + g, 24 + g of the block. For M = 3 or 4 the eight columns are two items x four rows
-// of x: lanes c and c ^ 1 share item 2 (w % 8) + c / 2, each with its own granule 2 (w / 8) + c % 2,
-// and an MMA still covers 256 weights (so M = 4 costs the MMAs of M = 1). Per packed word one shift and four LOP3s give the fp16 A halves 1024 + q
+// of x: lanes c and c ^ 1 share item 2 (w % 8) + c / 2, each with its own granule 2 (w / 8) + c % 2;
+// for M = 5..8 one item x eight rows: warp w takes item w, lane c its granule c. Either way an MMA
+// still covers 256 weights, so M = 8 costs the MMAs of M = 1.
+//
+// K-panels. When x for all of K does not fit beside the ring (M = 8 at K = 8192 would need 139 KB),
+// the CTA takes K in 2, 4, ... panels: it permutes the panel's x, runs all its row blocks over the
+// panel's stripes (the producer streams in the same order), and each warp adds its partials to the
+// earlier panels' in panel order. Per packed word one shift and four LOP3s give the fp16 A halves 1024 + q
 // and 1024 + 16 q exactly; the B registers of a word are reused for both 16-row tiles. Each tile's
 // low-half MMA chain starts from C = -1024 * (sum of the B values of the granule), which removes
 // the magic-number offset inside the tensor core, so after the stripe the accumulators hold
@@ -85,7 +91,8 @@ struct StripePlan {
   int rows_cap;    // rows of the largest CTA share
   int stripes;     // K / 2048
   int items;       // K / 128
-  int xs_stride;   // bytes of permuted x per row of x
+  int panels;      // K-panels: x is prepared one panel at a time (stripes split evenly)
+  int xs_stride;   // bytes of permuted x per row of x (one panel)
   int stages;
   int off_xs, off_bq, off_xsum, off_red, off_stage, smem_bytes;
   int strict;      // 1: read the weights only after griddepcontrol.wait
@@ -139,7 +146,7 @@ __device__ __forceinline__ void issue_stripe(const StripeBox& b, bool has_box, i
   }
 }
 
-// The producer warp: the CTA's blocks x stripes through the ring. Unless strict, the first
+// The producer warp: the CTA's K-panels x blocks x stripes through the ring (the consumers' order). Unless strict, the first
 // min(stages, total) stripes go out before griddepcontrol.wait. empty[s] expects one arrival per
 // consumer warp.
 __device__ __forceinline__ void stripe_produce(const StripePlan& p, const StripeMaps& maps,
@@ -155,21 +162,24 @@ __device__ __forceinline__ void stripe_produce(const StripePlan& p, const Stripe
   if (pre == 0) grid_dependency_wait();
   bool ok = true;
   int it = 0, slot = 0, use = 0;
-  for (int blk = 0; blk < blocks; ++blk) {
-    const int rows4 = (min(kSxRows, rows - blk * kSxRows) + 3) & ~3;
-    StripeBox b;
-    const bool has_box = stripe_box(maps, lane, rows4, row_begin + blk * kSxRows, &b);
-    for (int j = 0; j < p.stripes; ++j, ++it) {
-      if (it == pre && pre > 0) grid_dependency_wait();
-      if (ok && use > 0 && !mbar_wait_bounded(&empty[slot], (use - 1) & 1)) {
-        ok = false;
-        if (lane == 0) atomicExch(p.status, kStatusEmptyBarrierTimeout);
-      }
-      if (ok) issue_stripe(b, has_box, j, rows4, stages + slot * kSxStageBytes, &full[slot],
-                           policy, lane);
-      if (++slot == p.stages) {
-        slot = 0;
-        ++use;
+  for (int pn = 0; pn < p.panels; ++pn) {
+    const int j0 = pn * p.stripes / p.panels, j1 = (pn + 1) * p.stripes / p.panels;
+    for (int blk = 0; blk < blocks; ++blk) {
+      const int rows4 = (min(kSxRows, rows - blk * kSxRows) + 3) & ~3;
+      StripeBox b;
+      const bool has_box = stripe_box(maps, lane, rows4, row_begin + blk * kSxRows, &b);
+      for (int j = j0; j < j1; ++j, ++it) {
+        if (it == pre && pre > 0) grid_dependency_wait();
+        if (ok && use > 0 && !mbar_wait_bounded(&empty[slot], (use - 1) & 1)) {
+          ok = false;
+          if (lane == 0) atomicExch(p.status, kStatusEmptyBarrierTimeout);
+        }
+        if (ok) issue_stripe(b, has_box, j, rows4, stages + slot * kSxStageBytes, &full[slot],
+                             policy, lane);
+        if (++slot == p.stages) {
+          slot = 0;
+          ++use;
+        }
       }
     }
   }
@@ -183,13 +193,16 @@ __device__ __forceinline__ void stripe_produce(const StripePlan& p, const Stripe
   }
 }
 
-// x -> the permuted B layout and the two tables (see the file comment). Thread t handles blocks
-// (8 weights of one row of x) 2 t and 2 t + 1 of each 2 x NT-block step; a thread pair
-// covers one 4-word granule, eight threads one item.
+// x of one K-panel (8-weight blocks kw0 .. kw0 + kw_per_m - 1 of every row) -> the permuted B
+// layout and the two tables (see the file comment), indexed from the panel's first item. Thread t
+// handles blocks 2 t and 2 t + 1 of each 2 x NT-block step; a thread pair covers one 4-word
+// granule, eight threads one item. With TS = 8 (the MC = 8 layout, the four lanes of an MMA on the
+// four granules of one item) word w of granule g is stored at position w ^ g of the granule, so
+// those lanes' 16-byte loads hit distinct banks.
 template <int NT, int TS>
 __device__ __forceinline__ void stripe_prepare_x(const GemvArgs& a, const StripePlan& p,
-                                                 unsigned char* smem, int tid) {
-  const int kw_per_m = a.k / 8;
+                                                 unsigned char* smem, int tid, int kw0,
+                                                 int kw_per_m) {
   const int total = a.m * kw_per_m;
   unsigned char* xs = smem + p.off_xs;
   float* bq = reinterpret_cast<float*>(smem + p.off_bq);    // [items][4][TS]
@@ -203,7 +216,8 @@ __device__ __forceinline__ void stripe_prepare_x(const GemvArgs& a, const Stripe
       idx[s] = base + s * 2 * NT + 2 * tid;
       if (idx[s] < total) {
         const int m = idx[s] / kw_per_m, kw = idx[s] - m * kw_per_m;
-        const uint4* src = reinterpret_cast<const uint4*>(a.x + static_cast<int64_t>(m) * a.k) + kw;
+        const uint4* src =
+            reinterpret_cast<const uint4*>(a.x + static_cast<int64_t>(m) * a.k) + kw0 + kw;
         v[2 * s] = ld_stream_v4(src);
         v[2 * s + 1] = ld_stream_v4(src + 1);
       }
@@ -219,9 +233,15 @@ __device__ __forceinline__ void stripe_prepare_x(const GemvArgs& a, const Stripe
         kw = idx[s] - m * kw_per_m;
         const uint4 o0 = permute_x_block(v[2 * s], bsum, xsm);
         const uint4 o1 = permute_x_block(v[2 * s + 1], bsum, xsm);
-        unsigned char* row = xs + m * p.xs_stride + (kw >> 4) * kSxItemBytes + (kw & 15) * 16;
-        reinterpret_cast<uint4*>(row)[0] = o0;
-        reinterpret_cast<uint4*>(row)[1] = o1;
+        unsigned char* item_x = xs + m * p.xs_stride + (kw >> 4) * kSxItemBytes;
+        if constexpr (TS == 8) {
+          const int gr = (kw >> 2) & 3, w = kw & 3;  // kw is even: words w and w + 1
+          reinterpret_cast<uint4*>(item_x + (gr * 4 + (w ^ gr)) * 16)[0] = o0;
+          reinterpret_cast<uint4*>(item_x + (gr * 4 + ((w + 1) ^ gr)) * 16)[0] = o1;
+        } else {
+          reinterpret_cast<uint4*>(item_x + (kw & 15) * 16)[0] = o0;
+          reinterpret_cast<uint4*>(item_x + (kw & 15) * 16)[1] = o1;
+        }
       }
       bsum += __shfl_xor_sync(0xffffffffu, bsum, 1);  // the granule (4 words) of a thread pair
       xsm += __shfl_xor_sync(0xffffffffu, xsm, 1);
@@ -284,18 +304,31 @@ __device__ __forceinline__ void stripe_load(const unsigned char* st, const int (
 // TS: columns of the tables. With TS = 4 (the MC = 4 layout, one granule per lane) the lane's D
 // columns also take the B values of its partner lane (c ^ 1), whose granule is gran ^ 1; m0 is
 // the first of the lane's two rows of x.
+// TS = 8 (the MC = 8 layout): the D columns take the B values of all four lanes (the item's four
+// granules), and word u of the lane's granule sits at position u ^ swz (see stripe_prepare_x).
 template <int GPW, int TS>
 __device__ __forceinline__ void stripe_load_x(const unsigned char* const (&b_base)[GPW], int b_step,
                                               const float* bq, const float* xsum, int j, int item,
-                                              const int (&gran)[GPW], int m0, bool zero_term,
-                                              StripeX<GPW>& x) {
+                                              const int (&gran)[GPW], int m0, int swz,
+                                              bool zero_term, StripeX<GPW>& x) {
   const int tab = j * kSxItems + item;
   float2 ci = make_float2(0.0f, 0.0f);
 #pragma unroll
   for (int q = 0; q < GPW; ++q) {
     const unsigned char* bsrc = b_base[q] + j * b_step;
 #pragma unroll
-    for (int u = 0; u < 4; ++u) x.bx[q][u] = *reinterpret_cast<const uint4*>(bsrc + u * 16);
+    for (int u = 0; u < 4; ++u) {
+      x.bx[q][u] = *reinterpret_cast<const uint4*>(bsrc + (TS == 8 ? (u ^ swz) : u) * 16);
+    }
+    if constexpr (TS == 8) {
+#pragma unroll
+      for (int g4 = 0; g4 < 4; ++g4) {
+        const float2 v = *reinterpret_cast<const float2*>(bq + (tab * 4 + g4) * TS + m0);
+        ci.x += v.x;
+        ci.y += v.y;
+      }
+      continue;
+    }
     const float2 v = *reinterpret_cast<const float2*>(bq + (tab * 4 + gran[q]) * TS + m0);
     ci.x += v.x;
     ci.y += v.y;
@@ -386,14 +419,15 @@ __device__ __forceinline__ void stripe_epilogue(const StripeRegs<GPW>& r, const 
 // lane and stage) or 8 (two; MC <= 2 only); plus one producer warp. LO: the loads-only ceiling of the same stream (no x, no MMA):
 // every packed word and, once per (row, group), the scale and zero bits are XOR-folded into one
 // 32-bit word per row, written to ((uint32_t*) a.y)[row].
-template <int MC, int CW, bool LO = false>
+// PN: x in K-panels (p.panels > 1); false compiles the single-panel form.
+template <int MC, int CW, bool LO = false, bool PN = false>
 __global__ void __launch_bounds__((CW + 1) * kWarp, 1)
     stripe_mma_kernel(GemvArgs a, StripePlan p, const __grid_constant__ StripeMaps maps) {
   constexpr int kGPW = 16 / CW;            // granules per lane and stage
   constexpr int kConsumers = CW * kWarp;
-  constexpr int kTS = MC <= 2 ? 2 : 4;     // columns of the x tables
-  constexpr int kE = MC == 1 ? 1 : 2;      // the lane's D columns that hold rows of x
-  static_assert(MC != 4 || CW == 16, "the MC = 4 layout takes one granule per lane");
+  constexpr int kTS = MC <= 2 ? 2 : MC;     // columns of the x tables
+  constexpr int kE = MC == 1 ? 1 : 2;       // the lane's D columns that hold rows of x
+  static_assert(MC <= 2 || CW == 16, "the MC = 4 and 8 layouts take one granule per lane");
   extern __shared__ __align__(1024) unsigned char smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + kSxMaxStages;
@@ -430,10 +464,6 @@ __global__ void __launch_bounds__((CW + 1) * kWarp, 1)
 
   // ---------------- consumers ----------------
   grid_dependency_wait();  // x may come from the previous kernel in the stream
-  if constexpr (!LO) {
-    stripe_prepare_x<kConsumers, kTS>(a, p, smem, tid);
-    named_barrier(kSxBarrier, kConsumers);
-  }
 
   const int g = lane >> 2, c = lane & 3;
   // MC <= 2: lane c takes item 4 (w % 4) + c (column pair c), granule set w / 4 (kGPW granules);
@@ -441,14 +471,19 @@ __global__ void __launch_bounds__((CW + 1) * kWarp, 1)
   // MC = 4: lanes c and c ^ 1 take item 2 (w % 8) + c / 2 (columns 4 (c / 2) .. + 3), with the
   //   granules 2 (w / 8) + c % 2; column g is (item g / 4, row of x g % 4), and the lane's D
   //   columns 2c, 2c + 1 are rows m0 = 2 (c % 2) and m0 + 1 of its item.
+  // MC = 8: warp w takes item w, lane c its granule c; column g is row g of x, and the lane's D
+  //   columns are rows m0 = 2c and m0 + 1.
   // A k-slot's word depends on c only (never on g): B column g is supplied by the lanes of row g.
-  const int iq = MC == 4 ? (warp & 7) : (warp & 3);
-  const int wq = MC == 4 ? (warp >> 3) : (warp >> 2);
-  const int item = MC == 4 ? 2 * iq + (c >> 1) : 4 * iq + c;  // item of this lane in a stripe
+  const int iq = MC == 8 ? warp : MC == 4 ? (warp & 7) : (warp & 3);
+  const int wq = MC == 8 ? 0 : MC == 4 ? (warp >> 3) : (warp >> 2);
+  const int item = MC == 8 ? iq : MC == 4 ? 2 * iq + (c >> 1) : 4 * iq + c;  // in a stripe
   const bool zero_term = wq == 0;  // the warps holding granule 0 of their items add the zero term
-  const int xm = MC == 4 ? (g & 3) : g - 2 * c;  // the row of x whose B values this lane holds
-  const bool has_x = MC == 4 ? ((g >> 2) == (c >> 1) && xm < a.m) : (xm >= 0 && xm < MC);
-  const int m0 = MC == 4 ? 2 * (c & 1) : 0;
+  // the row of x whose B values this lane holds
+  const int xm = MC == 8 ? g : MC == 4 ? (g & 3) : g - 2 * c;
+  const bool has_x = MC == 8   ? xm < a.m
+                     : MC == 4 ? ((g >> 2) == (c >> 1) && xm < a.m)
+                               : (xm >= 0 && xm < MC);
+  const int m0 = MC == 8 ? 2 * c : MC == 4 ? 2 * (c & 1) : 0;
   const unsigned char* xs = smem + p.off_xs;
   const float* bq = reinterpret_cast<const float*>(smem + p.off_bq);
   const float* xsum = reinterpret_cast<const float*>(smem + p.off_xsum);
@@ -458,7 +493,7 @@ __global__ void __launch_bounds__((CW + 1) * kWarp, 1)
   for (int q = 0; q < kGPW; ++q) {
     // MC <= 2: granules rotated by c / 2 so the 16-byte loads of one shared-memory phase hit
     // distinct banks
-    gran[q] = MC == 4 ? 2 * wq + (c & 1) : (kGPW * wq + q + (c >> 1)) & 3;
+    gran[q] = MC == 8 ? c : MC == 4 ? 2 * wq + (c & 1) : (kGPW * wq + q + (c >> 1)) & 3;
     a_off[q] = g * kSxRowBytes + item * 64 + gran[q] * 16;
     b_base[q] = has_x ? xs + xm * p.xs_stride + item * kSxItemBytes + gran[q] * 64
                       : smem + kSxZeroOff;
@@ -473,10 +508,10 @@ __global__ void __launch_bounds__((CW + 1) * kWarp, 1)
   StageRingSx ring{full, p.stages, p.status, true, 0, 0u};
   // One block of rows: NT 16-row tiles (2, or 1 when the block has at most 16 rows), a
   // compile-time count so the two tiles' MMAs interleave freely.
-  auto run_block = [&]<int NT>(int blk, int rows_b) {
+  auto run_block = [&]<int NT>(int blk, int rows_b, int j0, int j1, bool accumulate) {
     if constexpr (LO) {
       uint32_t f[2][2] = {{0u, 0u}, {0u, 0u}};  // [tile][row g / g + 8]
-      for (int j = 0; j < p.stripes; ++j) {
+      for (int j = j0; j < j1; ++j) {
         const int slot = ring.next();
         StripeRegs<kGPW> r;
         stripe_load<kGPW, NT>(stages + slot * kSxStageBytes, a_off, s_off, z_off, zero_term, r);
@@ -500,7 +535,8 @@ __global__ void __launch_bounds__((CW + 1) * kWarp, 1)
           v ^= __shfl_xor_sync(0xffffffffu, v, 1);
           v ^= __shfl_xor_sync(0xffffffffu, v, 2);
           if (c == 0 && 16 * t + 8 * h + g < rows_b) {
-            redu[warp * p.rows_cap + blk * kSxRows + 16 * t + 8 * h + g] = v;
+            uint32_t* dst = &redu[warp * p.rows_cap + blk * kSxRows + 16 * t + 8 * h + g];
+            *dst = accumulate ? *dst ^ v : v;
           }
         }
       return;
@@ -512,12 +548,13 @@ __global__ void __launch_bounds__((CW + 1) * kWarp, 1)
       for (int h = 0; h < 2; ++h)
 #pragma unroll
         for (int e = 0; e < kE; ++e) acc[t][h][e] = 0.0f;
-    for (int j = 0; j < p.stripes; ++j) {
+    for (int j = j0; j < j1; ++j) {
       const int slot = ring.next();
       StripeRegs<kGPW> r;
       stripe_load<kGPW, NT>(stages + slot * kSxStageBytes, a_off, s_off, z_off, zero_term, r);
       StripeX<kGPW> xr;
-      stripe_load_x<kGPW, kTS>(b_base, b_step, bq, xsum, j, item, gran, m0, zero_term, xr);
+      stripe_load_x<kGPW, kTS>(b_base, b_step, bq, xsum, j - j0, item, gran, m0, c, zero_term,
+                               xr);
       float d[2][4];
       stripe_mma<kGPW, NT>(r, xr, d);
       stripe_epilogue<kE, kGPW, NT>(r, d, xr.xsm, zero_term, acc);
@@ -528,7 +565,8 @@ __global__ void __launch_bounds__((CW + 1) * kWarp, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);  // the stage may be refilled
     }
-    // the items of this warp (four, or two for MC = 4), then one partial per (row, m) and warp
+    // the items of this warp (four, two for MC = 4, one for MC = 8), then one partial per
+    // (row, m) and warp, added to the earlier K-panels' in panel order
 #pragma unroll
     for (int t = 0; t < NT; ++t)
 #pragma unroll
@@ -536,20 +574,31 @@ __global__ void __launch_bounds__((CW + 1) * kWarp, 1)
 #pragma unroll
         for (int e = 0; e < kE; ++e) {
           float v = acc[t][h][e];
-          if constexpr (MC != 4) v += __shfl_xor_sync(0xffffffffu, v, 1);
-          v += __shfl_xor_sync(0xffffffffu, v, 2);
-          const bool writer = MC == 4 ? c < 2 : c == 0;
+          if constexpr (MC <= 2) v += __shfl_xor_sync(0xffffffffu, v, 1);
+          if constexpr (MC <= 4) v += __shfl_xor_sync(0xffffffffu, v, 2);
+          const bool writer = MC == 8 ? true : MC == 4 ? c < 2 : c == 0;
           if (writer && 16 * t + 8 * h + g < rows_b) {
-            red[(warp * p.rows_cap + blk * kSxRows + 16 * t + 8 * h + g) * MC + m0 + e] = v;
+            float* dst = &red[(warp * p.rows_cap + blk * kSxRows + 16 * t + 8 * h + g) * MC + m0 + e];
+            *dst = accumulate ? *dst + v : v;
           }
         }
   };
-  for (int blk = 0; blk < blocks; ++blk) {
-    const int rows_b = min(kSxRows, rows - blk * kSxRows);
-    if (rows_b > 16) {  // uniform over the CTA
-      run_block.template operator()<2>(blk, rows_b);
-    } else {
-      run_block.template operator()<1>(blk, rows_b);
+  const int panels = PN ? p.panels : 1;
+  for (int pn = 0; pn < panels; ++pn) {
+    const int j0 = PN ? pn * p.stripes / p.panels : 0;
+    const int j1 = PN ? (pn + 1) * p.stripes / p.panels : p.stripes;
+    if constexpr (!LO) {
+      if (pn > 0) named_barrier(kSxBarrier, kConsumers);  // the last panel's x is no longer read
+      stripe_prepare_x<kConsumers, kTS>(a, p, smem, tid, j0 * (kSxK / 8), (j1 - j0) * (kSxK / 8));
+      named_barrier(kSxBarrier, kConsumers);
+    }
+    for (int blk = 0; blk < blocks; ++blk) {
+      const int rows_b = min(kSxRows, rows - blk * kSxRows);
+      if (rows_b > 16) {  // uniform over the CTA
+        run_block.template operator()<2>(blk, rows_b, j0, j1, PN && pn > 0);
+      } else {
+        run_block.template operator()<1>(blk, rows_b, j0, j1, PN && pn > 0);
+      }
     }
   }
 
@@ -584,7 +633,7 @@ bool stripe_plan(const GemvArgs& a, StripePlan* p, const char** why) {
     if (why) *why = reason;
     return false;
   };
-  if (a.m < 1 || a.m > 4) return fail("M must be in [1, 4]");
+  if (a.m < 1 || a.m > 8) return fail("M must be in [1, 8]");
   if (a.group != kItemK) return fail("group_size must be 128");
   if (a.k % kSxK != 0) return fail("K must be a multiple of 2048");
   if (a.epilogue != kStoreY) return fail("plain stores only");
@@ -597,26 +646,38 @@ bool stripe_plan(const GemvArgs& a, StripePlan* p, const char** why) {
   p->rows_cap = 4 * ((p->units + p->ctas - 1) / p->ctas);
   p->stripes = a.k / kSxK;
   p->items = a.k / kItemK;
-  p->xs_stride = p->items * kSxItemBytes;
-  int64_t off = kSxHeader;
-  p->off_xs = static_cast<int>(off);
-  off += static_cast<int64_t>(a.m) * p->xs_stride;
-  const int mc = a.m <= 2 ? a.m : 4;  // the kernel's MC
-  const int ts = a.m <= 2 ? 2 : 4;    // columns of the x tables
-  p->off_bq = static_cast<int>(off);
-  off += static_cast<int64_t>(p->items) * 4 * ts * 4;
-  p->off_xsum = static_cast<int>(off);
-  off += static_cast<int64_t>(p->items) * ts * 4;
-  p->off_red = static_cast<int>(off);
-  off += static_cast<int64_t>(16) * p->rows_cap * mc * 4;  // partials of up to 16 warps
-  off = (off + 1023) / 1024 * 1024;
-  p->off_stage = static_cast<int>(off);
-  if (off >= kSxSmemLimit) return fail("x does not fit in shared memory");
-  const int64_t stages =
-      std::min<int64_t>((kSxSmemLimit - off) / kSxStageBytes, kSxMaxStages);
-  if (stages < kSxMinStages) return fail("x does not fit in shared memory");
-  p->stages = static_cast<int>(stages);
-  p->smem_bytes = static_cast<int>(off + stages * kSxStageBytes);
+  const int mc = a.m <= 2 ? a.m : a.m <= 4 ? 4 : 8;  // the kernel's MC
+  const int ts = a.m <= 2 ? 2 : mc;                   // columns of the x tables
+  // The fewest K-panels (1, 2, 4, ... stripes) whose permuted x, tables and partials leave room
+  // for the three-stripe ring.
+  for (int panels = 1;; panels *= 2) {
+    // (M <= 2 keeps all of x: the single-panel kernels only)
+    if (panels > p->stripes || (a.m <= 2 && panels > 1)) {
+      return fail("x does not fit in shared memory");
+    }
+    p->panels = panels;
+    const int items = (p->stripes + panels - 1) / panels * kSxItems;  // of the longest panel
+    p->xs_stride = items * kSxItemBytes;
+    if (mc == 8) p->xs_stride += (64 - p->xs_stride % 128 + 128) % 128;  // rows 64 B apart in banks
+    int64_t off = kSxHeader;
+    p->off_xs = static_cast<int>(off);
+    off += static_cast<int64_t>(a.m) * p->xs_stride;
+    p->off_bq = static_cast<int>(off);
+    off += static_cast<int64_t>(items) * 4 * ts * 4;
+    p->off_xsum = static_cast<int>(off);
+    off += static_cast<int64_t>(items) * ts * 4;
+    p->off_red = static_cast<int>(off);
+    off += static_cast<int64_t>(16) * p->rows_cap * mc * 4;  // partials of up to 16 warps
+    off = (off + 1023) / 1024 * 1024;
+    p->off_stage = static_cast<int>(off);
+    if (off >= kSxSmemLimit) continue;
+    const int64_t stages =
+        std::min<int64_t>((kSxSmemLimit - off) / kSxStageBytes, kSxMaxStages);
+    if (stages < kSxMinStages) continue;
+    p->stages = static_cast<int>(stages);
+    p->smem_bytes = static_cast<int>(off + stages * kSxStageBytes);
+    break;
+  }
   p->strict = 0;
   p->status = nullptr;
   return true;
@@ -702,13 +763,18 @@ cudaError_t stripe_maps_for(const GemvArgs& a, StripeMaps* out) {
 #endif
 // Kernel instances (rows of x, consumer warps).
 template <typename F>
-cudaError_t with_stripe_m(int m, F&& f) {
-  if (m <= 1) return f.template operator()<1, STRIPE_CW>();
-  if (m == 2) return f.template operator()<2, STRIPE_CW>();
-  return f.template operator()<4, 16>();
+cudaError_t with_stripe_m(int m, int panels, F&& f) {
+  if (m <= 1) return f.template operator()<1, STRIPE_CW, false>();
+  if (m == 2) return f.template operator()<2, STRIPE_CW, false>();
+  if (m <= 4) {
+    if (panels > 1) return f.template operator()<4, 16, true>();
+    return f.template operator()<4, 16, false>();
+  }
+  if (panels > 1) return f.template operator()<8, 16, true>();
+  return f.template operator()<8, 16, false>();
 }
 
-std::once_flag g_stripe_attr_once[4][64];
+std::once_flag g_stripe_attr_once[8][2][64];
 
 }  // namespace
 
@@ -729,10 +795,10 @@ cudaError_t launch_stripe_mma(const GemvArgs& a, cudaStream_t stream, bool stric
   int dev = 0;
   const cudaError_t derr = cudaGetDevice(&dev);
   if (derr != cudaSuccess) return derr;
-  return with_stripe_m(a.m, [&]<int MC, int CW>() {
+  return with_stripe_m(a.m, p.panels, [&]<int MC, int CW, bool PN>() {
     cudaError_t result = cudaSuccess;
-    std::call_once(g_stripe_attr_once[MC - 1][dev & 63], [&] {
-      result = cudaFuncSetAttribute(stripe_mma_kernel<MC, CW>,
+    std::call_once(g_stripe_attr_once[MC - 1][PN ? 1 : 0][dev & 63], [&] {
+      result = cudaFuncSetAttribute(stripe_mma_kernel<MC, CW, false, PN>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, kSxSmemLimit);
     });
     if (result != cudaSuccess) return result;
@@ -746,7 +812,7 @@ cudaError_t launch_stripe_mma(const GemvArgs& a, cudaStream_t stream, bool stric
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, stripe_mma_kernel<MC, CW>, a, p, maps);
+    return cudaLaunchKernelEx(&cfg, stripe_mma_kernel<MC, CW, false, PN>, a, p, maps);
   });
 }
 
@@ -788,10 +854,10 @@ cudaError_t launch_stripe_load_only(uint32_t* out, const GemvArgs& args, cudaStr
 }
 
 cudaError_t stripe_mma_attrs(int m, KernelAttrs* out) {
-  const int mm = m < 1 ? 1 : m > 4 ? 4 : m;
-  return with_stripe_m(mm, [&]<int MC, int CW>() {
+  const int mm = m < 1 ? 1 : m > 8 ? 8 : m;
+  return with_stripe_m(mm, 1, [&]<int MC, int CW, bool PN>() {
     cudaFuncAttributes fa;
-    cudaError_t err = cudaFuncGetAttributes(&fa, stripe_mma_kernel<MC, CW>);
+    cudaError_t err = cudaFuncGetAttributes(&fa, stripe_mma_kernel<MC, CW, false, PN>);
     if (err != cudaSuccess) return err;
     out->registers = fa.numRegs;
     out->local_bytes = static_cast<int>(fa.localSizeBytes);

@@ -94,12 +94,14 @@ def test_workspace_size_is_nonnegative():
 
 def test_workspace_only_for_the_wide_fast_path():
     """The fast path uses a workspace (x permuted once per call) only where stream_mma's wide path
-    runs (5 <= M <= 8) on its own shapes (group 128, K % 1024 == 0); from M = 9 on tc_dequant is
-    picked and needs none from the caller."""
+    runs: 5 <= M <= 8 on its shapes (group 128, K % 1024 == 0) that stripe_mma does not take (K not
+    a multiple of 2048, or x and the partials of a CTA's rows too large); from M = 9 on tc_dequant
+    is picked and needs none from the caller."""
     size = capi.lib().int4gemv_w4a16_workspace_size
     assert size(1, 8192, 8192, 128) == 0 and size(4, 8192, 8192, 128) == 0
-    assert size(8, 8192, 8192, 128) > size(5, 8192, 8192, 128) > 0
-    assert size(8, 8192, 8192, 128) >= 8 * 8192 * 2  # at least x itself, permuted
+    assert size(8, 8192, 8192, 128) == 0 and size(5, 8192, 8192, 128) == 0  # stripe_mma
+    assert size(8, 28672, 8192, 128) > size(5, 8192, 3072, 128) > 0  # stream_mma's wide path
+    assert size(8, 28672, 8192, 128) >= 8 * 8192 * 2  # at least x itself, permuted
     assert size(9, 8192, 8192, 128) == 0 and size(32, 8192, 8192, 128) == 0
     assert size(8, 8192, 8192, 64) == 0 and size(8, 8192, 1152, 128) == 0
     assert size(0, 8192, 8192, 128) == 0 and size(16, 8192, 8192, 100) == 0

@@ -27,24 +27,41 @@ KERNELS = [
 FAST = ["stripe_mma", "tc_dequant", "stream_mma", "tcgen05", "mma_pipeline"]
 
 
-def expected_kernel(m, k, g=128, n=8192):
-    """The kernel int4gemv_w4a16 picks on the fast path's shapes: stripe_mma for M <= 4 and K a
-    multiple of 2048 when x (permuted, per-item padded), its tables, the warps' partials and three
-    34 KB stripes fit in 227 KB of shared memory; tc_dequant for 9 <= M <= 64; stream_mma for the
-    rest (M <= 32, K a multiple of 1024)."""
-    if 9 <= m <= 64 and g == 128 and k % 1024 == 0:
-        return "tc_dequant"
-    if m > 4 or k % 2048 or g != 128:
-        return "stream_mma"
+def stripe_fits(m, n, k):
+    """stripe_plan's shared-memory rule: the fewest K-panels (1, 2, 4, ...; one for M <= 2) whose
+    permuted x (17 bytes per 8 weights, per-item padded), tables and warp partials leave room for
+    three 34 KB stripes in 227 KB."""
+    if m > 8 or k % 2048:
+        return False
     units = (n + 3) // 4
     rows_cap = 4 * (-(-units // min(torch.cuda.get_device_properties(0).multi_processor_count,
                                     units)))
-    items = k // 128
-    ts = 2 if m <= 2 else 4  # columns of the x tables
-    mc = m if m <= 2 else 4  # columns of the partials
-    off = 1536 + m * items * 272 + items * 20 * ts + 16 * rows_cap * mc * 4
-    off = -(-off // 1024) * 1024
-    return "stripe_mma" if (227 * 1024 - off) // 34816 >= 3 else "stream_mma"
+    stripes = k // 2048
+    mc = m if m <= 2 else 4 if m <= 4 else 8
+    ts = 2 if m <= 2 else mc
+    panels = 1
+    while panels <= stripes and (m > 2 or panels == 1):
+        items = -(-stripes // panels) * 16
+        xs = items * 272
+        if mc == 8:
+            xs += (64 - xs % 128 + 128) % 128
+        off = 1536 + m * xs + items * 4 * ts * 4 + items * ts * 4 + 16 * rows_cap * mc * 4
+        off = -(-off // 1024) * 1024
+        if off < 227 * 1024 and (227 * 1024 - off) // 34816 >= 3:
+            return True
+        panels *= 2
+    return False
+
+
+def expected_kernel(m, k, g=128, n=8192):
+    """The kernel int4gemv_w4a16 picks on the fast path's shapes: stripe_mma for M <= 8 and K a
+    multiple of 2048 when its x panels fit (stripe_fits); tc_dequant for 9 <= M <= 64; stream_mma
+    for the rest (M <= 32, K a multiple of 1024)."""
+    if g != 128:
+        return "stream_mma"
+    if 9 <= m <= 64 and k % 1024 == 0:
+        return "tc_dequant"
+    return "stripe_mma" if stripe_fits(m, n, k) else "stream_mma"
 
 
 def cuda(*arrays):
@@ -187,13 +204,17 @@ def test_stream_mma_shapes(m, n, k):
 
 
 # stripe_mma edge cases: rows per CTA below one 16-row tile, between one and two tiles, several
-# 32-row blocks, N not a multiple of 4, M = 1 to 4 (M = 3 and 4: two groups x four rows of x per
-# MMA, M = 3 with an empty column), K from one stripe (2048) to 28672.
+# 32-row blocks, N not a multiple of 4, M = 1 to 8 (M = 3 and 4: two groups x four rows of x per
+# MMA, M = 3 with an empty column; M = 5..8: one group x eight rows), K from one stripe (2048) to
+# 28672, one or several K-panels of x.
 STRIPE = [
     (1, 1, 2048), (2, 5, 2048), (1, 37, 8192), (2, 148 * 4 + 3, 4096), (1, 148 * 20 + 1, 6144),
     (2, 148 * 24, 2048), (1, 148 * 36 + 2, 10240), (2, 4099, 8192), (1, 1000, 28672),
     (2, 300, 14336), (1, 28672, 2048), (3, 1, 2048), (4, 37, 8192), (3, 148 * 4 + 3, 4096),
     (4, 4099, 8192), (3, 8192, 8192), (4, 14336, 4096), (4, 148 * 36 + 2, 6144),
+    # K-panels (x prepared one panel at a time) and the MC = 8 layout (M = 5..8)
+    (4, 4096, 14336), (3, 1000, 28672), (5, 37, 2048), (6, 4099, 4096), (7, 148 * 4 + 3, 8192),
+    (8, 8192, 8192), (8, 4096, 14336), (5, 14336, 4096), (8, 1000, 28672), (8, 148 * 36 + 2, 6144),
 ]
 
 
@@ -209,7 +230,7 @@ def test_stripe_mma_shapes(m, n, k):
 
 def test_stripe_mma_rejects():
     """Shapes stripe_mma does not take raise a clear error when it is asked for by name."""
-    for m, k, why in ((5, 2048, r"M must be in \[1, 4\]"), (1, 3072, "K must be a multiple of 2048")):
+    for m, k, why in ((9, 2048, r"M must be in \[1, 8\]"), (1, 3072, "K must be a multiple of 2048")):
         args = cuda(*oracle.synthetic(m, 64, k, 128))
         with pytest.raises(RuntimeError, match=why):
             ops.w4a16_with(*args, 128, "stripe_mma")
@@ -291,7 +312,7 @@ def test_w4a16_f32_tc_dequant(m, n, k):
 
 
 @pytest.mark.parametrize("kern,m", [("stripe_mma", 1), ("stripe_mma", 2), ("stripe_mma", 3),
-                                    ("stripe_mma", 4), ("stream_mma", 1),
+                                    ("stripe_mma", 4), ("stripe_mma", 8), ("stream_mma", 1),
                                     ("stream_mma", 2), ("stream_mma", 8), ("stream_mma", 16),
                                     ("tcgen05", 1), ("tc_dequant", 1), ("tc_dequant", 16),
                                     ("tc_dequant", 40)])
