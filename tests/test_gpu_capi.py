@@ -32,8 +32,7 @@ def test_w4a16_through_c_abi(m, n, k):
     torch.cuda.synchronize()
     ok, msg = oracle.check_close(y.float().cpu().numpy(), oracle.reference(x, q, s, z))
     assert ok, msg
-    want = ("stripe_mma" if m <= 2 and k % 2048 == 0 else
-            "tc_dequant" if m >= 9 else "stream_mma")
+    want = "tc_dequant" if m >= 9 else "stripe_mma" if k % 2048 == 0 else "stream_mma"
     assert capi.w4a16_kernel_name(*ptrs(tx, tq, ts, tz), m, n, k, 128) == want
 
 
