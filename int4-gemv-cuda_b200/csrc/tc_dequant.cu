@@ -526,22 +526,36 @@ __global__ void __launch_bounds__(kTdThreads, 1)
           // c_lo's range may start in an earlier tile (then this is its last tile, slot 1); every
           // later contributor starts in this tile (slot 0).
           const int lo_slot = unit_begin(p, c_lo) / p.spt == t ? 0 : 1;
-          for (int m0 = 0; m0 < a.m; m0 += 16) {
-            float sum[16];
+          // Eight outputs at a time, the partials of up to four contributors loaded together
+          // (one round trip to L2 instead of one per contributor), then added in CTA order.
+          for (int m0 = 0; m0 < a.m; m0 += 8) {
+            float sum[8];
 #pragma unroll
-            for (int e = 0; e < 16; ++e) sum[e] = 0.0f;
-            for (int c = c_lo; c <= c_hi; ++c) {
-              const int cs = c == c_lo ? lo_slot : 0;
-              const float* src =
-                  p.partials + ((static_cast<int64_t>(c) * 2 + cs) * a.m + m0) * 128 + rl;
+            for (int e = 0; e < 8; ++e) sum[e] = 0.0f;
+            for (int c0 = c_lo; c0 <= c_hi; c0 += 4) {
+              float v[4][8];
 #pragma unroll
-              for (int e = 0; e < 16; ++e) {
-                if (m0 + e < a.m) sum[e] += __ldcg(src + e * 128);
+              for (int ci = 0; ci < 4; ++ci) {
+                const int c = c0 + ci;
+                const int cs = c == c_lo ? lo_slot : 0;
+                const float* src =
+                    p.partials + ((static_cast<int64_t>(c) * 2 + cs) * a.m + m0) * 128 + rl;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                  v[ci][e] = c <= c_hi && m0 + e < a.m ? __ldcg(src + e * 128) : 0.0f;
+                }
+              }
+#pragma unroll
+              for (int ci = 0; ci < 4; ++ci) {
+                if (c0 + ci <= c_hi) {
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) sum[e] += v[ci][e];
+                }
               }
             }
             if (store) {
 #pragma unroll
-              for (int e = 0; e < 16; ++e) {
+              for (int e = 0; e < 8; ++e) {
                 if (m0 + e < a.m) td_store(a, m0 + e, row, sum[e]);
               }
             }
