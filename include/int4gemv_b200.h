@@ -261,6 +261,9 @@ size_t int4gemv_peers_struct_bytes(void);
 
 /* The GEMV of this rank's shard with the exchange fused into its epilogue, on the fast path's
  * shapes (group_size 128, K % 1024 == 0, M <= 32), y [m, n_total] (ROWS) or [m, n] (K) fp16.
+ * The shard's GEMV runs on stripe_mma where it takes the shape (M <= 8, K % 2048 == 0, 16-byte
+ * aligned pointers), else on stream_mma; ranks whose K shares differ may run different kernels,
+ * the exchange words are the same.
  * ROWS: the shard's rows are columns [col0, col0 + n) of y; each CTA writes its outputs, each
  * tagged with the call number in the same 8-byte store, into every rank's exchange buffer over
  * NVLink (peer stores), then copies the rows its counterpart CTAs wrote into y as their tags show

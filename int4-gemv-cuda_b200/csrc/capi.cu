@@ -779,7 +779,11 @@ int int4gemv_w4a16_exchange(void* y, const void* x, const void* qweight, const v
   i4::GemvArgs a = make_args(y, x, qweight, scales, zeros, m, n, k, group_size);
   a.epilogue = mode == INT4GEMV_SHARD_ROWS ? i4::kGatherPeers : i4::kReducePeers;
   const char* why = "unsupported shape";
-  if (!i4::stream_mma_supported(a, &why)) return fail(INT4GEMV_ERR_INVALID, "%s: %s", name, why);
+  // the M <= 8 stripe kernel where it takes the shape, else the stream kernel
+  const bool stripe = i4::stripe_mma_supported(a, nullptr);
+  if (!stripe && !i4::stream_mma_supported(a, &why)) {
+    return fail(INT4GEMV_ERR_INVALID, "%s: %s", name, why);
+  }
   i4::PeerSet ps{};
   for (int r = 0; r < peers->world; ++r) ps.out[r] = peers->out[r];
   ps.counters = static_cast<unsigned*>(peers->counters);
@@ -788,8 +792,9 @@ int int4gemv_w4a16_exchange(void* y, const void* x, const void* qweight, const v
   ps.rank = peers->rank;
   ps.n_total = static_cast<int>(n_out);
   ps.col0 = static_cast<int>(mode == INT4GEMV_SHARD_ROWS ? peers->col0 : 0);
-  return launched(name, i4::launch_stream_mma(a, static_cast<cudaStream_t>(stream),
-                                              strict_weights(), &ps));
+  const auto st = static_cast<cudaStream_t>(stream);
+  return launched(name, stripe ? i4::launch_stripe_mma(a, st, strict_weights(), &ps)
+                               : i4::launch_stream_mma(a, st, strict_weights(), &ps));
 }
 
 int int4gemv_w4a16_exchange_static(void* y, const void* x, const void* qweight,
@@ -820,7 +825,9 @@ int int4gemv_w4a16_exchange_static(void* y, const void* x, const void* qweight,
     i4::GemvArgs a = make_args(y, x, qweight, scales, zeros, m, n, k, group_size);
     a.epilogue = mode == INT4GEMV_SHARD_ROWS ? i4::kGatherPeers : i4::kReducePeers;
     const char* why = "unsupported shape";
-    if (!i4::stream_mma_supported(a, &why)) return fail(INT4GEMV_ERR_INVALID, "%s: %s", name, why);
+    if (!i4::stripe_mma_supported(a, nullptr) && !i4::stream_mma_supported(a, &why)) {
+      return fail(INT4GEMV_ERR_INVALID, "%s: %s", name, why);
+    }
   }
   void* out = nullptr;
   void* counters = nullptr;

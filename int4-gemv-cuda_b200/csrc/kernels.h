@@ -11,8 +11,8 @@ namespace i4 {
 
 // What the GEMV writes. kStoreY: y [m, n]. kSiluMul: the rows of W are gate and up rows
 // interleaved (row 2i = gate i, row 2i + 1 = up i) and y [m, n / 2] = silu(gate) * up.
-// kGatherPeers / kReducePeers: the fused exchange of a layer sharded over the ranks of one node
-// (PeerSet below): rows split (every rank's y gets this rank's columns) or K split (every rank
+// kGatherPeers / kReducePeers (stripe_mma and stream_mma): the fused exchange of a layer sharded
+// over the ranks of one node (PeerSet below): rows split (every rank's y gets this rank's columns) or K split (every rank
 // gets this rank's fp32 partial sums, then each adds all ranks' partials in rank order).
 // kGroupedY: the rows of W are several matrices stacked (GroupOut below) and each matrix's
 // outputs go to its own y.
@@ -110,8 +110,9 @@ bool tc_gemv_supported(const GemvArgs& a, const char** why);
 cudaError_t launch_tc_gemv(const GemvArgs& a, cudaStream_t stream, bool strict);
 cudaError_t tc_gemv_attrs(int m, KernelAttrs* out);
 
-// TMA-tile-fed mma.sync GEMV for M <= 32, group 128 (stream_mma.cu): the fast path. Launched
-// with programmatic stream serialization like launch_tc_gemv.
+// TMA-tile-fed mma.sync GEMV for M <= 32, group 128, K % 1024 == 0 (stream_mma.cu): the M <= 8
+// shapes stripe_mma does not take, and the fused epilogues. Launched with programmatic stream
+// serialization like launch_tc_gemv.
 bool stream_mma_supported(const GemvArgs& a, const char** why);
 // With a workspace of at least stream_mma_workspace_bytes(a) bytes (> 0 for the wide path, M >= 5,
 // plain stores), a small pre-kernel permutes x once and the GEMV's CTAs copy it instead of each
@@ -125,7 +126,9 @@ cudaError_t stream_mma_attrs(int m, KernelAttrs* out);
 // Stripe-fed mma.sync GEMV for M <= 8, group 128, K % 2048 == 0 (stripe_mma.cu): 2-D TMA tiles of
 // 32 rows x 2048 weights, the whole ring issued before the dependency wait unless strict.
 bool stripe_mma_supported(const GemvArgs& a, const char** why);
-cudaError_t launch_stripe_mma(const GemvArgs& a, cudaStream_t stream, bool strict);
+// With peers (kGatherPeers / kReducePeers) it runs the fused exchange like launch_stream_mma.
+cudaError_t launch_stripe_mma(const GemvArgs& a, cudaStream_t stream, bool strict,
+                              const PeerSet* peers = nullptr);
 cudaError_t stripe_mma_attrs(int m, KernelAttrs* out);
 // The loads-only ceiling of the stripe stream (M = 1 plan, no x, no MMA): out[row] = XOR of the
 // row's packed words and of (scale bits | zero bits << 16) of each of its groups. a.y, a.x and

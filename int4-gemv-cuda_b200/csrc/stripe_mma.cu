@@ -50,6 +50,7 @@
 #include <mutex>
 #include <vector>
 
+#include "exchange.cuh"
 #include "weight_stream.cuh"
 
 namespace i4 {
@@ -422,7 +423,8 @@ __device__ __forceinline__ void stripe_epilogue(const StripeRegs<GPW>& r, const 
 // PN: x in K-panels (p.panels > 1); false compiles the single-panel form.
 template <int MC, int CW, bool LO = false, bool PN = false>
 __global__ void __launch_bounds__((CW + 1) * kWarp, 1)
-    stripe_mma_kernel(GemvArgs a, StripePlan p, const __grid_constant__ StripeMaps maps) {
+    stripe_mma_kernel(GemvArgs a, StripePlan p, const __grid_constant__ StripeMaps maps,
+                      const __grid_constant__ PeerSet peers) {
   constexpr int kGPW = 16 / CW;            // granules per lane and stage
   constexpr int kConsumers = CW * kWarp;
   constexpr int kTS = MC <= 2 ? 2 : MC;     // columns of the x tables
@@ -614,12 +616,83 @@ __global__ void __launch_bounds__((CW + 1) * kWarp, 1)
     }
     return;
   }
-  for (int o = tid; o < rows * a.m; o += kConsumers) {
-    const int m = o / rows;
-    const int r = o - m * rows;
+  auto row_sum = [&](int r, int m) {
     float sum = 0.0f;
 #pragma unroll
     for (int w = 0; w < CW; ++w) sum += red[(w * p.rows_cap + r) * MC + m];
+    return sum;
+  };
+  if (a.epilogue == kGatherPeers) {
+    // Rows split over ranks: this rank's columns of y, each as a tagged word (fp16 bits, call
+    // number), into every other rank's gather buffer and straight into this rank's y; then the
+    // same rows of every other rank's shard, each once its tag shows this call.
+    const unsigned epoch = exchange_epoch(peers);
+    named_barrier(kSxBarrier, kConsumers);  // every thread has read the call number
+    for (int o = tid; o < rows * a.m; o += kConsumers) {
+      const int m = o / rows;
+      const int r = o - m * rows;
+      const unsigned h = __half_as_ushort(__float2half_rn(row_sum(r, m)));
+      const int64_t at = static_cast<int64_t>(m) * peers.n_total + peers.col0 + row_begin + r;
+      for (int q = 0; q < peers.world; ++q) {
+        if (q == peers.rank) {
+          if (ring.ok) a.y[at] = __ushort_as_half(static_cast<unsigned short>(h));
+        } else {
+          st_tagged(exchange_words(peers, q, epoch) + at, h, epoch);
+        }
+      }
+    }
+    const unsigned long long* buf = exchange_words(peers, peers.rank, epoch);
+    bool live = true;
+    for (int o = tid; o < peers.world * rows * a.m; o += kConsumers) {
+      const int q = o / (rows * a.m);
+      if (q == peers.rank) continue;
+      const int rem = o - q * rows * a.m;
+      const int m = rem / rows;
+      const int r = rem - m * rows;
+      const int64_t at = static_cast<int64_t>(m) * peers.n_total + q * a.n + row_begin + r;
+      const unsigned h = exchange_read(buf + at, epoch, &live, p.status);
+      if (ring.ok) a.y[at] = __ushort_as_half(static_cast<unsigned short>(h));
+    }
+    exchange_done(peers, epoch, tid);
+    return;
+  }
+  if (a.epilogue == kReducePeers) {
+    // K split over ranks: this rank's fp32 partial sums, as tagged words, into slot `rank` of
+    // every other rank's buffer; then the ranks' partials of this CTA's rows added in rank order
+    // (this rank's own from shared memory), the same on every rank.
+    const unsigned epoch = exchange_epoch(peers);
+    named_barrier(kSxBarrier, kConsumers);  // every thread has read the call number
+    const int64_t slot = static_cast<int64_t>(a.m) * a.n;
+    for (int o = tid; o < rows * a.m; o += kConsumers) {
+      const int m = o / rows;
+      const int r = o - m * rows;
+      const unsigned bits = __float_as_uint(row_sum(r, m));
+      const int64_t at = peers.rank * slot + static_cast<int64_t>(m) * a.n + row_begin + r;
+      for (int q = 0; q < peers.world; ++q) {
+        if (q != peers.rank) st_tagged(exchange_words(peers, q, epoch) + at, bits, epoch);
+      }
+    }
+    const unsigned long long* mine = exchange_words(peers, peers.rank, epoch);
+    bool live = true;
+    for (int o = tid; o < rows * a.m; o += kConsumers) {
+      const int m = o / rows;
+      const int r = o - m * rows;
+      const int64_t at = static_cast<int64_t>(m) * a.n + row_begin + r;
+      float total = 0.0f;
+      for (int q = 0; q < peers.world; ++q) {
+        total += q == peers.rank
+                     ? row_sum(r, m)
+                     : __uint_as_float(exchange_read(mine + q * slot + at, epoch, &live, p.status));
+      }
+      if (ring.ok) a.y[at] = store_value(a, m, row_begin + r, total);
+    }
+    exchange_done(peers, epoch, tid);
+    return;
+  }
+  for (int o = tid; o < rows * a.m; o += kConsumers) {
+    const int m = o / rows;
+    const int r = o - m * rows;
+    const float sum = row_sum(r, m);
     if (ring.ok) {
       a.y[static_cast<int64_t>(m) * a.n + row_begin + r] = store_value(a, m, row_begin + r, sum);
     }
@@ -636,7 +709,8 @@ bool stripe_plan(const GemvArgs& a, StripePlan* p, const char** why) {
   if (a.m < 1 || a.m > 8) return fail("M must be in [1, 8]");
   if (a.group != kItemK) return fail("group_size must be 128");
   if (a.k % kSxK != 0) return fail("K must be a multiple of 2048");
-  if (a.epilogue != kStoreY) return fail("plain stores only");
+  if (a.epilogue != kStoreY && a.epilogue != kGatherPeers && a.epilogue != kReducePeers)
+    return fail("plain stores or the fused exchange only");
   if (reinterpret_cast<uintptr_t>(a.q) % 16 || reinterpret_cast<uintptr_t>(a.s) % 16 ||
       reinterpret_cast<uintptr_t>(a.z) % 16 || reinterpret_cast<uintptr_t>(a.x) % 16) {
     return fail("x, qweight, scales and zeros must be 16-byte aligned");
@@ -783,7 +857,12 @@ bool stripe_mma_supported(const GemvArgs& a, const char** why) {
   return stripe_plan(a, &p, why);
 }
 
-cudaError_t launch_stripe_mma(const GemvArgs& a, cudaStream_t stream, bool strict) {
+cudaError_t launch_stripe_mma(const GemvArgs& a, cudaStream_t stream, bool strict,
+                              const PeerSet* peers) {
+  const bool exchange = a.epilogue == kGatherPeers || a.epilogue == kReducePeers;
+  if (exchange != (peers != nullptr)) return cudaErrorInvalidValue;
+  PeerSet ps{};
+  if (peers) ps = *peers;
   StripePlan p;
   if (!stripe_plan(a, &p, nullptr)) return cudaErrorInvalidValue;
   p.strict = strict ? 1 : 0;
@@ -812,7 +891,7 @@ cudaError_t launch_stripe_mma(const GemvArgs& a, cudaStream_t stream, bool stric
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, stripe_mma_kernel<MC, CW, false, PN>, a, p, maps);
+    return cudaLaunchKernelEx(&cfg, stripe_mma_kernel<MC, CW, false, PN>, a, p, maps, ps);
   });
 }
 
@@ -850,7 +929,7 @@ cudaError_t launch_stripe_load_only(uint32_t* out, const GemvArgs& args, cudaStr
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, stripe_mma_kernel<1, STRIPE_CW, true>, a, p, maps);
+  return cudaLaunchKernelEx(&cfg, stripe_mma_kernel<1, STRIPE_CW, true>, a, p, maps, PeerSet{});
 }
 
 cudaError_t stripe_mma_attrs(int m, KernelAttrs* out) {

@@ -62,8 +62,9 @@ def test_static_rejects_oversize():
 
 def test_static_alternating_shapes_share_one_buffer():
     """Calls of different shapes and modes in a row on the one static buffer, with a rejected
-    oversize call in between: each result is bit-identical to the same kernel (stream_mma) run
-    through the named-kernel entry point, and the device status stays clean."""
+    oversize call in between: each result is bit-identical to the same kernel (stripe_mma, which
+    the exchange runs on for M <= 8 and K % 2048 == 0) run through the named-kernel entry point,
+    and the device status stays clean."""
     k = 4096
     _, q, s, z = oracle.synthetic(1, 8192, k, 128, seed=23)
     tq, ts, tz = (torch.from_numpy(a).cuda() for a in (q, s, z))
@@ -83,7 +84,7 @@ def test_static_alternating_shapes_share_one_buffer():
         y_plain = torch.empty(m, n, dtype=torch.float16, device="cuda")
         capi.call("int4gemv_w4a16_exchange_static", y_static.data_ptr(), tx.data_ptr(),
                   tq.data_ptr(), ts.data_ptr(), tz.data_ptr(), m, n, k, 128, mode, stream)
-        capi.call("int4gemv_w4a16_kernel", b"stream_mma", y_plain.data_ptr(), tx.data_ptr(),
+        capi.call("int4gemv_w4a16_kernel", b"stripe_mma", y_plain.data_ptr(), tx.data_ptr(),
                   tq.data_ptr(), ts.data_ptr(), tz.data_ptr(), m, n, k, 128, stream)
         torch.cuda.synchronize()
         assert torch.equal(y_static.view(torch.int16), y_plain.view(torch.int16)), (mode, m, n)
