@@ -822,6 +822,9 @@ def run_profile_case(args):
     elif args.profile == "reference_vectorized":
         ref = reference_module()
         fns = [lambda i=i: ref.vectorized(x, *sets[i], GROUP) for i in range(n_sets)]
+    elif args.profile.startswith("kernel:"):  # one named kernel, e.g. kernel:tc_wide
+        name = args.profile.split(":", 1)[1]
+        fns = [lambda i=i: ops.w4a16_with(x, *sets[i], GROUP, name) for i in range(n_sets)]
     else:
         fn = getattr(ops, args.profile)
         fns = [lambda i=i: fn(x, *sets[i], GROUP) for i in range(n_sets)]
@@ -836,7 +839,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--profile", default=None,
                     help="run --calls launches of one kernel (w4a16, vectorized, naive, coalesced, "
-                         "load_only, quantize, cublas, reference_vectorized) for ncu, then exit")
+                         "load_only, quantize, cublas, reference_vectorized, or kernel:NAME for "
+                         "a named kernel) for ncu, then exit")
     ap.add_argument("--m", type=int, default=M)
     ap.add_argument("--n", type=int, default=N)
     ap.add_argument("--k", type=int, default=K)

@@ -126,8 +126,11 @@ int int4gemv_stripe_load_only(void* out, const void* qweight, const void* scales
                               void* stream);
 
 /* Runs one named kernel instead of the automatic choice: "stripe_mma", "tc_dequant",
- * "stream_mma", "tcgen05", "mma_pipeline", "vectorized" (128 threads, 2 rows per warp),
- * "coalesced" or "naive". For tests and benchmarks.
+ * "stream_mma", "tcgen05", "tc_wide", "mma_pipeline", "vectorized" (128 threads, 2 rows per warp),
+ * "coalesced" or "naive". For tests and benchmarks. "tcgen05" and "tc_wide" are tcgen05 designs
+ * that the automatic choice does not use (slower than the kernels it picks, at every shape
+ * measured); "tc_wide" (1 <= M <= 64, K % 1024 == 0) keeps its own static split-K scratch and
+ * orders its calls across streams like tc_dequant.
  * Fails with
  * INT4GEMV_ERR_INVALID if that kernel does not support the shape or the pointers' alignment. */
 int int4gemv_w4a16_kernel(const char* kernel, void* y, const void* x, const void* qweight,

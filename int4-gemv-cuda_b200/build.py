@@ -35,7 +35,7 @@ NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++20", "-Xcompiler", "-fPIC",
                      f"-I{INCLUDE}", f"-I{CSRC}"]
 CU_SOURCES = [
     "capi.cu", "simt.cu", "mma_pipeline.cu", "tc_gemv.cu", "stream_mma.cu", "stripe_mma.cu",
-    "tc_dequant.cu",
+    "tc_dequant.cu", "tc_wide.cu",
     "weight_stream.cu",
     "packed.cu", "quantize.cu", "repack.cu",
 ]

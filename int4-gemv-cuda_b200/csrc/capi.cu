@@ -528,6 +528,10 @@ int int4gemv_w4a16_kernel(const char* kernel, void* y, const void* x, const void
     if (!i4::tc_dequant_supported(a, &why)) return fail(INT4GEMV_ERR_INVALID, "tc_dequant: %s", why);
     return launched(name, i4::launch_tc_dequant(a, st, strict_weights()));
   }
+  if (std::strcmp(kernel, "tc_wide") == 0) {
+    if (!i4::tc_wide_supported(a, &why)) return fail(INT4GEMV_ERR_INVALID, "tc_wide: %s", why);
+    return launched(name, i4::launch_tc_wide(a, st, strict_weights()));
+  }
   if (std::strcmp(kernel, "tcgen05") == 0) {
     if (!i4::tc_gemv_supported(a, &why)) return fail(INT4GEMV_ERR_INVALID, "tcgen05: %s", why);
     return launched(name, i4::launch_tc_gemv(a, st, strict_weights()));

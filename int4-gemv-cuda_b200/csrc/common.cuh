@@ -183,6 +183,30 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   return true;
 }
 
+// mbar_wait_bounded with a suspend-time hint: a thread whose phase has not completed is suspended
+// in hardware (up to kSuspendHintNs per try, woken when the phase completes) instead of spinning,
+// so waiting warps do not take issue slots from the warps doing the work. Same bound, same result.
+constexpr uint32_t kSuspendHintNs = 100000;
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return done != 0;
+}
+__device__ __forceinline__ bool mbar_wait_bounded_suspend(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait_suspend(bar, parity)) return true;
+  const long long start = clock64();
+  while (!mbar_try_wait_suspend(bar, parity)) {
+    if (clock64() - start > kWaitLimitCycles) return false;
+  }
+  return true;
+}
+
 // Releasing a ring stage right after loading it. mbarrier.arrive does not wait for the warp's
 // shared-memory loads that are still in flight (measured on B200: with the weights in L2, a refill
 // landed before such loads had read the stage). So before the release every lane folds the

@@ -143,6 +143,13 @@ bool tc_dequant_supported(const GemvArgs& a, const char** why);
 cudaError_t launch_tc_dequant(const GemvArgs& a, cudaStream_t stream, bool strict);
 cudaError_t tc_dequant_attrs(int m, KernelAttrs* out);
 
+// tcgen05 GEMV for M <= 64 with the weights as the MMA's N operand (tc_wide.cu): 256-row tiles,
+// x and the dequantised weights both in shared memory, stream-K like tc_dequant with its own
+// static partial sums and counters.
+bool tc_wide_supported(const GemvArgs& a, const char** why);
+cudaError_t launch_tc_wide(const GemvArgs& a, cudaStream_t stream, bool strict);
+cudaError_t tc_wide_attrs(int m, KernelAttrs* out);
+
 // TMA-bulk-fed mma.sync pipeline (mma_pipeline.cu). `why` gets a reason when unsupported.
 bool mma_pipeline_supported(const GemvArgs& a, const char** why);
 cudaError_t launch_mma_pipeline(const GemvArgs& a, cudaStream_t stream);

@@ -289,6 +289,47 @@ def test_tc_dequant_two_streams():
         assert_close(outs[i], oracle.reference(x, q, s, z, 128), f"call {i}")
 
 
+# tc_wide: 256-row tiles and 64-weight stages, so other tile / range boundaries than
+# tc_dequant's: N one row past a tile, N below one tile, K long enough for several s/z windows per
+# CTA (16 stages each), contributors per tile from one to hundreds, every M up to 64 (rows of x
+# past M in the last 8-row group).
+TW = [(1, 1, 1024), (9, 37, 1024), (16, 100, 28672), (33, 1000, 4096), (48, 300, 3072),
+      (63, 3000, 5120), (16, 8192, 8192), (64, 8192, 8192), (16, 257, 1024),
+      (9, 148 * 256 + 1, 1024), (5, 512, 28672), (64, 255, 4096), (1, 256, 1024)]
+
+
+@pytest.mark.parametrize("m,n,k", TW, ids=[f"m{m}_n{n}_k{k}" for m, n, k in TW])
+def test_tc_wide_shapes(m, n, k):
+    x, q, s, z = oracle.synthetic(m, n, k, 128, seed=29 * m + n + k)
+    args = cuda(x, q, s, z)
+    y = ops.w4a16_with(*args, 128, "tc_wide")
+    torch.cuda.synchronize()
+    assert_close(y, oracle.reference(x, q, s, z, 128), f"tc_wide {m}x{n}x{k}")
+    y2 = ops.w4a16_with(*args, 128, "tc_wide")
+    torch.cuda.synchronize()
+    assert torch.equal(y, y2), "tc_wide must be deterministic (fixed-order split-K sums)"
+    from int4gemv import capi
+
+    assert capi.device_status() == 0
+
+
+def test_tc_wide_two_streams():
+    """Like tc_dequant, tc_wide's partial sums and tile counters are static; calls on two streams
+    with no synchronisation between them are ordered by the library."""
+    m, n, k = 16, 4096, 4096
+    sets = [oracle.synthetic(m, n, k, 128, seed=400 + i) for i in range(6)]
+    dev = [cuda(*st) for st in sets]
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    torch.cuda.synchronize()
+    outs = []
+    for i, args in enumerate(dev):
+        with torch.cuda.stream(streams[i % 2]):
+            outs.append(ops.w4a16_with(*args, 128, "tc_wide"))
+    torch.cuda.synchronize()
+    for i, (x, q, s, z) in enumerate(sets):
+        assert_close(outs[i], oracle.reference(x, q, s, z, 128), f"call {i}")
+
+
 @pytest.mark.parametrize("m,n,k,g", [(1, 2048, 3584, 128), (3, 300, 768, 64), (2, 100, 96, 16),
                                      (12, 257, 1536, 128)])
 def test_w4a16_f32_any_shape(m, n, k, g):
