@@ -120,8 +120,16 @@ def test_full_size_w4a16(m, n, k):
     args = cuda(x, q, s, z)
     y = ops.w4a16(*args, 128)
     ref = oracle.reference(x, q, s, z, 128)
-    assert_close(y, ref, f"w4a16 {m}x{n}x{k} ({ops.w4a16_kernel(*args, 128)})")
-    assert ops.w4a16_kernel(*args, 128) == expected_kernel(m, k, n=n)
+    kernel = ops.w4a16_kernel(*args, 128)
+    assert_close(y, ref, f"w4a16 {m}x{n}x{k} ({kernel})")
+    assert kernel == expected_kernel(m, k, n=n)
+    # The margin: the largest error as a fraction of the allowed bound. Measured on B200 at these
+    # shapes: at most 0.05 for the warp-MMA kernels (the fp16 rounding of y) up to K = 28672, and
+    # 0.35 for tc_dequant (weights rounded to fp16); half the budget is the alarm.
+    yf = y.float().cpu().numpy().astype(np.float64)
+    bound = min(ATOL * float(np.sqrt(np.mean(ref.astype(np.float64) ** 2))), ATOL) + RTOL * np.abs(ref)
+    ratio = float((np.abs(yf - ref) / bound).max())
+    assert ratio < 0.5, f"w4a16 {m}x{n}x{k} ({kernel}): error uses {ratio:.2f} of the tolerance"
 
 
 @pytest.mark.parametrize("name,cfg", KERNELS[:3] + [("w4a16", {})])
